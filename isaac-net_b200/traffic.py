@@ -1,0 +1,351 @@
+"""Traffic models that run inside the engine step (level "L2"), and the policy's Requests.
+
+The models and their draw order are isaac_net's (isaac_net/core/traffic.py:51-430): every model draws from one
+``torch.Generator`` owned by the engine (step draws) and a second one for resets, in exactly the reference's call
+order and shapes, so an engine on the same device with the same seed sees the same arrivals as the reference.  The
+draws stay torch calls on purpose: the reference's arrival stream is defined by torch's generator (mt19937 on CPU,
+Philox on CUDA), and a re-implementation would change it.  Everything downstream of the arrivals (enqueue, the
+per-slot arrival gate, the MAC) runs in the B200 kernels.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, replace
+from typing import Callable, Optional, Union
+
+import torch
+
+KINDS = ("periodic", "bursty", "video", "event", "policy")
+
+
+@dataclass
+class Requests:
+    """Messages the policy enqueues in one control step (isaac_net/core/proto/netsim.py:163-172).
+
+    send [E,R] long (0 = nothing, c >= 1 = one message of class c), det [E,R] bool, hid [E] long."""
+    send: torch.Tensor
+    det: Optional[torch.Tensor] = None
+    hid: Optional[torch.Tensor] = None
+
+
+@dataclass(frozen=True)
+class TrafficModel:
+    """One traffic generator (isaac_net/core/traffic.py:51-176). Build it with the constructors."""
+    kind: str
+    size_bytes: float = 0.0
+    period_ms: float = 0.0
+    jitter_ms: float = 0.0
+    phase: str = "random"
+    rate_hz: float = 0.0
+    burst_size: int = 1
+    on_off: tuple = (1.0, 0.0)
+    gop: Optional[tuple] = None
+    trigger: Union[str, Callable, None] = None
+    det: bool = False
+    robots: Optional[tuple] = None
+    tag: Optional[int] = None
+    priority: int = 0
+    deadline_ms: float = math.inf
+    max_msgs_per_step: Optional[int] = None
+    direction: str = "ul"
+
+    @staticmethod
+    def periodic(size_bytes, period_ms, jitter_ms=0.0, phase="random", **kw):
+        assert period_ms > 0 and 0 <= jitter_ms < period_ms and size_bytes > 0
+        assert phase in ("random", "aligned")
+        return TrafficModel("periodic", size_bytes=float(size_bytes), period_ms=float(period_ms),
+                            jitter_ms=float(jitter_ms), phase=phase, **kw)
+
+    @staticmethod
+    def bursty(size_bytes, rate_hz, burst_size, on_off=(1.0, 1.0), **kw):
+        assert size_bytes > 0 and rate_hz > 0 and burst_size >= 1 and on_off[0] > 0 and on_off[1] >= 0
+        return TrafficModel("bursty", size_bytes=float(size_bytes), rate_hz=float(rate_hz),
+                            burst_size=int(burst_size), on_off=(float(on_off[0]), float(on_off[1])), **kw)
+
+    @staticmethod
+    def video(fps, mean_frame_bytes=None, gop=None, phase="random", jitter_ms=0.0, **kw):
+        assert fps > 0 and (mean_frame_bytes is not None or gop is not None)
+        if gop is not None:
+            i_b, p_b, n = float(gop[0]), float(gop[1]), int(gop[2])
+            if mean_frame_bytes is not None:
+                s = float(mean_frame_bytes) / ((i_b + (n - 1) * p_b) / n)
+                i_b, p_b = i_b * s, p_b * s
+            gop = (i_b, p_b, n)
+            size = (i_b + (n - 1) * p_b) / n
+        else:
+            size = float(mean_frame_bytes)
+        period = 1000.0 / fps
+        assert 0 <= jitter_ms < period and phase in ("random", "aligned")
+        return TrafficModel("video", size_bytes=size, period_ms=period, jitter_ms=float(jitter_ms), phase=phase,
+                            gop=gop, **kw)
+
+    @staticmethod
+    def event(size_bytes, trigger="event", det=False, **kw):
+        assert size_bytes > 0
+        return TrafficModel("event", size_bytes=float(size_bytes), trigger=trigger, det=bool(det), **kw)
+
+    @staticmethod
+    def policy():
+        return TrafficModel("policy")
+
+    def on(self, robots):
+        if robots is None:
+            return replace(self, robots=None)
+        if isinstance(robots, int):
+            robots = (robots,)
+        return replace(self, robots=tuple(int(r) for r in robots))
+
+    def with_(self, **kw):
+        return replace(self, **kw)
+
+    @property
+    def generates(self):
+        return self.kind != "policy"
+
+    def bursts_per_step(self, step_ms):
+        if self.max_msgs_per_step is not None:
+            return max(1, int(self.max_msgs_per_step) // self.burst_size)
+        lam = self.rate_hz * step_ms / 1000.0
+        return int(math.ceil(lam + 4 * math.sqrt(lam))) + 1
+
+    def max_per_step(self, step_ms):
+        if self.max_msgs_per_step is not None:
+            return int(self.max_msgs_per_step)
+        if self.kind in ("periodic", "video"):
+            return int(math.floor((step_ms + self.jitter_ms) / self.period_ms)) + 1
+        if self.kind == "bursty":
+            return self.burst_size * self.bursts_per_step(step_ms)
+        return 1 if self.kind == "event" else 0
+
+
+def normalize_traffic(traffic):
+    if traffic is None:
+        return None
+    if isinstance(traffic, TrafficModel):
+        traffic = (traffic,)
+    traffic = tuple(traffic)
+    for m in traffic:
+        if not isinstance(m, TrafficModel) or m.kind not in KINDS:
+            raise TypeError(f"NRConfig.traffic takes TrafficModel objects, got {m!r}")
+        if m.direction != "ul":
+            raise ValueError("downlink traffic models need the downlink MAC, which the B200 engine does not build")
+    return traffic or None
+
+
+def generates(traffic):
+    return traffic is not None and any(m.generates for m in traffic)
+
+
+@dataclass
+class Arrivals:
+    """Messages of one control step [E,R,M], sorted by arrival slot per robot (invalid entries last)."""
+    valid: torch.Tensor
+    nbytes: torch.Tensor
+    slot: torch.Tensor
+    tag: torch.Tensor
+    prio: torch.Tensor
+    dline: torch.Tensor
+    det: torch.Tensor
+
+
+class _Source:
+    """Per-robot state of one model [E,R]; draws from the engine's step / reset generators."""
+
+    def __init__(self, model, idx, E, R, dev, step_ms, gens):
+        self.m, self.E, self.R, self.dev, self.step_ms = model, E, R, dev, step_ms
+        self.gens = gens                      # [step generator, reset generator]; gens[2] selects the active one
+        self.width = model.max_per_step(step_ms)
+        self.tag = model.tag if model.tag is not None else idx + 1
+        on = torch.zeros(R, dtype=torch.bool, device=dev)
+        if model.robots is None:
+            on[:] = True
+        else:
+            bad = [r for r in model.robots if not 0 <= r < R]
+            if bad:
+                raise ValueError(f"traffic model {model.kind}: robots {bad} outside 0..{R - 1}")
+            on[list(model.robots)] = True
+        self.mask = on[None, :].expand(E, R)
+        full = lambda dt, v: torch.full((E, R), v, dtype=dt, device=dev)
+        if model.kind in ("periodic", "video"):
+            self.nom, self.nxt, self.cnt = full(torch.float64, 0.0), full(torch.float64, 0.0), full(torch.long, 0)
+            self.names = ("nom", "nxt", "cnt")
+        elif model.kind == "bursty":
+            self.on, self.t_tog, self.t_bur = (full(torch.bool, False), full(torch.float64, 0.0),
+                                               full(torch.float64, 0.0))
+            self.names = ("on", "t_tog", "t_bur")
+        else:
+            self.names = ()
+        self.deferred = torch.zeros((), dtype=torch.long, device=dev)
+        self._gen = gens[0]
+
+    def _u(self):
+        return torch.rand(self.E, self.R, generator=self._gen, device=self.dev, dtype=torch.float64)
+
+    def _expo(self, mean_ms):
+        return -torch.log1p(-self._u()) * mean_ms
+
+    def _write_back(self, bufs):
+        for n, b in bufs.items():          # in place: captured graphs and callers keep the same buffers
+            b.copy_(getattr(self, n))
+            setattr(self, n, b)
+
+    def reset(self, me):
+        bufs = {n: getattr(self, n) for n in self.names}
+        self._gen = self.gens[1]
+        try:
+            m, md = me[:, None], self.m
+            if md.kind in ("periodic", "video"):
+                nom = self._u() * md.period_ms if md.phase == "random" else torch.zeros_like(self.nom)
+                nxt = nom + self._u() * md.jitter_ms
+                self.nom = torch.where(m, nom, self.nom)
+                self.nxt = torch.where(m, nxt, self.nxt)
+                self.cnt = torch.where(m, torch.zeros_like(self.cnt), self.cnt)
+            elif md.kind == "bursty":
+                on_ms, off_ms = md.on_off[0] * 1000.0, md.on_off[1] * 1000.0
+                on = self._u() < on_ms / (on_ms + off_ms)
+                a = self._expo(on_ms)
+                b = self._expo(off_ms)
+                t_tog = torch.where(on, a, b)
+                t_bur = self._expo(1000.0 / md.rate_hz)
+                if off_ms == 0:
+                    t_tog = torch.full_like(t_tog, math.inf)
+                self.on = torch.where(m, on, self.on)
+                self.t_tog = torch.where(m, t_tog, self.t_tog)
+                self.t_bur = torch.where(m, t_bur, self.t_bur)
+        finally:
+            self._gen = self.gens[0]
+        self._write_back(bufs)
+
+    def step(self, clock, trig):
+        bufs = {n: getattr(self, n) for n in self.names}
+        out = self._draw(clock, trig)
+        self._write_back(bufs)
+        return out
+
+    def _draw(self, clock, trig):
+        md, E, R, W, T = self.m, self.E, self.R, self.width, self.step_ms
+        if md.kind in ("periodic", "video"):
+            vs, bs, ts = [], [], []
+            for _ in range(W):
+                hit = (self.nxt < T) & self.mask
+                if md.kind == "video" and md.gop is not None:
+                    i_b, p_b, n = md.gop
+                    size = torch.where(self.cnt % n == 0, torch.full_like(self.nxt, i_b), torch.full_like(self.nxt, p_b))
+                else:
+                    size = torch.full_like(self.nxt, md.size_bytes)
+                vs.append(hit), bs.append(size), ts.append(self.nxt)
+                self.cnt = self.cnt + hit.long()
+                self.nom = torch.where(hit, self.nom + md.period_ms, self.nom)
+                self.nxt = torch.where(hit, self.nom + self._u() * md.jitter_ms, self.nxt)
+            self.deferred += ((self.nxt < T) & self.mask).sum()
+            self.nom = self.nom - T
+            self.nxt = self.nxt - T
+            return torch.stack(vs, -1), torch.stack(bs, -1), torch.stack(ts, -1)
+        if md.kind == "bursty":
+            nb = W // md.burst_size
+            on_ms, off_ms = md.on_off[0] * 1000.0, md.on_off[1] * 1000.0
+            iat = 1000.0 / md.rate_hz
+            loops = nb + 2 * (int(math.ceil(T / max(min(on_ms, off_ms if off_ms > 0 else on_ms), 1e-9))) + 1)
+            loops = min(loops, nb + 64)
+            cnt = torch.zeros(E, R, dtype=torch.long, device=self.dev)
+            times = torch.full((E, R, nb), math.inf, dtype=torch.float64, device=self.dev)
+            slots = torch.arange(nb, device=self.dev)
+            for _ in range(loops):
+                t_b = torch.where(self.on, self.t_bur, torch.full_like(self.t_bur, math.inf))
+                due = self.mask & self.on & (t_b <= self.t_tog) & (t_b < T)
+                burst = due & (cnt < nb)
+                blocked = due & (cnt >= nb)
+                tog = self.mask & ~burst & ~blocked & (self.t_tog < T) & (self.t_tog < t_b)
+                times = torch.where((cnt[..., None] == slots) & burst[..., None], t_b[..., None], times)
+                cnt = cnt + burst.long()
+                self.t_bur = torch.where(burst, self.t_bur + self._expo(iat), self.t_bur)
+                now_on = ~self.on
+                d_on = self._expo(on_ms)
+                d_off = self._expo(off_ms) if off_ms > 0 else torch.full_like(self.t_tog, math.inf)
+                new_tog = self.t_tog + torch.where(now_on, d_on, d_off)
+                self.t_bur = torch.where(tog & now_on, self.t_tog + self._expo(iat), self.t_bur)
+                self.t_tog = torch.where(tog, new_tog, self.t_tog)
+                self.on = torch.where(tog, now_on, self.on)
+            t_b = torch.where(self.on, self.t_bur, torch.full_like(self.t_bur, math.inf))
+            self.deferred += (self.mask & (torch.minimum(t_b, self.t_tog) < T)).sum()
+            self.t_bur = self.t_bur - T
+            self.t_tog = self.t_tog - T
+            valid = torch.isfinite(times).repeat_interleave(md.burst_size, -1)
+            t = times.repeat_interleave(md.burst_size, -1)
+            return valid, torch.full(valid.shape, md.size_bytes, dtype=torch.float32, device=self.dev), t
+        if md.kind == "event":
+            if callable(md.trigger):
+                mask = md.trigger(clock)
+            elif torch.is_tensor(trig):
+                mask = trig
+            elif isinstance(trig, dict) and md.trigger in trig:
+                mask = trig[md.trigger]
+            else:
+                mask = None
+            if mask is None:
+                valid = torch.zeros(E, R, dtype=torch.bool, device=self.dev)
+            else:
+                mask = mask.to(self.dev, torch.bool)
+                valid = (mask[:, None].expand(E, R) if mask.dim() == 1 else mask) & self.mask
+            z = torch.zeros(E, R, 1, dtype=torch.float64, device=self.dev)
+            return valid[..., None], torch.full((E, R, 1), md.size_bytes, dtype=torch.float32, device=self.dev), z
+        raise AssertionError(md.kind)
+
+
+class TrafficGen:
+    """All generating uplink models of a config for E envs x R robots; step() -> Arrivals [E,R,M]."""
+
+    def __init__(self, traffic, E, R, device, step_ms, slots_per_step, seed=None):
+        self.E, self.R, self.dev = E, R, torch.device(device)
+        self.N = int(slots_per_step)
+        self.step_ms, self.slot_ms = float(step_ms), float(step_ms) / self.N
+        seed = 0 if seed is None else int(seed)
+        self.gen = torch.Generator(device=self.dev)
+        self.gen.manual_seed(seed)
+        self.rgen = torch.Generator(device=self.dev)
+        self.rgen.manual_seed((seed + 0x9E3779B97F4A7C15) % 2 ** 63)
+        models = normalize_traffic(traffic) or ()
+        gens = (self.gen, self.rgen)
+        self.sources = [_Source(m, i, E, R, self.dev, self.step_ms, gens)
+                        for i, m in enumerate(models) if m.generates]
+        self.M = sum(s.width for s in self.sources)
+        self.reset(None)
+
+    @property
+    def deferred(self):
+        return sum((s.deferred for s in self.sources), torch.zeros((), dtype=torch.long, device=self.dev))
+
+    def reset(self, env_mask_e=None):
+        m = torch.ones(self.E, dtype=torch.bool, device=self.dev) if env_mask_e is None else env_mask_e
+        for s in self.sources:
+            s.reset(m)
+        if env_mask_e is None:
+            for s in self.sources:
+                s.deferred.zero_()
+
+    def step(self, clock=None, triggers=None) -> Arrivals:
+        E, R, d = self.E, self.R, self.dev
+        cols = {k: [] for k in ("v", "b", "t", "tag", "prio", "dl", "det")}
+        for s in self.sources:
+            v, b, t = s.step(clock, triggers)
+            k = v.shape[-1]
+            cols["v"].append(v), cols["b"].append(b.float()), cols["t"].append(t)
+            cols["tag"].append(torch.full((E, R, k), s.tag, dtype=torch.long, device=d))
+            cols["prio"].append(torch.full((E, R, k), s.m.priority, dtype=torch.long, device=d))
+            cols["dl"].append(torch.full((E, R, k), s.m.deadline_ms, dtype=torch.float64, device=d))
+            cols["det"].append(torch.full((E, R, k), s.m.det, dtype=torch.bool, device=d))
+        if not cols["v"]:
+            z = torch.zeros(E, R, 0, device=d)
+            return Arrivals(z.bool(), z.float(), z.long(), z.long(), z.long(), z.double(), z.bool())
+        valid, nbytes, t = torch.cat(cols["v"], -1), torch.cat(cols["b"], -1), torch.cat(cols["t"], -1)
+        t = torch.where(valid, t, torch.zeros_like(t))
+        slot = torch.floor(t.clamp(min=0) / self.slot_ms).long().clamp(0, self.N - 1)
+        M = valid.shape[-1]
+        key = torch.where(valid, slot, torch.full_like(slot, self.N)) * M + torch.arange(M, device=d)
+        order = key.argsort(-1)
+        g = lambda x: x.gather(-1, order)
+        return Arrivals(g(valid), g(nbytes), g(slot), g(torch.cat(cols["tag"], -1)), g(torch.cat(cols["prio"], -1)),
+                        g(torch.cat(cols["dl"], -1)), g(torch.cat(cols["det"], -1)))
+
+
+__all__ = ["Requests", "TrafficModel", "TrafficGen", "Arrivals", "normalize_traffic", "generates"]

@@ -1,0 +1,157 @@
+"""Generate the golden fixtures of the NR uplink engine from the reference implementation (isaac-net v0.2.0).
+
+Run in a container where the reference is importable (its source tree on PYTHONPATH or given with --ref):
+
+    python tests/golden/make_golden.py --ref /path/to/isaac-net
+
+For each benchmark workload (isaac-net_b200/presets.py) at a small E x R, the reference engine
+(make_engine("L2", E, R, "cpu", cfg, backend="reference")) is driven with this repository's seeded pose generator for
+a number of control steps, with two partial resets on the way.  The fixture keeps, per step: the poses, the traffic
+arrivals the reference generated (captured at TrafficGen.step), the reset schedule, every key of the step dict, and
+the engine state after the step (MAC, queue, fading, RNG counters, radio fields, engine clocks) under the reference's
+attribute names.  The fixtures are what the oracle (oracle/nr_oracle.py) and the host-side traffic generator are
+pinned against; tests read them with numpy only.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+
+# name: (workload id, E, R, steps, resets {step: env ids}, state snapshot every k steps, config overrides).
+# The "s" cases stress the retransmission paths: a weak link (HARQ failures, exhaustion and RLC resends), short
+# deadlines (purged frames) and a small frame buffer (refused messages).
+CASES = {
+    "1": (1, 6, 16, 40, {12: [1], 30: [0, 4]}, 1, {}),
+    "2": (2, 3, 32, 32, {15: [2]}, 2, {}),
+    "4": (4, 2, 128, 16, {10: [1]}, 4, {}),
+    "1s": (1, 4, 16, 40, {20: [2]}, 1, dict(ue_tx_dbm=-12.0, timeout_steps=5, frame_buffer=8, max_harq_tx=2,
+                                            rlc_retx_slots=7)),
+    "2s": (2, 3, 32, 32, {11: [0]}, 2, dict(ue_tx_dbm=-8.0, n_harq=4, timeout_steps=6, frame_buffer=6)),
+}
+
+
+def _ref_traffic(ref_tm, m):
+    kw = dict(size_bytes=m.size_bytes, period_ms=m.period_ms, jitter_ms=m.jitter_ms, phase=m.phase,
+              rate_hz=m.rate_hz, burst_size=m.burst_size, on_off=m.on_off, gop=m.gop, trigger=m.trigger, det=m.det,
+              robots=m.robots, tag=m.tag, priority=m.priority, deadline_ms=m.deadline_ms,
+              max_msgs_per_step=m.max_msgs_per_step, direction=m.direction)
+    return ref_tm(m.kind, **kw)
+
+
+def ref_config(wl, **over):
+    from isaac_net.core.config import NRConfig as RefCfg
+    from isaac_net.core.traffic import TrafficModel as RefTM
+    f = {**wl.fields, **over}
+    if f.get("traffic") is not None:
+        f["traffic"] = tuple(_ref_traffic(RefTM, m) for m in f["traffic"])
+    return RefCfg(**f)
+
+
+def ref_state(eng):
+    """Engine state under the reference's names (numpy)."""
+    net, ul = eng.net, eng.net.ul
+    q = ul.q
+    st = {}
+    for n in ("sent", "floor", "olla", "avg", "bsr", "sr_t", "last_tx", "csi", "h_state", "h_lo", "h_hi", "h_ready",
+              "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb"):
+        st["ul." + n] = getattr(ul, n)
+    for n in ("cap", "start", "end", "lost", "fin", "enq", "cls", "det", "hid"):
+        st["q." + n] = getattr(q, n)
+    for n in ("off", "tag", "prio", "dline"):
+        if hasattr(q, n):
+            st["q." + n] = getattr(q, n)
+    st["net.h"] = net.h
+    if net.rician:
+        st["net.spec"] = net.spec
+        st["net.k_lin"] = net.k_lin
+    st["net.last_g"] = torch.tensor(-1 if net.last_g is None else net.last_g)
+    st["rng.episode"] = net.rng.episode
+    st["rng.ctr_step"] = net.rng.ctr[2]
+    st["eng.T"] = torch.tensor(eng.T)
+    st["eng.epoch"] = eng.epoch
+    st["eng.last_snr"] = eng._last_snr
+    st["eng.last_hid"] = eng._last_hid
+    rad = eng.radio
+    if rad is not None:
+        if rad.k is not None:
+            st["radio.k"], st["radio.phi"] = rad.k, rad.phi
+        ch = rad.ch
+        if ch is not None and hasattr(ch, "sf_los"):
+            for nm in ("sf_los", "sf_nlos", "los_field"):
+                fld = getattr(ch, nm)
+                st[f"radio.{nm}.k"], st[f"radio.{nm}.phi"] = fld.k, fld.phi
+    for k, v in ul.ctr.items():
+        st["ctr." + k] = v
+    st["ctr.ntx_hist"], st["ctr.rv_tx"], st["ctr.rv_fail"] = ul.ntx_hist, ul.rv_tx, ul.rv_fail
+    st["ctr.prb_used_env"] = ul.prb_used_env
+    return {k: v.detach().cpu().clone().numpy() for k, v in st.items()}
+
+
+def run_case(i, E, R, steps, resets, every, over):
+    from isaac_net import make_engine as ref_make
+    b200 = importlib.import_module("isaac-net_b200")
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(i)
+    cfg = ref_config(wl, **over)
+    eng = ref_make("L2", E, R, "cpu", cfg, strict=None, seed=wl.seed)
+    cap = []
+    tstep = eng.traffic.step
+
+    def grab(clock=None, triggers=None):
+        a = tstep(clock, triggers)
+        cap.append(a)
+        return a
+    eng.traffic.step = grab
+    mot = presets.Motion(i, E, R, seed=wl.seed, step_ms=cfg.control_step_ms)
+    rec = {"E": np.int64(E), "R": np.int64(R), "steps": np.int64(steps), "workload": np.int64(i)}
+    st0 = ref_state(eng)
+    for k, v in st0.items():
+        rec["init/" + k] = v
+    pos = mot.current()
+    reset_rows = np.full((steps, E), False)
+    for s in range(steps):
+        if s in resets:
+            ids = resets[s]
+            reset_rows[s, ids] = True
+            eng.reset(torch.tensor(ids))
+        out = eng.step(None, pos)
+        a = cap[-1]
+        rec[f"s{s}/pos"] = pos.numpy()
+        for n in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det"):
+            rec[f"s{s}/arr.{n}"] = getattr(a, n).numpy()
+        for k, v in out.items():
+            rec[f"s{s}/out.{k}"] = v.detach().cpu().clone().numpy()
+        if s % every == 0 or s == steps - 1 or (s + 1) in resets:
+            for k, v in ref_state(eng).items():
+                rec[f"s{s}/st.{k}"] = v
+        pos = mot.advance()
+    rec["resets"] = reset_rows
+    return rec
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF", "/root/reference"))
+    ap.add_argument("--cases", default=",".join(str(k) for k in CASES))
+    a = ap.parse_args()
+    sys.path.insert(0, a.ref)
+    sys.path.insert(0, ROOT)
+    torch.set_num_threads(8)
+    for c in a.cases.split(","):
+        rec = run_case(*CASES[c])
+        rec["overrides"] = np.array(repr(CASES[c][-1]))
+        path = os.path.join(HERE, f"cfg{c}.npz")
+        np.savez_compressed(path, **rec)
+        print(path, os.path.getsize(path))
+
+
+if __name__ == "__main__":
+    main()

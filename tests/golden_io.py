@@ -1,0 +1,45 @@
+"""Reading the golden fixtures (tests/golden/*.npz, written by tests/golden/make_golden.py)."""
+import ast
+import importlib
+import os
+
+import numpy as np
+
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+CASES = ("1", "2", "4", "1s", "2s")
+
+
+class Golden:
+    def __init__(self, case):
+        self.case = case
+        self.d = np.load(os.path.join(GOLDEN, f"cfg{case}.npz"))
+        self.E, self.R, self.steps = int(self.d["E"]), int(self.d["R"]), int(self.d["steps"])
+        self.workload_id = int(self.d["workload"])
+        self.overrides = ast.literal_eval(str(self.d["overrides"]))
+        self.resets = self.d["resets"]
+
+    def workload(self):
+        return importlib.import_module("isaac-net_b200.presets").workload(self.workload_id)
+
+    def config(self):
+        return self.workload().config(**self.overrides)
+
+    def pos(self, s):
+        return self.d[f"s{s}/pos"]
+
+    def arrivals(self, s):
+        return {n: self.d[f"s{s}/arr.{n}"] for n in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det")}
+
+    def outputs(self, s):
+        pre = f"s{s}/out."
+        return {k[len(pre):]: self.d[k] for k in self.d.files if k.startswith(pre)}
+
+    def has_state(self, s):
+        return f"s{s}/st.eng.T" in self.d.files
+
+    def state(self, s):
+        pre = "init/" if s < 0 else f"s{s}/st."
+        return {k[len(pre):]: self.d[k] for k in self.d.files if k.startswith(pre)}
+
+    def reset_ids(self, s):
+        return np.nonzero(self.resets[s])[0].tolist()

@@ -1,0 +1,105 @@
+"""Pin the oracle (oracle/nr_oracle.py) against the reference's own outputs (tests/golden/, CPU).
+
+In "aten" mode the oracle runs the same torch reductions as the reference, so on CPU every step output and every
+state tensor must be bitwise equal to the fixture, free-running over every recorded step (partial resets included).
+"seq" mode (the kernel's numerics contract) changes only the association order of RBG sums, so it is checked
+teacher-forced: loaded with the reference state before each recorded step, it must reproduce the integer outputs and
+state of nearly every robot-step; the residual is measured and bounded.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from golden_io import CASES, Golden
+from oracle.nr_oracle import OracleEngine
+
+INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
+           "priority", "bytes", "deadline_miss", "serving_cell", "t", "gen_accepted", "gen_bytes")
+FLOAT_OUT = ("delay", "queue_bytes", "sinr_db", "arrival")
+
+
+def _arr(g, s, dev="cpu"):
+    return {k: torch.as_tensor(v).to(dev) for k, v in g.arrivals(s).items()}
+
+
+def _eq(a, b):
+    a, b = np.asarray(a), np.asarray(b)
+    if a.dtype.kind == "f":
+        return np.array_equal(a, b, equal_nan=True)
+    return np.array_equal(a, b)
+
+
+def _state_diff(o, ref):
+    bad = []
+    mine = {k: v.cpu().numpy() for k, v in o.reference_state().items()}
+    for k, v in ref.items():
+        if k in mine and not _eq(mine[k], v):
+            bad.append(k)
+    return bad
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_aten_bitwise_free_running(case):
+    g = Golden(case)
+    wl = g.workload()
+    o = OracleEngine(g.config(), g.E, g.R, "cpu", seed=wl.seed, reduce="aten")
+    assert not _state_diff(o, g.state(-1)), "initial state"
+    for s in range(g.steps):
+        ids = g.reset_ids(s)
+        if ids:
+            o.reset(ids)
+        out = o.step(torch.as_tensor(g.pos(s)), _arr(g, s))
+        ref = g.outputs(s)
+        assert set(ref) == set(out), (set(ref) ^ set(out))
+        for k, v in ref.items():
+            assert _eq(out[k].cpu().numpy(), v), f"step {s} output {k}"
+        if g.has_state(s):
+            bad = _state_diff(o, g.state(s))
+            assert not bad, f"step {s} state {bad}"
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_oracle_seq_teacher_forced(case):
+    g = Golden(case)
+    wl = g.workload()
+    o = OracleEngine(g.config(), g.E, g.R, "cpu", seed=wl.seed, reduce="seq")
+    robot_steps = flips = 0
+    n = 0
+    for s in range(1, g.steps):
+        if not g.has_state(s - 1) or g.reset_ids(s):
+            continue
+        o.load_reference_state(g.state(s - 1))
+        o.radio = None
+        # the pose input goes through the radio, whose fields are drawn from (seed, env, episode) at first use
+        out = o.step(torch.as_tensor(g.pos(s)), _arr(g, s))
+        ref = g.outputs(s)
+        rows = np.ones((g.E, g.R), dtype=bool)
+        for k in INT_OUT:
+            if k in ref:
+                eq = np.asarray(out[k].cpu().numpy() == ref[k])
+                rows &= eq.reshape(g.E, -1).all(-1)[:, None] if eq.ndim == 1 else eq.reshape(g.E, g.R, -1).all(-1)
+        flips += int((~rows).sum())
+        robot_steps += g.E * g.R
+        for k in FLOAT_OUT:
+            if k in ref:
+                a, b = out[k].cpu().double().numpy(), ref[k].astype(np.float64)
+                both = np.isfinite(a) & np.isfinite(b)
+                assert np.array_equal(np.isnan(a), np.isnan(b)) or flips > 0, f"step {s} {k} nan pattern"
+                assert np.allclose(a[both], b[both], rtol=1e-5, atol=1e-4), f"step {s} {k}"
+        n += 1
+    assert n > 0
+    assert flips <= max(1, robot_steps // 1000), (flips, robot_steps)
+
+
+def test_oracle_golden_cases_have_activity():
+    """The stress fixtures do exercise retransmissions, HARQ exhaustion, timeouts and refused messages."""
+    g = Golden("1s")
+    last = g.state(g.steps - 1)
+    assert last["ctr.tb_retx"] > 100 and last["ctr.exhaust"] > 5
+    timed = sum(int(g.outputs(s)["timed_out"].sum()) for s in range(g.steps))
+    assert timed > 100
+    gen = sum(int(g.arrivals(s)["valid"].sum()) for s in range(g.steps))
+    acc = sum(int(g.outputs(s)["gen_accepted"].sum()) for s in range(g.steps))
+    assert acc < gen
