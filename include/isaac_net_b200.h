@@ -1,0 +1,167 @@
+/*
+ * isaac_net_b200 C ABI: the B200 (sm_100a) NR uplink control-step engine of isaac-net, level "L2".
+ *
+ * Plain C types only (device pointers, sizes, a CUDA stream as void*): any host language can bind it (ctypes, cgo,
+ * JNI, N-API).  Every buffer is owned by the caller, allocated once, updated in place; the entry points never
+ * allocate device memory and never synchronize with the host, so a step can be captured in a CUDA graph.
+ *
+ * Reference interfaces replaced (isaac-net v0.2.0):
+ *   inb_nr_step        the slot loop and finish of one control step: NRNet.step / step_rx (isaac_net/core/nr_engine.py
+ *                      :613-668) + NRNet._finish (nr_engine.py:843-888), MacLink.slot (isaac_net/core/mac.py:228-508),
+ *                      UlMac hooks (isaac_net/core/mac_ul.py:66-236), the traffic enqueue and arrival gate of
+ *                      NREngine._inject / _open_gate (isaac_net/core/engine.py:505-573) and the step-dict outputs of
+ *                      NREngine.step (engine.py:538-631).  It is the seam the Triton backend's launch_step occupies
+ *                      (isaac_net/core/nr_triton.py:1104-1167, nr_fast.py:702-752).
+ *   inb_nr_reset       the device side of NRNet.reset(env_ids) (nr_engine.py:250-320) and MacLink / FrameQueue reset
+ *                      (mac.py:176-189, queues.py:399-407): new episode, counter-RNG reset draws (initial fading,
+ *                      Rician phase) and the per-robot state back to its initial values, for a mask of envs.
+ *   inb_rng_draw       CounterRNG reset draws (isaac_net/core/proto/rng.py:116-161, rng_triton.launch_draw): uniforms
+ *                      or Box-Muller normals [E, n] keyed by (seed, env, episode, channel, counter, stream).
+ * Status: 0 = launched; negative = invalid arguments (nothing launched).  Kernel-side faults are reported in the
+ * int32 device status word `status` (0 = ok), which the host reads only when it asks for it.
+ */
+#ifndef ISAAC_NET_B200_H
+#define ISAAC_NET_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define INB_ABI_VERSION 1
+#define INB_MAX_S 32      /* RBGs per carrier */
+#define INB_MAX_P 32      /* HARQ processes */
+#define INB_MAX_F 64      /* frame slots per robot */
+#define INB_MAX_M 64      /* traffic arrivals per robot per step */
+#define INB_MAX_MCS 32
+#define INB_MAX_ROWS 64   /* scheduled slots per control step */
+#define INB_NCTR 64       /* per-env counter words (int64) */
+
+/* counter words of InbStepArgs.ctr (per env, int64), MacLink.ctr / ntx_hist / rv_tx / rv_fail (mac.py:116-126) */
+enum {
+  INB_CTR_TB_NEW = 0, INB_CTR_TB_RETX, INB_CTR_TB_OK, INB_CTR_TB_FAIL, INB_CTR_EXHAUST, INB_CTR_BYTES_OK,
+  INB_CTR_BYTES_NEW, INB_CTR_NEW_WHILE_PENDING, INB_CTR_PRB_USED, INB_CTR_LOST_FRAMES,
+  INB_CTR_NTX_HIST = 16, INB_CTR_RV_TX = 32, INB_CTR_RV_FAIL = 48
+};
+
+/* Per-robot state, reference layouts and dtypes ([E,R], [E,R,S], [E,R,P], [E,R,F]); bool = uint8. */
+typedef struct {
+  int64_t *sent, *floor_, *bsr, *sr_t, *last_tx, *enq;     /* [E,R] */
+  float *olla, *avg;                                       /* [E,R] */
+  float *csi;                                              /* [E,R,S] */
+  float *h;                                                /* [E,R,S,2] AR(1) fading state */
+  float *spec, *k_lin;                                     /* Rician: [E,R,2] phasor, [E,R] K (NULL: Rayleigh) */
+  int64_t *h_state, *h_lo, *h_hi, *h_ready, *h_ntx, *h_mcs, *h_tbs, *h_nsb;   /* [E,R,P] */
+  float *h_comb;                                           /* [E,R,P] */
+  int64_t *cap, *start, *end_, *cls, *hid, *tag, *prio;    /* [E,R,F] */
+  uint8_t *lost, *det;                                     /* [E,R,F] */
+  double *fin, *off, *dline;                               /* [E,R,F] */
+} InbState;
+
+/* Step outputs (the step dict of NREngine.step), [E,R,F] unless noted. */
+typedef struct {
+  uint8_t *delivered, *timed_out, *dropped, *deadline_miss;
+  int64_t *cap, *cls, *arrival_slot, *tag, *priority, *bytes;
+  float *delay;
+  double *arrival;
+  int64_t *newest, *queue_len, *gen_accepted, *gen_bytes;  /* [E,R] */
+  float *queue_bytes, *sinr_db, *pathgain;                 /* [E,R] */
+  uint8_t *det_env;                                        /* [E] */
+} InbOutputs;
+
+/* Traffic arrivals of this step [E,R,M] (TrafficGen.step, sorted by slot), or M = 0. */
+typedef struct {
+  const uint8_t *valid, *det;
+  const float *nbytes;
+  const int64_t *slot, *tag, *prio;
+  const double *dline;
+} InbArrivals;
+
+/* Static tables (built once per engine on the device). */
+typedef struct {
+  const float *bler;            /* [M, C, G] code-block BLER */
+  const float *thr_ref;         /* [M] 10 % BLER SINR of a 10-PRB RBG */
+  const float *se, *beta, *rate;/* [M] spectral efficiency, EESM beta, code rate (float32 as the reference) */
+  const float *w, *lw, *lw10;   /* [S] PRBs per RBG, log(w), 10 log10(w / snr_ref_prbs) */
+  const int32_t *la_tbs;        /* [NPRB+1, M] TBS (bits) of the data-slot symbols */
+  const int32_t *la_i0;         /* [NPRB+1, M] BLER-table code-block index */
+  const float *la_wi, *la_ncb;  /* [NPRB+1, M] code-block interpolation weight, number of code blocks */
+  const float *fk, *fphi;       /* radio shadowing plane waves: [C,E,K,2], [C,E,K] (NULL: pathgain input) */
+  const float *gnb;             /* [C,2] gNB positions */
+} InbTables;
+
+/* Scalars of the step; float values are already rounded to float32 exactly as torch rounds python scalars. */
+typedef struct {
+  int32_t E, R, S, P, F, M, MCS, mcs_max, C_axis, G_axis, nprb, N, K_rows, Kf;
+  int64_t T;                    /* global control step */
+  int32_t rows[INB_MAX_ROWS][4];/* schedule: (rel, UL data symbols, SR opportunity, fading update) */
+  float rowf[INB_MAX_ROWS][2];  /* per row: rho^dt, sqrt(1 - rho^2) of the AR(1) fading update (float32) */
+  int32_t sched;                /* 0 pf, 1 maxci, 2 rr */
+  int32_t olla_on, phr_cap, retx_priority, comb_cc, harq_drop, purge, fading, rician, radio;  /* flags */
+  int32_t sr_delay, ul_rtt, rlc_retx, max_tx, tb_oh, timeout;
+  int32_t dmrs, oh, ref_prbs;
+  uint32_t s0;                  /* seed key */
+  float inv_sqrt2;              /* float32(1) / float32(sqrt(2)): torch's CUDA division by a python scalar */
+  float ul_ref0, noise_prb, ue_tx, sub_noise;   /* ul_ref = (ul_ref0 + pg) - noise_prb; sinr = (pg + ue_tx) - sub_noise */
+  float phr_min, olla_up, olla_dn, pf_a, pf_b, target, inv_S;
+  float s0_snr, inv_ds, c0_cbs, inv_dc;         /* BLER grid: first SNR, 1/step; first CBS, 1/step */
+  double proc_off;              /* proc_offset_ms / control_step_ms */
+  double ctl_ms;                /* control_step_ms */
+  double inv_N_d;               /* 1.0 / slots_per_step (float64) */
+  float inv_ref_prbs;           /* float32(1) / float32(snr_ref_prbs) */
+  /* radio: tr38901 (0 UMi, 1 UMa, forced LOS) or log_distance (2) */
+  int32_t radio_model;
+  float h_bs, h_ut, dbp, fc_term, pl_a, pl_n1, pl_b_term, sigma_sf, amp, hh2;
+  float pl_const, pl_10n;
+} InbParams;
+
+typedef struct {
+  InbParams p;
+  InbState s;
+  InbOutputs o;
+  InbArrivals a;
+  InbTables t;
+  const float *pos;             /* [E,R,2] poses (radio) or NULL */
+  const float *pathgain_in;     /* [E,R] dB path gain (teacher forcing / SNR input) or NULL */
+  const float *ul_ref_in;       /* [E,R,S] per-RBG reference SINR input (snr_db=) or NULL */
+  const int64_t *env_id, *episode;   /* [E] counter-RNG keys */
+  int64_t *rng_ctr;             /* [E] STEP call counter (incremented at the end of the step) */
+  const int64_t *epoch;         /* [E] */
+  const int64_t *last_hid;      /* [E] */
+  int64_t *ctr;                 /* [E, INB_NCTR] counters, accumulated */
+  int32_t *status;              /* device status word */
+  int64_t *trace;               /* optional per-slot trace [K_rows, E, R, 8] (NULL = off): bsr after the SR grant,
+                                   need, won RBG mask, new-TB MCS, flags (has_rx | new_el << 1 | tx_rx << 2 |
+                                   tx_new << 3 | ok << 4), send pointer after the slot, PHR cap, bits of `left` */
+} InbStepArgs;
+
+/* One control step of the NR uplink engine. */
+int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
+
+/* Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial
+ * values, fading state h = N(0,1)/sqrt(2) draws (site H0), Rician phasor (site KPHI) and K. */
+typedef struct {
+  int32_t E, R, S, P, F;
+  uint32_t s0;
+  int32_t rician;
+  float k_lin0, inv_sqrt2, two_pi;
+  const uint8_t *mask;
+  const int64_t *env_id;
+  int64_t *episode, *rng_ctr;
+  InbState s;
+} InbResetArgs;
+int inb_nr_reset(const InbResetArgs *args, void *cuda_stream);
+
+/* Counter-RNG draws out[E, n] (float32) for every env row: uniforms (normal = 0) or normals (normal = 1), channel
+ * RESET or STEP with the given counters. */
+int inb_rng_draw(int32_t E, int32_t n, uint32_t s0, uint32_t channel, uint32_t stream, const int64_t *env_id,
+                 const int64_t *episode, const int64_t *ctr, int32_t normal, float *out, void *cuda_stream);
+
+/* ABI version of the loaded library (INB_ABI_VERSION). */
+int inb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ISAAC_NET_B200_H */

@@ -1,0 +1,114 @@
+"""ctypes binding of the C ABI in include/isaac_net_b200.h (libisaac_net_b200.so, built in-tree).
+
+The structures below mirror the C structures field by field; tests/test_abi.py checks their sizes and offsets
+against the compiled header.  There is no fallback: if the shared library is missing or was built for another ABI
+version, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
+LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200.so")
+ABI_VERSION = 1
+MAX_ROWS = 64
+NCTR = 64
+CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
+             "prb_used", "lost_frames")
+CTR_NTX_HIST, CTR_RV_TX, CTR_RV_FAIL = 16, 32, 48
+
+P = ctypes.c_void_p
+i32, i64, u32, f32, f64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctypes.c_float, ctypes.c_double
+
+STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg", "csi", "h", "spec", "k_lin",
+                "h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb", "cap", "start",
+                "end_", "cls", "hid", "tag", "prio", "lost", "det", "fin", "off", "dline")
+OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
+              "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
+              "sinr_db", "pathgain", "det_env")
+ARR_FIELDS = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
+TAB_FIELDS = ("bler", "thr_ref", "se", "beta", "rate", "w", "lw", "lw10", "la_tbs", "la_i0", "la_wi", "la_ncb", "fk",
+              "fphi", "gnb")
+
+
+class InbState(ctypes.Structure):
+    _fields_ = [(n, P) for n in STATE_FIELDS]
+
+
+class InbOutputs(ctypes.Structure):
+    _fields_ = [(n, P) for n in OUT_FIELDS]
+
+
+class InbArrivals(ctypes.Structure):
+    _fields_ = [(n, P) for n in ARR_FIELDS]
+
+
+class InbTables(ctypes.Structure):
+    _fields_ = [(n, P) for n in TAB_FIELDS]
+
+
+class InbParams(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("E", "R", "S", "P", "F", "M", "MCS", "mcs_max", "C_axis", "G_axis", "nprb", "N",
+                                    "K_rows", "Kf")]
+                + [("T", i64), ("rows", (i32 * 4) * MAX_ROWS), ("rowf", (f32 * 2) * MAX_ROWS), ("sched", i32)]
+                + [(n, i32) for n in ("olla_on", "phr_cap", "retx_priority", "comb_cc", "harq_drop", "purge",
+                                      "fading", "rician", "radio")]
+                + [(n, i32) for n in ("sr_delay", "ul_rtt", "rlc_retx", "max_tx", "tb_oh", "timeout")]
+                + [(n, i32) for n in ("dmrs", "oh", "ref_prbs")]
+                + [("s0", u32), ("inv_sqrt2", f32)]
+                + [(n, f32) for n in ("ul_ref0", "noise_prb", "ue_tx", "sub_noise")]
+                + [(n, f32) for n in ("phr_min", "olla_up", "olla_dn", "pf_a", "pf_b", "target", "inv_S")]
+                + [(n, f32) for n in ("s0_snr", "inv_ds", "c0_cbs", "inv_dc")]
+                + [("proc_off", f64), ("ctl_ms", f64), ("inv_N_d", f64), ("inv_ref_prbs", f32), ("radio_model", i32)]
+                + [(n, f32) for n in ("h_bs", "h_ut", "dbp", "fc_term", "pl_a", "pl_n1", "pl_b_term", "sigma_sf",
+                                      "amp", "hh2")]
+                + [(n, f32) for n in ("pl_const", "pl_10n")])
+
+
+class InbStepArgs(ctypes.Structure):
+    _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
+                ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
+                ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("trace", P)]
+
+
+class InbResetArgs(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("E", "R", "S", "P", "F")] + [("s0", u32), ("rician", i32)]
+                + [(n, f32) for n in ("k_lin0", "inv_sqrt2", "two_pi")]
+                + [(n, P) for n in ("mask", "env_id", "episode", "rng_ctr")] + [("s", InbState)])
+
+
+EXPORTS = ("inb_nr_step", "inb_nr_reset", "inb_rng_draw", "inb_abi_version")
+_lib = None
+
+
+def lib():
+    """The loaded shared library (raises if it is missing: build it with __graft_entry__.build())."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: the B200 engine has no fallback path. Build the CUDA library with "
+                           "`python -c 'import __graft_entry__ as g; g.build()'` (nvcc, sm_100a).")
+    L = ctypes.CDLL(LIB_PATH)
+    L.inb_abi_version.restype = ctypes.c_int
+    L.inb_abi_version.argtypes = []
+    if L.inb_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{LIB_PATH} has ABI {L.inb_abi_version()}, expected {ABI_VERSION}: rebuild it")
+    L.inb_nr_step.restype = ctypes.c_int
+    L.inb_nr_step.argtypes = [ctypes.POINTER(InbStepArgs), P]
+    L.inb_nr_reset.restype = ctypes.c_int
+    L.inb_nr_reset.argtypes = [ctypes.POINTER(InbResetArgs), P]
+    L.inb_rng_draw.restype = ctypes.c_int
+    L.inb_rng_draw.argtypes = [i32, i32, u32, u32, u32, P, P, P, i32, P, P]
+    _lib = L
+    return L
+
+
+def check(rc, what):
+    if rc != 0:
+        raise RuntimeError(f"{what} failed with status {rc}")
+
+
+__all__ = ["lib", "check", "InbStepArgs", "InbResetArgs", "InbParams", "InbState", "InbOutputs", "InbArrivals",
+           "InbTables", "EXPORTS", "LIB_PATH"]

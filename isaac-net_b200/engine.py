@@ -1,0 +1,634 @@
+"""NRB200Engine: isaac-net's NR uplink engine (level "L2") with the control step on B200 CUDA kernels.
+
+Drop-in for ``isaac_net.make_engine("L2", E, R, device, config, backend=...)`` on the uplink path: the same contract
+API as ``NREngine`` (isaac_net/core/engine.py:319-960): ``reset(env_ids)``, ``submit(t, requests, snr_db=None, *,
+tag, priority, deadline_ms)``, ``step(t, x, cur_hid=None, *, snr_db, triggers)`` -> the step dict, ``clock``,
+``counters()``, ``output_schema()``, ``reference_state()`` / ``load_reference_state()`` and the legacy
+``add_frames`` / ``step(t, snr, hid)`` forms.
+
+What runs where:
+  * host (Python / torch plumbing): config checks, the schedule table of each control step, the traffic models'
+    generator draws (TrafficGen, torch.Generator by design), the clocks, and building the argument block;
+  * device (libisaac_net_b200.so, sm_100a): one fused launch per control step (inb_nr_step: enqueue + arrival gate,
+    radio path gain, every scheduled slot, finish and compaction, all outputs) and one per reset (inb_nr_reset).
+There is no CPU path: the engine refuses any device but CUDA, and raises if the shared library is missing.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+
+import numpy as np
+import torch
+
+from . import _native as nat
+from .config import NRConfig
+from .phy import PhyTables
+from .traffic import Requests, TrafficGen, generates
+
+# counter-RNG constants (isaac_net/core/proto/rng.py:33-38, nr_rng.py:34, radio.py:53-56)
+M32 = 0xFFFFFFFF
+GOLD = 0x9E3779B9
+CH_RESET = 3
+RADIO_STREAM = 0x52 << 16
+LOG_DISTANCE_STREAM = 10
+# TR 38.901: (default BS height, SF correlation LOS, SF correlation NLOS, sigma_SF LOS, sigma_SF NLOS, PL a, n1, b)
+SCN = {"UMi": (10.0, 10.0, 13.0, 4.0, 7.82, 32.4, 21.0, 9.5), "UMa": (25.0, 37.0, 50.0, 4.0, 6.0, 28.0, 22.0, 9.0)}
+
+
+class B200Unsupported(NotImplementedError, ValueError):
+    """The config asks for a feature the B200 engine does not implement (see NRConfig.refusals)."""
+
+
+def _mix32(x):
+    x ^= x >> 16
+    x = (x * 0x21F0AAAD) & M32
+    x ^= x >> 15
+    x = (x * 0x735A2D97) & M32
+    return x ^ (x >> 15)
+
+
+def _salt(v):
+    return (_mix32(v & M32) + GOLD) & M32
+
+
+def seed_key(seed):
+    """Key of an engine seed (CounterRNG.s0, proto/rng.py:60)."""
+    seed = int(seed)
+    return _mix32(_mix32(seed & M32) ^ _salt((seed >> 32) & M32))
+
+
+def _f32(x):
+    return float(np.float32(x))
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else None
+
+
+def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, sizes=None, seed=None, strict=False):
+    """The B200 NR engine for E envs x R robots (isaac_net/core/engine.py:232-293)."""
+    if level != "L2":
+        raise ValueError(f"the B200 backend implements level 'L2' (the NR engine), not {level!r}")
+    if backend not in ("b200", "auto"):
+        raise ValueError(f"unknown backend {backend!r}; this package provides 'b200'")
+    cfg = config if config is not None else NRConfig()
+    if sizes is not None:
+        cfg = cfg.with_(msg_sizes=tuple(float(s) for s in sizes))
+    if seed is None:
+        seed = cfg.seed
+    return NRB200Engine(E, R, device, cfg, seed=seed)
+
+
+class NRB200Engine:
+    """Contract API of NREngine over the fused B200 kernels (one cell, uplink)."""
+
+    level = "L2"
+    backend = "b200"
+
+    def __init__(self, E, R, device, cfg: NRConfig, seed=None):
+        no = cfg.refusals()
+        if no:
+            raise B200Unsupported("the B200 engine does not implement " + "; ".join(f"{f}: {w}" for f, w in no))
+        dev = torch.device(device)
+        if dev.type != "cuda":
+            raise B200Unsupported(f"the B200 engine runs on CUDA devices only (got {dev}); it has no CPU path")
+        if not 1 <= R <= 128:
+            raise B200Unsupported(f"R={R}: the B200 engine handles 1..128 robots per env")
+        if cfg.special_ul_data and "S" in cfg.tdd_pattern:
+            raise B200Unsupported("UL data in special slots (a second UL symbol count) is not built")
+        if dev.index is None:
+            dev = torch.device("cuda", torch.cuda.current_device())
+        self.L = nat.lib()
+        self.E, self.R, self.dev, self.config = E, R, dev, cfg
+        if seed is None:
+            seed = int(torch.randint(0, 2 ** 62, ()).item())
+        self.seed = int(seed)
+        self.S, self.P, self.F, self.N = cfg.n_subbands, cfg.n_harq, cfg.frame_buffer, cfg.slots_per_step
+        self.tab = PhyTables(cfg, cfg.subband_prbs, dev)
+        self.rician = cfg.rician_mode == "fixed"
+        self._alloc_state()
+        self.s0 = seed_key(self.seed)
+        self.env_id = torch.arange(E, dtype=torch.long, device=dev)
+        self.env_offset = 0
+        self.episode = torch.full((E,), -1, dtype=torch.long, device=dev)
+        self.rng_ctr = torch.zeros(E, dtype=torch.long, device=dev)
+        self.ctr = torch.zeros(E, nat.NCTR, dtype=torch.long, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.T = 0
+        self.epoch = torch.zeros(E, dtype=torch.long, device=dev)
+        self._uniform_epoch = 0
+        self._last_snr = torch.zeros(E, R, device=dev)
+        self._last_hid = torch.zeros(E, dtype=torch.long, device=dev)
+        self.last_g = None
+        self.prb_avail = 0.0
+        self.traffic = None
+        self._extras = False
+        if generates(cfg.traffic):
+            tseed = (int(self.seed) * 6364136223846793005 + 1442695040888963407) % 2 ** 62
+            self.traffic = TrafficGen(cfg.traffic, E, R, dev, cfg.control_step_ms, self.N, seed=tseed)
+            self._extras = True
+        self._fields = None
+        self._gnb = torch.tensor(cfg.gnb_xy(), dtype=torch.float32, device=dev).contiguous()
+        self._sched = {}
+        self._args = nat.InbStepArgs()
+        self._fill_static()
+        self._kernel_reset(None)
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_state(self):
+        E, R, S, P, F, d = self.E, self.R, self.S, self.P, self.F, self.dev
+        full = lambda shape, dt, v: torch.full(shape, v, dtype=dt, device=d)
+        L, f32, b = torch.long, torch.float32, torch.bool
+        st = {}
+        for n, v in (("sent", 0), ("floor_", 0), ("bsr", 0), ("sr_t", -1), ("last_tx", -1), ("enq", 0)):
+            st[n] = full((E, R), L, v)
+        st["olla"], st["avg"] = full((E, R), f32, 0.0), full((E, R), f32, 100.0)
+        st["csi"] = full((E, R, S), f32, 0.0)
+        st["h"] = full((E, R, S, 2), f32, 0.0)
+        if self.rician:
+            st["spec"], st["k_lin"] = full((E, R, 2), f32, 0.0), full((E, R), f32, 0.0)
+        for n in ("h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb"):
+            st[n] = full((E, R, P), L, 0)
+        st["h_comb"] = full((E, R, P), f32, 0.0)
+        st["cap"] = full((E, R, F), L, -1)
+        for n in ("start", "end_", "cls", "hid", "tag", "prio"):
+            st[n] = full((E, R, F), L, 0)
+        st["lost"], st["det"] = full((E, R, F), b, False), full((E, R, F), b, False)
+        st["fin"] = full((E, R, F), torch.float64, math.inf)
+        st["off"] = full((E, R, F), torch.float64, 0.0)
+        st["dline"] = full((E, R, F), torch.float64, math.inf)
+        self.st = st
+
+    def _state_struct(self):
+        s = nat.InbState()
+        for n in nat.STATE_FIELDS:
+            t = self.st.get(n)
+            setattr(s, n, t.data_ptr() if t is not None else None)
+        return s
+
+    def _fill_static(self):
+        cfg, a, tab = self.config, self._args, self.tab
+        p = a.p
+        p.E, p.R, p.S, p.P, p.F = self.E, self.R, self.S, self.P, self.F
+        p.MCS, p.mcs_max, p.C_axis, p.G_axis = tab.M, tab.mcs_max, tab.C, tab.G
+        p.nprb, p.N = cfg.nprb, self.N
+        p.sched = {"pf": 0, "maxci": 1, "rr": 2}[cfg.scheduler]
+        p.olla_on, p.phr_cap, p.retx_priority = int(cfg.olla), int(cfg.phr_cap), int(cfg.retx_priority)
+        p.comb_cc, p.harq_drop = int(cfg.harq_combining == "cc"), int(cfg.harq_fail == "drop")
+        p.purge, p.fading, p.rician = int(cfg.discard == "purge"), int(cfg.fading), int(self.rician)
+        p.sr_delay, p.ul_rtt, p.rlc_retx = cfg.sr_delay, cfg.ul_rtt, cfg.rlc_retx_slots
+        p.max_tx, p.tb_oh, p.timeout = cfg.max_harq_tx, cfg.tb_overhead_bytes, cfg.timeout_steps
+        p.dmrs, p.oh, p.ref_prbs = cfg.dmrs_re_per_prb, cfg.overhead_re_per_prb, cfg.snr_ref_prbs
+        p.s0 = 0
+        p.inv_sqrt2 = _f32(np.float32(1.0) / np.float32(math.sqrt(2)))
+        p.ul_ref0 = _f32(cfg.ue_tx_dbm - 10 * math.log10(cfg.snr_ref_prbs))
+        p.noise_prb = _f32(cfg.noise_dbm_per_prb("gnb"))
+        p.ue_tx = _f32(cfg.ue_tx_dbm)
+        p.sub_noise = _f32(cfg.subband_noise_dbm)
+        p.phr_min = _f32(cfg.phr_min_db)
+        p.olla_up = _f32(cfg.olla_up_db)
+        p.olla_dn = _f32(cfg.olla_up_db * (1 - cfg.bler_target) / cfg.bler_target)
+        p.pf_a = _f32(1 - 1 / cfg.pf_window)
+        p.pf_b = _f32(1 / cfg.pf_window)
+        p.target = _f32(cfg.bler_target)
+        p.inv_S = _f32(1.0 / self.S)
+        p.s0_snr, p.c0_cbs = _f32(tab.s0), _f32(tab.c0)
+        p.inv_ds = _f32(np.float32(1.0) / np.float32(tab.ds))
+        p.inv_dc = _f32(np.float32(1.0) / np.float32(tab.dc))
+        p.proc_off = cfg.proc_offset_ms / cfg.control_step_ms
+        p.ctl_ms = float(cfg.control_step_ms)
+        p.inv_N_d = 1.0 / self.N
+        p.inv_ref_prbs = _f32(np.float32(1.0) / np.float32(cfg.snr_ref_prbs))
+        K = cfg.shadow_modes
+        p.Kf = K
+        if cfg.channel == "tr38901":
+            hbs, _, _, sl, _, pa, n1, bb = SCN[cfg.tr38901_scenario]
+            h_bs = float(cfg.gnb_height_m) if cfg.gnb_height_m is not None else hbs
+            h_ut = float(cfg.ue_height_m)
+            fc = cfg.carrier_ghz * 1e9
+            dbp = 4 * (h_bs - 1.0) * (h_ut - 1.0) * fc / 3.0e8
+            p.radio_model = 0 if cfg.tr38901_scenario == "UMi" else 1
+            p.h_bs, p.h_ut, p.dbp = _f32(h_bs), _f32(h_ut), _f32(dbp)
+            p.pl_a, p.pl_n1 = _f32(pa), _f32(n1)
+            p.fc_term = _f32(20 * math.log10(cfg.carrier_ghz))
+            p.pl_b_term = _f32(bb * math.log10(dbp ** 2 + (h_bs - h_ut) ** 2))
+            p.sigma_sf = _f32(sl)
+            p.amp = _f32(math.sqrt(2 / K))
+            p.hh2 = _f32((h_bs - h_ut) ** 2)
+            if cfg.tr38901_los != "los":
+                raise B200Unsupported("tr38901 with an NLOS state is not built (forced LOS only)")
+        elif cfg.channel == "log_distance":
+            p.radio_model = 2
+            p.pl_const, p.pl_10n = _f32(cfg.pl_const_db), _f32(10 * cfg.pathloss_exp)
+            p.amp = _f32(cfg.shadow_sigma_db * math.sqrt(2 / K))
+        a.s = self._state_struct()
+        t = a.t
+        t.bler, t.thr_ref, t.se, t.beta, t.rate = (tab.bler.data_ptr(), tab.thr_ref.data_ptr(), tab.se.data_ptr(),
+                                                   tab.beta.data_ptr(), tab.rate.data_ptr())
+        t.w, t.lw, t.lw10 = tab.w.data_ptr(), tab.lw.data_ptr(), tab.lw10.data_ptr()
+        t.la_tbs, t.la_i0, t.la_wi, t.la_ncb = (tab.la_tbs.data_ptr(), tab.la_i0.data_ptr(), tab.la_wi.data_ptr(),
+                                                tab.la_ncb.data_ptr())
+        t.gnb = self._gnb.data_ptr()
+        a.env_id, a.episode, a.rng_ctr = self.env_id.data_ptr(), self.episode.data_ptr(), self.rng_ctr.data_ptr()
+        a.epoch, a.last_hid, a.ctr, a.status = (self.epoch.data_ptr(), self._last_hid.data_ptr(),
+                                                self.ctr.data_ptr(), self.status.data_ptr())
+
+    def _stream(self):
+        return ctypes.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
+
+    # ------------------------------------------------------------------ radio fields (channels/fields.py:38-91)
+    def _uniforms(self, stream, n):
+        out = torch.empty(self.E, n, dtype=torch.float32, device=self.dev)
+        rc = self.L.inb_rng_draw(self.E, n, self.s0, CH_RESET, stream, self.env_id.data_ptr(), self.episode.data_ptr(),
+                                 None, 0, out.data_ptr(), self._stream())
+        nat.check(rc, "inb_rng_draw")
+        return out
+
+    def _plane_waves(self, stream, spectrum, dcorr):
+        C, K = 1, self.config.shadow_modes
+        rand = lambda i: self._uniforms(stream + i, C * K).view(self.E, C, K)
+        ang = rand(0) * 2 * math.pi
+        if spectrum == "sos":
+            wl = 20 + 40 * rand(1)
+            if dcorr != 10.3:
+                wl = wl * (dcorr / 10.3)
+            k = torch.stack([torch.cos(ang), torch.sin(ang)], -1) * (2 * math.pi / wl)[..., None]
+        else:
+            u = rand(1).clamp(max=1 - 1e-6)
+            kmag = torch.sqrt((1 - u) ** -2 - 1) / dcorr
+            k = torch.stack([torch.cos(ang), torch.sin(ang)], -1) * kmag[..., None]
+        phi = rand(2) * 2 * math.pi
+        return k.permute(1, 0, 2, 3).contiguous(), phi.permute(1, 0, 2).contiguous()
+
+    def _draw_fields(self):
+        cfg = self.config
+        if cfg.channel == "tr38901":
+            return self._plane_waves(RADIO_STREAM + 16, "exp", SCN[cfg.tr38901_scenario][1])
+        return self._plane_waves(LOG_DISTANCE_STREAM, cfg.shadow_acf, cfg.shadow_dcorr_m)
+
+    def _make_radio(self):
+        self._fields = self._draw_fields()
+        self._bind_fields()
+
+    def _bind_fields(self):
+        k, phi = self._fields
+        self._args.t.fk, self._args.t.fphi = k.data_ptr(), phi.data_ptr()
+
+    def _reset_radio(self, m):
+        if self._fields is None:
+            return
+        k, phi = self._draw_fields()
+        k0, p0 = self._fields
+        k0.copy_(torch.where(m.view(1, -1, 1, 1), k, k0))
+        p0.copy_(torch.where(m.view(1, -1, 1), phi, p0))
+
+    # ------------------------------------------------------------------ resets
+    def _kernel_reset(self, mask):
+        a = nat.InbResetArgs()
+        a.E, a.R, a.S, a.P, a.F = self.E, self.R, self.S, self.P, self.F
+        a.s0, a.rician = self.s0, int(self.rician)
+        a.k_lin0 = _f32(10 ** (self.config.rician_k_db / 10)) if self.rician else 0.0
+        a.inv_sqrt2 = self._args.p.inv_sqrt2
+        a.two_pi = _f32(2 * math.pi)
+        a.mask = mask.data_ptr() if mask is not None else None
+        a.env_id, a.episode, a.rng_ctr = self.env_id.data_ptr(), self.episode.data_ptr(), self.rng_ctr.data_ptr()
+        a.s = self._state_struct()
+        nat.check(self.L.inb_nr_reset(ctypes.byref(a), self._stream()), "inb_nr_reset")
+
+    def _ids(self, env_ids):
+        if env_ids is None or (isinstance(env_ids, slice) and env_ids == slice(None)):
+            return None
+        if isinstance(env_ids, torch.Tensor):
+            if env_ids.dtype == torch.bool:
+                return env_ids.to(self.dev).nonzero(as_tuple=True)[0]
+            return env_ids.to(device=self.dev, dtype=torch.long).reshape(-1)
+        return torch.as_tensor(list(env_ids), dtype=torch.long, device=self.dev)
+
+    def reset(self, env_ids=None):
+        """Re-initialize env_ids (None = all): queues, HARQ, SR/BSR, OLLA, PF, CSI, fading, radio and clock."""
+        ids = self._ids(env_ids)
+        if ids is not None and ids.numel() == 0:
+            return
+        if ids is None:
+            if self.traffic is not None:
+                self.traffic.reset(None)
+            self._kernel_reset(None)
+            self.ctr.zero_()
+            self.prb_avail = 0.0
+            self.T = 0
+            self.epoch.zero_()
+            self._uniform_epoch = 0
+            self._last_snr.zero_()
+            self._last_hid.zero_()
+            self.last_g = None
+            if self._fields is not None:
+                self._reset_radio(torch.ones(self.E, dtype=torch.bool, device=self.dev))
+            return
+        m = torch.zeros(self.E, dtype=torch.bool, device=self.dev)
+        m[ids] = True
+        if self.traffic is not None:
+            self.traffic.reset(m)
+        self._kernel_reset(m)
+        self.epoch.index_fill_(0, ids, self.T)
+        self._uniform_epoch = None
+        self._last_snr.index_fill_(0, ids, 0.0)
+        self._last_hid.index_fill_(0, ids, 0)
+        self._reset_radio(m)
+
+    def set_env_offset(self, offset):
+        """Key the counter RNG rows by global env id offset + i (a shard of a larger batch, sharded.py:61-77)."""
+        offset = int(offset)
+        self.env_id.add_(offset - self.env_offset)
+        self.env_offset = offset
+
+    # ------------------------------------------------------------------ clocks
+    @property
+    def clock(self):
+        return self.T - self.epoch
+
+    def _now(self, t):
+        if t is None:
+            return self.T
+        if isinstance(t, torch.Tensor):
+            if t.dim() == 0:
+                t = int(t)
+            else:
+                if not torch.equal(t.to(self.dev, torch.long), self.clock):
+                    raise ValueError("t must equal the engine clock (the NR engine cannot jump in time); pass t=None")
+                return self.T
+        t = int(t)
+        if self._uniform_epoch is None:
+            raise ValueError("after a partial reset the envs have different clocks: pass t=None")
+        if t + self._uniform_epoch != self.T:
+            raise ValueError(f"t={t} but the engine clock is {self.T - self._uniform_epoch}: pass t=None")
+        return self.T
+
+    # ------------------------------------------------------------------ policy messages (engine.py:796-819)
+    def submit(self, t, requests, snr_db=None, *, tag=None, priority=None, deadline_ms=None):
+        """Enqueue the policy's messages at capture step t: Requests or send [E,R]; returns accepted [E,R]."""
+        T = self._now(t)
+        req = requests if isinstance(requests, Requests) else Requests(send=requests)
+        send = req.send.to(self.dev, torch.long)
+        det = req.det.to(self.dev, torch.bool) if req.det is not None else torch.zeros_like(send, dtype=torch.bool)
+        hid = req.hid.to(self.dev, torch.long) if req.hid is not None else torch.zeros(self.E, dtype=torch.long,
+                                                                                          device=self.dev)
+        self._last_hid.copy_(hid)
+        if tag is not None or priority is not None or deadline_ms is not None:
+            self._extras = True
+        st, F = self.st, self.F
+        sizes = torch.tensor(self.config.msg_sizes, dtype=torch.float32, device=self.dev)
+        nbytes = sizes[(send - 1).clamp(min=0)]
+        cnt = (st["cap"] >= 0).sum(-1)
+        acc = (send > 0) & (cnt < F) & (nbytes > 0)
+        i = cnt.clamp(max=F - 1)
+        oh = (i[..., None] == torch.arange(F, device=self.dev)) & acc[..., None]
+        nb = nbytes.round().long()
+        put = lambda n, v: st[n].copy_(torch.where(oh, v[..., None].to(st[n].dtype) if torch.is_tensor(v)
+                                                   else torch.full_like(st[n], v), st[n]))
+        put("cap", T)
+        put("start", st["enq"])
+        put("end_", st["enq"] + nb)
+        put("lost", False)
+        put("fin", math.inf)
+        put("off", 0.0)
+        put("cls", send)
+        put("det", det)
+        put("hid", hid[:, None].expand(-1, self.R))
+        for n, v, dflt in (("tag", tag, 0), ("prio", priority, 0), ("dline", deadline_ms, math.inf)):
+            if v is None:
+                put(n, dflt)
+            else:
+                put(n, torch.as_tensor(v, dtype=st[n].dtype, device=self.dev).expand(self.E, self.R))
+        st["enq"].add_(nb * acc)
+        return acc
+
+    def add_frames(self, t, send, det, hid, snr_db):
+        """Legacy wrapper (NetSlot API)."""
+        self.submit(t, Requests(send, det, hid), snr_db)
+
+    # ------------------------------------------------------------------ one control step
+    def _rows(self, g0):
+        """Schedule rows of the step at slot g0 with the fading coefficients of each row (advances last_g)."""
+        cfg = self.config
+        sched = cfg.schedule(g0)
+        dt0 = 0 if not sched else (1 if self.last_g is None else g0 + sched[0][0] - self.last_g)
+        key = (g0 % cfg.schedule_period(), dt0 if cfg.fading else 0)
+        ent = self._sched.get(key)
+        if ent is None:
+            rows, rowf = [], []
+            prev = None
+            for rel, uls, sr in sched:
+                dt = dt0 if prev is None else rel - prev
+                prev = rel
+                rho = cfg.fading_rho_per_ms ** (dt * cfg.slot_ms)
+                rows.append((rel, uls, int(sr), int(dt > 0)))
+                rowf.append((_f32(rho), _f32(math.sqrt(1 - rho ** 2))))
+            if len(rows) > nat.MAX_ROWS:
+                raise B200Unsupported(f"{len(rows)} scheduled slots per control step (at most {nat.MAX_ROWS})")
+            ent = (rows, rowf, sum(1 for r in rows if r[1]))
+            self._sched[key] = ent
+        if sched and cfg.fading:
+            self.last_g = g0 + sched[-1][0]
+        return ent
+
+    def _out_layout(self, M):
+        E, R, F = self.E, self.R, self.F
+        spec = [("delivered", torch.bool, (E, R, F)), ("timed_out", torch.bool, (E, R, F)),
+                ("dropped", torch.bool, (E, R, F)), ("deadline_miss", torch.bool, (E, R, F)),
+                ("cap", torch.long, (E, R, F)), ("cls", torch.long, (E, R, F)),
+                ("arrival_slot", torch.long, (E, R, F)), ("tag", torch.long, (E, R, F)),
+                ("priority", torch.long, (E, R, F)), ("bytes", torch.long, (E, R, F)),
+                ("delay", torch.float32, (E, R, F)), ("arrival", torch.float64, (E, R, F)),
+                ("newest", torch.long, (E, R)), ("queue_len", torch.long, (E, R)),
+                ("gen_accepted", torch.long, (E, R)), ("gen_bytes", torch.long, (E, R)),
+                ("queue_bytes", torch.float32, (E, R)), ("sinr_db", torch.float32, (E, R)),
+                ("pathgain", torch.float32, (E, R)), ("det_env", torch.bool, (E,))]
+        off, lay = 0, []
+        for n, dt, shape in spec:
+            nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
+            lay.append((n, dt, shape, off, nb))
+            off += (nb + 255) // 256 * 256
+        return lay, off
+
+    def _alloc_outputs(self):
+        lay = getattr(self, "_lay", None)
+        if lay is None:
+            self._lay = lay = self._out_layout(0)
+        spec, total = lay
+        blob = torch.empty(total, dtype=torch.uint8, device=self.dev)
+        out = {}
+        o = nat.InbOutputs()
+        for n, dt, shape, off, nb in spec:
+            v = blob[off:off + nb].view(dt).view(shape)
+            out[n] = v
+            setattr(o, n, v.data_ptr())
+        return out, o
+
+    def step(self, t=None, x=None, cur_hid=None, *, snr_db=None, dl_snr_db=None, pathgain_db=None, vel=None,
+             triggers=None, blockers=None, _pathgain=None, _arrivals=None):
+        """Advance [t, t+1). x: poses [E,R,2|3] (through the engine's radio) or SNR [E,R] dB; snr_db= [E,R] or
+        [E,R,S]; triggers= feeds event traffic models.  Returns the step dict (or (newest, det_env) in the legacy
+        form step(t, snr, cur_hid))."""
+        cfg = self.config
+        if dl_snr_db is not None:
+            raise B200Unsupported("dl_snr_db: the downlink is not built")
+        if pathgain_db is not None:
+            raise ValueError("pathgain_db= needs config.n_cells > 1; use x (poses or SNR) with one cell")
+        if blockers is not None:
+            raise B200Unsupported("blockers= (screen blockage) is not built")
+        T = self._now(t)
+        legacy = cur_hid is not None
+        if legacy:
+            self._last_hid.copy_(cur_hid.to(self.dev, torch.long))
+        E, R, S, a, p = self.E, self.R, self.S, self._args, self._args.p
+        keep = []                                   # tensors whose pointers the launch reads
+        gen = None
+        if self.traffic is not None:
+            arr = self.traffic.step(self.clock, triggers) if _arrivals is None else _arrivals
+            self.last_arrivals = arr
+            M = arr.valid.shape[-1]
+            if M > 64:
+                raise B200Unsupported(f"{M} traffic arrivals per robot per step (at most 64)")
+            fields = {"valid": arr.valid, "det": arr.det, "nbytes": arr.nbytes, "slot": arr.slot, "tag": arr.tag,
+                      "prio": arr.prio, "dline": arr.dline}
+            for n, v in fields.items():
+                v = v.contiguous()
+                keep.append(v)
+                setattr(a.a, n, v.data_ptr())
+            p.M = M
+            gen = arr
+        else:
+            p.M = 0
+            for n in nat.ARR_FIELDS:
+                setattr(a.a, n, None)
+        # inputs
+        a.pos = a.pathgain_in = a.ul_ref_in = None
+        snr_out = None
+        if _pathgain is not None:
+            pg = _pathgain.to(self.dev, torch.float32).contiguous()
+            keep.append(pg)
+            a.pathgain_in = pg.data_ptr()
+        elif snr_db is not None or (x is not None and x.dim() == 2):
+            s = snr_db if snr_db is not None else x
+            s = s.to(self.dev, torch.float32)
+            ref = (s if s.dim() == 3 else s[..., None].expand(E, R, S)).contiguous()
+            zero = torch.zeros(E, R, device=self.dev)
+            keep += [ref, zero]
+            a.ul_ref_in, a.pathgain_in = ref.data_ptr(), zero.data_ptr()
+            snr_out = s if s.dim() == 2 else s.mean(-1)
+        elif x is not None and x.dim() == 3:
+            pos = x[..., :2].to(self.dev, torch.float32).contiguous()
+            keep.append(pos)
+            if self._fields is None:
+                self._make_radio()
+            a.pos = pos.data_ptr()
+        else:
+            raise ValueError("step needs poses [E,R,2|3] or an SNR [E,R] (x= or snr_db=)")
+        rows, rowf, n_ul = self._rows(T * self.N)
+        p.K_rows = len(rows)
+        for k, (r4, f2) in enumerate(zip(rows, rowf)):
+            p.rows[k][0], p.rows[k][1], p.rows[k][2], p.rows[k][3] = r4
+            p.rowf[k][0], p.rowf[k][1] = f2
+        p.T = T
+        p.s0 = self.s0
+        out, o = self._alloc_outputs()
+        a.o = o
+        tr = getattr(self, "trace_buf", None)
+        a.trace = tr.data_ptr() if tr is not None else None
+        nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+        self.prb_avail += float(cfg.nprb) * E * n_ul
+        self.T = T + 1
+        sinr = out.pop("sinr_db") if snr_out is None else snr_out.clone()
+        self.pathgain = out.pop("pathgain")
+        self._last_snr.copy_(sinr)
+        if legacy:
+            return out["newest"], out["det_env"]
+        res = {k: out[k] for k in ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "delay",
+                                   "queue_len", "queue_bytes")}
+        if self._extras:
+            for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
+                res[k] = out[k]
+        res["sinr_db"] = sinr
+        res["serving_cell"] = torch.zeros(E, R, dtype=torch.long, device=self.dev)
+        res["t"] = (T - self.epoch).clone()
+        if gen is not None:
+            res["gen_accepted"] = out["gen_accepted"]
+            res["gen_bytes"] = out["gen_bytes"]
+        self._keep = keep                           # the launch is asynchronous: keep its inputs alive
+        return res
+
+    # ------------------------------------------------------------------ observability
+    def counters(self):
+        """{"ul": counters} as NRNet.counters() (nr_engine.py:916-925), folded from the per-env device words."""
+        c = self.ctr.sum(0).cpu()
+        res = {k: float(c[i]) for i, k in enumerate(nat.CTR_NAMES)}
+        res["prb_avail"] = self.prb_avail
+        H = self.config.max_harq_tx + 1
+        res["ntx_hist"] = [float(v) for v in c[nat.CTR_NTX_HIST:nat.CTR_NTX_HIST + H]]
+        res["rv_tx"] = [float(v) for v in c[nat.CTR_RV_TX:nat.CTR_RV_TX + H]]
+        res["rv_fail"] = [float(v) for v in c[nat.CTR_RV_FAIL:nat.CTR_RV_FAIL + H]]
+        return {"ul": res}
+
+    def queued(self):
+        return (self.st["cap"] >= 0).sum(-1)
+
+    def output_schema(self):
+        """{key: {"shape", "dtype"}} of the keys step() returns under this config."""
+        E, R, F = self.E, self.R, self.F
+        sch = {"newest": ((E, R), "int64"), "det_env": ((E,), "bool"), "delivered": ((E, R, F), "bool"),
+               "timed_out": ((E, R, F), "bool"), "dropped": ((E, R, F), "bool"), "cap": ((E, R, F), "int64"),
+               "cls": ((E, R, F), "int64"), "delay": ((E, R, F), "float32"), "queue_len": ((E, R), "int64"),
+               "queue_bytes": ((E, R), "float32"), "sinr_db": ((E, R), "float32"),
+               "serving_cell": ((E, R), "int64"), "t": ((E,), "int64")}
+        if self._extras:
+            sch.update({"arrival": ((E, R, F), "float64"), "arrival_slot": ((E, R, F), "int64"),
+                        "tag": ((E, R, F), "int64"), "priority": ((E, R, F), "int64"),
+                        "bytes": ((E, R, F), "int64"), "deadline_miss": ((E, R, F), "bool")})
+        if self.traffic is not None:
+            sch.update({"gen_accepted": ((E, R), "int64"), "gen_bytes": ((E, R), "int64")})
+        return {k: {"shape": s, "dtype": d} for k, (s, d) in sch.items()}
+
+    # ------------------------------------------------------------------ state exchange (reference names)
+    _REF = {"ul.sent": "sent", "ul.floor": "floor_", "ul.olla": "olla", "ul.avg": "avg", "ul.bsr": "bsr",
+            "ul.sr_t": "sr_t", "ul.last_tx": "last_tx", "ul.csi": "csi", "ul.h_state": "h_state",
+            "ul.h_lo": "h_lo", "ul.h_hi": "h_hi", "ul.h_ready": "h_ready", "ul.h_ntx": "h_ntx",
+            "ul.h_mcs": "h_mcs", "ul.h_tbs": "h_tbs", "ul.h_nsb": "h_nsb", "ul.h_comb": "h_comb",
+            "q.cap": "cap", "q.start": "start", "q.end": "end_", "q.lost": "lost", "q.fin": "fin", "q.enq": "enq",
+            "q.cls": "cls", "q.det": "det", "q.hid": "hid", "q.off": "off", "q.tag": "tag", "q.prio": "prio",
+            "q.dline": "dline", "net.h": "h", "net.spec": "spec", "net.k_lin": "k_lin"}
+
+    def reference_state(self):
+        """Engine state under the reference's names (ul.*, q.*, net.*, rng.*, eng.*), device tensors (views)."""
+        out = {k: self.st[v] for k, v in self._REF.items() if v in self.st}
+        out["net.last_g"] = torch.tensor(-1 if self.last_g is None else self.last_g)
+        out["rng.episode"], out["rng.ctr_step"] = self.episode, self.rng_ctr
+        out["eng.T"], out["eng.epoch"] = torch.tensor(self.T), self.epoch
+        out["eng.last_snr"], out["eng.last_hid"] = self._last_snr, self._last_hid
+        return out
+
+    def load_reference_state(self, snap):
+        """Copy a state dict keyed by the reference's names into the engine's buffers (in place)."""
+        for k, v in snap.items():
+            t = torch.as_tensor(np.asarray(v) if not torch.is_tensor(v) else v)
+            if k in self._REF and self._REF[k] in self.st:
+                self.st[self._REF[k]].copy_(t.to(self.dev))
+            elif k == "net.last_g":
+                self.last_g = None if int(t) < 0 else int(t)
+            elif k == "rng.episode":
+                self.episode.copy_(t.to(self.dev))
+            elif k == "rng.ctr_step":
+                self.rng_ctr.copy_(t.to(self.dev))
+            elif k == "eng.T":
+                self.T = int(t)
+            elif k == "eng.epoch":
+                self.epoch.copy_(t.to(self.dev))
+            elif k == "eng.last_snr":
+                self._last_snr.copy_(t.to(self.dev))
+            elif k == "eng.last_hid":
+                self._last_hid.copy_(t.to(self.dev))
+        if torch.any(self.epoch != 0):
+            self._uniform_epoch = None
+
+
+__all__ = ["make_engine", "NRB200Engine", "B200Unsupported", "seed_key"]
