@@ -1,0 +1,293 @@
+"""Benchmark of the B200 NR uplink engine: env-steps/s (envs x control steps per second).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 2]
+    python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
+        bench.py --gpus N ...
+
+One step = one control step of the engine over its whole batch: traffic generation, the fused kernel (enqueue and
+arrival gate, radio, the K = 10 slots, finish) and the step dict, through the public API (engine.step).  The default
+workload is BASELINE config 2 (4096 envs x 32 robots, 100 MHz / 18 RBGs, PF, Rician K = 5 dB, mixed periodic +
+Poisson traffic) per GPU; with N GPUs every rank runs its own 4096-env shard (global env ids rank * 4096 + i, no
+collective inside the step), so per-GPU work is fixed ("scaling": "weak").
+
+  value   env-steps/s with the poses already resident in HBM, K steps between a barrier + synchronize pair, timed
+          with CUDA events, max over ranks;
+  e2e     the same through the public API from pinned host memory: every step copies its poses host -> device and
+          reads the per-robot observations (newest, queue_len, queue_bytes, sinr_db) back device -> host;
+  roofline  algorithmic bytes of one fused launch (every per-robot state field read and written once at the
+          reference's widths, the step-dict outputs and the pose input: 6680 B per robot for config 2) / its average
+          duration (CUDA events on the launching stream), against the measured HBM copy bandwidth;
+  cpu_baseline  the oracle port (oracle/nr_oracle.py, torch on the host cores, the reference's own op sequence) on a
+          bounded sample of the same workload.
+The state of one step is ~0.9 GB for config 2, larger than the 126 MB L2, so no L2 flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+
+def b_env(cfg, R):
+    """Algorithmic bytes per env-step (reference widths): per-robot state read + written once, outputs, pose."""
+    S, P, F, C = cfg.n_subbands, cfg.n_harq, cfg.frame_buffer, cfg.n_cells
+    tr = 1 if cfg.traffic else 0
+    mc = 1 if C > 1 else 0
+    per = 2 * (56 + 4 * S + 8 * C * S + 76 * P + 50 * F + 32 * F * tr + 40 * mc) + (23 * F + 32) + \
+        (41 * F + 16) * tr + 8
+    return R * per + 16 * C * S * mc
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        try:
+            os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
+            self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.f.close()
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in open(self.path):
+            c = [x.strip() for x in line.split(",")]
+            if len(c) < 9:
+                continue
+            try:
+                sm.append(float(c[1]))
+                mx = float(c[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, c[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n):
+    if int(os.environ.get("WORLD_SIZE", "1")) <= 1:
+        return 0, 1, None
+    import datetime
+    import torch.distributed as dist
+    rank = int(os.environ["RANK"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", local))
+    return rank, dist.get_world_size(), dist
+
+
+def cpu_baseline(wl, cfg, E_sample, steps, warm=1):
+    """The oracle port (reference op sequence, torch on the host cores) on E_sample envs of the workload."""
+    from oracle.nr_oracle import OracleEngine
+    tr = importlib.import_module("isaac-net_b200.traffic")
+    presets = importlib.import_module("isaac-net_b200.presets")
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    E, R = E_sample, wl.R
+    o = OracleEngine(cfg, E, R, "cpu", seed=wl.seed, reduce="aten")
+    tseed = (int(wl.seed) * 6364136223846793005 + 1442695040888963407) % 2 ** 62
+    gen = tr.TrafficGen(cfg.traffic, E, R, "cpu", cfg.control_step_ms, cfg.slots_per_step, seed=tseed) \
+        if cfg.traffic else None
+    mot = presets.Motion(wl_id(wl), E, R, seed=wl.seed, step_ms=cfg.control_step_ms)
+    pos = mot.current()
+
+    def one():
+        nonlocal pos
+        arr = None
+        if gen is not None:
+            a = gen.step(o.T - o.epoch, None)
+            arr = {k: getattr(a, k) for k in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det")}
+        o.step(pos, arr)
+        pos = mot.advance()
+    for _ in range(warm):
+        one()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    dt = time.perf_counter() - t0
+    return {"value": E * steps / dt, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": f"oracle port (torch CPU, reference op order) on {E} of {wl.E} envs x {R} robots, {steps} "
+                      f"control steps after {warm} warm-up"}
+
+
+def wl_id(wl):
+    return int(wl.name[3])
+
+
+def run_reference(a):
+    """--impl reference: the reference's CPU path (the oracle port) on the host cores, rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(a.workload)
+    cfg = wl.config()
+    steps = max(1, a.steps)
+    res = cpu_baseline(wl, cfg, a.cpu_envs, steps, warm=max(1, min(a.warmup, 2)))
+    v = res["value"]
+    line = {"metric": "env-steps/sec", "value": v, "unit": "env-steps/s", "n_gpus": a.gpus, "steps": steps,
+            "warmup": a.warmup, "ms_per_step": a.cpu_envs / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+            "config": {"workload": wl.name, "envs": a.cpu_envs, "robots": wl.R, "parallelism": "host cores"},
+            "cpu_baseline": res, "e2e": {"value": v, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
+                                          "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
+    ap.add_argument("--workload", type=int, default=2)
+    ap.add_argument("--cpu-envs", type=int, default=256)
+    ap.add_argument("--cpu-steps", type=int, default=5)
+    ap.add_argument("--no-cpu", action="store_true")
+    a = ap.parse_args()
+    if a.impl == "reference":
+        return run_reference(a)
+    a.warmup = max(3, a.warmup)
+    rank, world, dist = dist_setup(a.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    ib = importlib.import_module("isaac-net_b200")
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(a.workload)
+    cfg = wl.config()
+    E, R = wl.E, wl.R
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
+    eng.set_env_offset(rank * E)
+    if rank:
+        eng.reset(None)                       # redraw every env under its global id
+    mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
+    n_all = a.warmup + 2 * a.steps
+    host_pos = torch.empty(n_all, E, R, 2, dtype=torch.float32).pin_memory()
+    host_pos[0] = mot.current()
+    for i in range(1, n_all):
+        host_pos[i] = mot.advance()
+    dev_pos = host_pos[: a.warmup + a.steps].to(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for i in range(a.warmup):
+        eng.step(None, dev_pos[i])
+    clocks = Clocks(dev.index)
+    barrier()
+    clocks.start()
+    ev0.record()
+    for i in range(a.steps):
+        eng._kernel_events = kev[i]
+        eng.step(None, dev_pos[a.warmup + i])
+    ev1.record()
+    barrier()
+    clk = clocks.stop()
+    eng._kernel_events = None
+    t_ms = ev0.elapsed_time(ev1)
+    k_ms = sum(s.elapsed_time(e) for s, e in kev) / a.steps
+    # e2e: poses from pinned host memory each step, observations read back each step
+    obs_keys = ("newest", "queue_len", "queue_bytes", "sinr_db")
+    host_obs = {k: torch.empty(E, R, dtype=torch.int64 if k in ("newest", "queue_len") else torch.float32)
+                .pin_memory() for k in obs_keys}
+    stage = torch.empty(E, R, 2, dtype=torch.float32, device=dev)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(a.steps):
+        stage.copy_(host_pos[a.warmup + a.steps + i], non_blocking=True)
+        out = eng.step(None, stage)
+        for k in obs_keys:
+            host_obs[k].copy_(out[k], non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    h2d = E * R * 2 * 4
+    d2h = sum(host_obs[k].numel() * host_obs[k].element_size() for k in obs_keys)
+    if dist is not None:
+        t = torch.tensor([t_ms, e2e_ms, k_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_ms, e2e_ms, k_ms = t.tolist()
+    total_envs = E * world
+    value = total_envs * a.steps / (t_ms / 1e3)
+    e2e = total_envs * a.steps / (e2e_ms / 1e3)
+    peak, peak_kind = peaks()
+    per_launch = b_env(cfg, R) * E
+    achieved = per_launch / (k_ms / 1e3) / 1e9
+    traffic = None
+    tp = os.path.join(ROOT, "profiles", "nr_step_traffic.json")
+    if os.path.exists(tp):
+        try:
+            tj = json.load(open(tp))
+            traffic = tj.get("bytes_per_launch_scaled", {}).get(wl.name)
+        except Exception:
+            traffic = None
+    line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
+            "config": {"workload": wl.name, "envs_per_gpu": E, "robots": R, "slots_per_step": cfg.slots_per_step,
+                       "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
+                       "parallelism": f"env shards x{world}", "l2": "state > L2 (no flush needed)"},
+            "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": a.steps,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
+            "clocks": clk}
+    if rank == 0 and world == 1 and not a.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(wl, cfg, a.cpu_envs, a.cpu_steps)
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -98,6 +98,7 @@ typedef struct {
   int32_t rows[INB_MAX_ROWS][4];/* schedule: (rel, UL data symbols, SR opportunity, fading update) */
   float rowf[INB_MAX_ROWS][2];  /* per row: rho^dt, sqrt(1 - rho^2) of the AR(1) fading update (float32) */
   int32_t sched;                /* 0 pf, 1 maxci, 2 rr */
+  int32_t thr_mono;             /* thr_ref is non-decreasing: the per-RBG MCS lookup may binary-search */
   int32_t olla_on, phr_cap, retx_priority, comb_cc, harq_drop, purge, fading, rician, radio;  /* flags */
   int32_t sr_delay, ul_rtt, rlc_retx, max_tx, tb_oh, timeout;
   int32_t dmrs, oh, ref_prbs;
@@ -131,6 +132,7 @@ typedef struct {
   const int64_t *last_hid;      /* [E] */
   int64_t *ctr;                 /* [E, INB_NCTR] counters, accumulated */
   int32_t *status;              /* device status word */
+  const int64_t *T_dev;         /* if set, the global control step is read from device memory (CUDA-graph replay) */
   int64_t *trace;               /* optional per-slot trace [K_rows, E, R, 8] (NULL = off): bsr after the SR grant,
                                    need, won RBG mask, new-TB MCS, flags (has_rx | new_el << 1 | tx_rx << 2 |
                                    tx_new << 3 | ok << 4), send pointer after the slot, PHR cap, bits of `left` */

@@ -10,7 +10,8 @@ import ctypes
 import os
 
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
-LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200.so")
+LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
+                        else "libisaac_net_b200.so")
 ABI_VERSION = 1
 MAX_ROWS = 64
 NCTR = 64
@@ -51,7 +52,8 @@ class InbTables(ctypes.Structure):
 class InbParams(ctypes.Structure):
     _fields_ = ([(n, i32) for n in ("E", "R", "S", "P", "F", "M", "MCS", "mcs_max", "C_axis", "G_axis", "nprb", "N",
                                     "K_rows", "Kf")]
-                + [("T", i64), ("rows", (i32 * 4) * MAX_ROWS), ("rowf", (f32 * 2) * MAX_ROWS), ("sched", i32)]
+                + [("T", i64), ("rows", (i32 * 4) * MAX_ROWS), ("rowf", (f32 * 2) * MAX_ROWS), ("sched", i32),
+                   ("thr_mono", i32)]
                 + [(n, i32) for n in ("olla_on", "phr_cap", "retx_priority", "comb_cc", "harq_drop", "purge",
                                       "fading", "rician", "radio")]
                 + [(n, i32) for n in ("sr_delay", "ul_rtt", "rlc_retx", "max_tx", "tb_oh", "timeout")]
@@ -69,7 +71,8 @@ class InbParams(ctypes.Structure):
 class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
-                ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("trace", P)]
+                ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
+                ("trace", P)]
 
 
 class InbResetArgs(ctypes.Structure):

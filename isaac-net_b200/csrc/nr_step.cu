@@ -1,10 +1,11 @@
-// C entry point of the fused NR uplink step: argument checks and dispatch to the kernel variant of the RBG count
-// (nr_step_s13.cu, nr_step_s18.cu, nr_step_s32.cu; the kernel itself is in nr_step.cuh).
+// C entry point of the fused NR uplink step: argument checks and dispatch to the kernel variant of the group width
+// (nr_step_g16.cu ... nr_step_g128.cu; the kernel itself is in nr_step.cuh).
 #include "nr_common.cuh"
 namespace inb {
-cudaError_t launch_step_s13(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_s18(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_s32(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
 }  // namespace inb
 
 extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
@@ -22,12 +23,14 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
     return -5;
   cudaStream_t s = (cudaStream_t)cuda_stream;
   cudaError_t err;
-  if (p.S <= 13)
-    err = inb::launch_step_s13(a, s);
-  else if (p.S <= 18)
-    err = inb::launch_step_s18(a, s);
+  if (p.R <= 16)
+    err = inb::launch_step_g16(a, s);
+  else if (p.R <= 32)
+    err = inb::launch_step_g32(a, s);
+  else if (p.R <= 64)
+    err = inb::launch_step_g64(a, s);
   else
-    err = inb::launch_step_s32(a, s);
+    err = inb::launch_step_g128(a, s);
   return err == cudaSuccess ? 0 : -100 - (int)err;
 }
 

@@ -1,0 +1,6 @@
+// Instantiation of the fused step kernel for groups of 128 lanes (one translation unit per width, compiled in
+// parallel).
+#include "nr_step_launch.cuh"
+namespace inb {
+cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<128>(a, stream); }
+}  // namespace inb

@@ -1,21 +1,21 @@
 #pragma once
+// Launch of the fused step kernel for one group width GW (robots per env rounded up to a power of two).
 #include "nr_step.cuh"
 namespace inb {
-template <int GW, int SM>
-static cudaError_t launch_gw(const InbStepArgs& a, cudaStream_t stream) {
+template <int GW>
+cudaError_t launch_gw(const InbStepArgs& a, cudaStream_t stream) {
+  constexpr int NT = GW > 32 ? GW : 128;
   const int gpb = GW > 32 ? 1 : 128 / GW;
-  dim3 grid((a.p.E + gpb - 1) / gpb), block(GW > 32 ? GW : 128);
-  nr_step_kernel<GW, SM><<<grid, block, 0, stream>>>(a);
+  const int vecs = a.ul_ref_in != nullptr ? 6 : 5;
+  const size_t smem = (size_t)vecs * a.p.S * NT * sizeof(float);
+  static size_t configured = 0;   // dynamic shared memory above 48 KB needs an opt-in, once per size
+  if (smem > 48 * 1024 && smem > configured) {
+    cudaError_t e = cudaFuncSetAttribute(nr_step_kernel<GW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    configured = smem;
+  }
+  dim3 grid((a.p.E + gpb - 1) / gpb), block(NT);
+  nr_step_kernel<GW><<<grid, block, smem, stream>>>(a);
   return cudaGetLastError();
 }
-
-template <int SM>
-static cudaError_t launch_sm(const InbStepArgs& a, cudaStream_t stream) {
-  const int R = a.p.R;
-  if (R <= 16) return launch_gw<16, SM>(a, stream);
-  if (R <= 32) return launch_gw<32, SM>(a, stream);
-  if (R <= 64) return launch_gw<64, SM>(a, stream);
-  return launch_gw<128, SM>(a, stream);
-}
-
 }  // namespace inb

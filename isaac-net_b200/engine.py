@@ -174,6 +174,8 @@ class NRB200Engine:
         p.MCS, p.mcs_max, p.C_axis, p.G_axis = tab.M, tab.mcs_max, tab.C, tab.G
         p.nprb, p.N = cfg.nprb, self.N
         p.sched = {"pf": 0, "maxci": 1, "rr": 2}[cfg.scheduler]
+        thr = tab.thr_ref[: tab.mcs_max + 1].cpu()
+        p.thr_mono = int(bool((thr[1:] >= thr[:-1]).all()))
         p.olla_on, p.phr_cap, p.retx_priority = int(cfg.olla), int(cfg.phr_cap), int(cfg.retx_priority)
         p.comb_cc, p.harq_drop = int(cfg.harq_combining == "cc"), int(cfg.harq_fail == "drop")
         p.purge, p.fading, p.rician = int(cfg.discard == "purge"), int(cfg.fading), int(self.rician)
@@ -536,7 +538,12 @@ class NRB200Engine:
         a.o = o
         tr = getattr(self, "trace_buf", None)
         a.trace = tr.data_ptr() if tr is not None else None
+        ev = getattr(self, "_kernel_events", None)      # optional (start, end) CUDA events around the launch
+        if ev is not None:
+            ev[0].record()
         nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+        if ev is not None:
+            ev[1].record()
         self.prb_avail += float(cfg.nprb) * E * n_ul
         self.T = T + 1
         sinr = out.pop("sinr_db") if snr_out is None else snr_out.clone()
