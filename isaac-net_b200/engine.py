@@ -86,7 +86,7 @@ class NRB200Engine:
     level = "L2"
     backend = "b200"
 
-    def __init__(self, E, R, device, cfg: NRConfig, seed=None):
+    def __init__(self, E, R, device, cfg: NRConfig, seed=None, graphs=True):
         no = cfg.refusals()
         if no:
             raise B200Unsupported("the B200 engine does not implement " + "; ".join(f"{f}: {w}" for f, w in no))
@@ -131,6 +131,14 @@ class NRB200Engine:
         self._fields = None
         self._gnb = torch.tensor(cfg.gnb_xy(), dtype=torch.float32, device=dev).contiguous()
         self._sched = {}
+        # CUDA graphs: one captured step (traffic draws + the fused launch) per schedule key, replayed with the poses
+        # copied into a static buffer and the control step read from device memory
+        self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ()))
+        self._graphs = {}
+        self._pool = None
+        self._T_dev = torch.zeros((), dtype=torch.long, device=dev)
+        self._pos_buf = None
+        self._steps_done = 0
         self._args = nat.InbStepArgs()
         self._fill_static()
         self._kernel_reset(None)
@@ -272,6 +280,7 @@ class NRB200Engine:
     def _make_radio(self):
         self._fields = self._draw_fields()
         self._bind_fields()
+        self._graphs.clear()
 
     def _bind_fields(self):
         k, phi = self._fields
@@ -432,6 +441,7 @@ class NRB200Engine:
             self._sched[key] = ent
         if sched and cfg.fading:
             self.last_g = g0 + sched[-1][0]
+        self._rows_key = key
         return ent
 
     def _out_layout(self, M):
@@ -484,6 +494,11 @@ class NRB200Engine:
         if legacy:
             self._last_hid.copy_(cur_hid.to(self.dev, torch.long))
         E, R, S, a, p = self.E, self.R, self.S, self._args, self._args.p
+        if (self.graphs and self._steps_done > 0 and not legacy and _pathgain is None and _arrivals is None
+                and snr_db is None and x is not None and x.dim() == 3 and self._fields is not None
+                and getattr(self, "trace_buf", None) is None and getattr(self, "_kernel_events", None) is None):
+            return self._graph_step(T, x)
+        self._steps_done += 1
         keep = []                                   # tensors whose pointers the launch reads
         gen = None
         if self.traffic is not None:
@@ -563,6 +578,80 @@ class NRB200Engine:
             res["gen_accepted"] = out["gen_accepted"]
             res["gen_bytes"] = out["gen_bytes"]
         self._keep = keep                           # the launch is asynchronous: keep its inputs alive
+        return res
+
+    # ------------------------------------------------------------------ CUDA-graph step
+    def _capture(self, key, rows, rowf):
+        """Capture one control step (traffic generation + the fused launch) for this schedule key."""
+        a = nat.InbStepArgs.from_buffer_copy(self._args)
+        p = a.p
+        p.K_rows = len(rows)
+        for k, (r4, f2) in enumerate(zip(rows, rowf)):
+            p.rows[k][0], p.rows[k][1], p.rows[k][2], p.rows[k][3] = r4
+            p.rowf[k][0], p.rowf[k][1] = f2
+        p.T, p.s0 = 0, self.s0
+        a.T_dev = self._T_dev.data_ptr()
+        a.pos, a.pathgain_in, a.ul_ref_in, a.trace = self._pos_buf.data_ptr(), None, None, None
+        out, o = self._alloc_outputs()
+        a.o = o
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        if self.traffic is not None:
+            g.register_generator_state(self.traffic.gen)
+        arr = None
+        with torch.cuda.graph(g, pool=self._pool):
+            if self.traffic is not None:
+                arr = self.traffic.step(self._T_dev - self.epoch, None)
+                for n in nat.ARR_FIELDS:
+                    setattr(a.a, n, getattr(arr, n).data_ptr())
+                p.M = arr.valid.shape[-1]
+            else:
+                p.M = 0
+            nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+        ent = {"graph": g, "args": a, "out": out, "arr": arr, "blob": self._blob_of(out)}
+        self._graphs[key] = ent
+        return ent
+
+    def _blob_of(self, out):
+        """The storage behind the output views (one allocation, copied in one piece after a replay)."""
+        return out[self._lay[0][0][0]].untyped_storage()
+
+    def _graph_step(self, T, x):
+        cfg, E, R = self.config, self.E, self.R
+        if self._pos_buf is None:
+            self._pos_buf = torch.empty(E, R, 2, dtype=torch.float32, device=self.dev)
+        rows, rowf, n_ul = self._rows(T * self.N)
+        key = self._rows_key
+        self._pos_buf.copy_(x[..., :2], non_blocking=True)
+        self._T_dev.fill_(T)
+        ent = self._graphs.get(key)
+        if ent is None:
+            ent = self._capture(key, rows, rowf)
+        ent["graph"].replay()
+        self._steps_done += 1
+        self.last_arrivals = ent["arr"]
+        # one copy of the static output block, then views of the copy (the caller owns fresh tensors)
+        spec, total = self._lay
+        src = torch.empty(0, dtype=torch.uint8, device=self.dev).set_(ent["blob"], 0, (total,), (1,))
+        blob = src.clone()
+        out = {n: blob[off:off + nb].view(dt).view(shape) for n, dt, shape, off, nb in spec}
+        self.prb_avail += float(cfg.nprb) * E * n_ul
+        self.T = T + 1
+        sinr = out.pop("sinr_db")
+        self.pathgain = out.pop("pathgain")
+        self._last_snr.copy_(sinr)
+        res = {k: out[k] for k in ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "delay",
+                                   "queue_len", "queue_bytes")}
+        if self._extras:
+            for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
+                res[k] = out[k]
+        res["sinr_db"] = sinr
+        res["serving_cell"] = torch.zeros(E, R, dtype=torch.long, device=self.dev)
+        res["t"] = (T - self.epoch).clone()
+        if self.traffic is not None:
+            res["gen_accepted"] = out["gen_accepted"]
+            res["gen_bytes"] = out["gen_bytes"]
         return res
 
     # ------------------------------------------------------------------ observability
