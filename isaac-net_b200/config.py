@@ -371,8 +371,6 @@ class NRConfig:
             out.append(("blockage=True", "blockage is not built yet"))
         if self.los_source != "stochastic":
             out.append((f"los_source={self.los_source!r}", "geometric LOS sources are not built"))
-        if self.channel == "log_distance" and self.shadow_acf != "exp" and self.shadow_dcorr_m != 10.3:
-            pass
         if self.frame_buffer > 64:
             out.append((f"frame_buffer={self.frame_buffer}", "at most 64 frames per robot"))
         if self.n_harq > 32:
@@ -380,10 +378,6 @@ class NRConfig:
         if self.n_subbands > 32:
             out.append((f"{self.n_subbands} RBGs", "at most 32 RBGs"))
         return out
-
-
-def _f(**kw):
-    return kw
 
 
 __all__ = ["NRConfig", "NRB_FR1", "rbg_size_38214"]
