@@ -10,13 +10,16 @@
  *                      :613-668) + NRNet._finish (nr_engine.py:843-888), MacLink.slot (isaac_net/core/mac.py:228-508),
  *                      UlMac hooks (isaac_net/core/mac_ul.py:66-236), the traffic enqueue and arrival gate of
  *                      NREngine._inject / _open_gate (isaac_net/core/engine.py:505-573) and the step-dict outputs of
- *                      NREngine.step (engine.py:538-631).  It is the seam the Triton backend's launch_step occupies
+ *                      NREngine.step (engine.py:575-594, 918-960).  It is the seam the Triton backend's launch_step occupies
  *                      (isaac_net/core/nr_triton.py:1104-1167, nr_fast.py:702-752).
  *   inb_nr_reset       the device side of NRNet.reset(env_ids) (nr_engine.py:250-320) and MacLink / FrameQueue reset
  *                      (mac.py:176-189, queues.py:399-407): new episode, counter-RNG reset draws (initial fading,
  *                      Rician phase) and the per-robot state back to its initial values, for a mask of envs.
  *   inb_rng_draw       CounterRNG reset draws (isaac_net/core/proto/rng.py:116-161, rng_triton.launch_draw): uniforms
  *                      or Box-Muller normals [E, n] keyed by (seed, env, episode, channel, counter, stream).
+ *   inb_traffic_step   TrafficGen.step (isaac_net/core/traffic.py:408-430) with _Stream._step (traffic.py:301-365) for
+ *                      periodic, video and bursty models: the step's arrivals [E,R,M] from the engine's
+ *                      torch.Generator stream (CUDA Philox), reproduced draw for draw.
  * Status: 0 = launched; negative = invalid arguments (nothing launched).  Kernel-side faults are reported in the
  * int32 device status word `status` (0 = ok), which the host reads only when it asks for it.
  */
@@ -29,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 1
+#define INB_ABI_VERSION 2
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
 #define INB_MAX_F 64      /* frame slots per robot */
@@ -159,6 +162,48 @@ int inb_nr_reset(const InbResetArgs *args, void *cuda_stream);
  * RESET or STEP with the given counters. */
 int inb_rng_draw(int32_t E, int32_t n, uint32_t s0, uint32_t channel, uint32_t stream, const int64_t *env_id,
                  const int64_t *episode, const int64_t *ctr, int32_t normal, float *out, void *cuda_stream);
+
+/* One generating traffic model (TrafficModel of kind periodic, video or bursty) and its per-robot state [E,R]. */
+#define INB_MAX_SRC 8
+typedef struct {
+  int32_t kind;                 /* 0 periodic, 1 video, 2 bursty */
+  int32_t width;                /* arrival columns of this model (max_per_step) */
+  int32_t col;                  /* its first column in the [E,R,M] arrivals */
+  int32_t nb, loops, burst;     /* bursty: bursts per step, event-loop iterations, messages per burst */
+  int32_t gop_n;                /* video: GOP length (0: constant frame size) */
+  int32_t det;                  /* the model's det flag */
+  int64_t tag, prio;
+  double dline;                 /* deadline_ms (inf: none) */
+  double size, gop_i, gop_p;    /* message bytes; video I / P frame bytes */
+  double period, jitter;        /* periodic / video, ms */
+  double on_ms, off_ms, iat;    /* bursty: mean ON / OFF durations, mean inter-burst time, ms */
+  const uint8_t *mask;          /* [R] robots the model runs on */
+  double *nom, *nxt;            /* periodic / video state: nominal and jittered next emission (ms from step start) */
+  int64_t *cnt;                 /*   frames emitted */
+  uint8_t *on;                  /* bursty state: ON period, */
+  double *t_tog, *t_bur;        /*   next ON/OFF toggle, next burst (ms from step start) */
+  int64_t *deferred;            /* scalar: emissions due inside the step that did not fit its columns (accumulated) */
+} InbTrafficSource;
+
+/* Arrivals of one control step for E envs x R robots from the engine's traffic torch.Generator (CUDA Philox
+ * stream of seed `seed`, offset `off0` before the first step): uniform draw d of step n is element (e R + r) of the
+ * float64 torch.rand([E, R]) call at Philox offset off0 + (n ndraws + d) inc, as torch's grid-stride launch of
+ * `stride` threads lays it out. */
+typedef struct {
+  int32_t E, R, M, N, n_src;
+  uint64_t seed, off0;
+  int64_t stride;               /* threads of torch's uniform launch over E*R elements */
+  int64_t inc;                  /* Philox offset advance of one [E,R] draw */
+  int64_t ndraws;               /* [E,R] draws per step, all models */
+  double step_ms, inv_slot_ms;  /* control step; float64 1 / slot duration (torch's CUDA division by a scalar) */
+  int64_t *calls;               /* [E,R] steps generated so far (read, then incremented) */
+  InbTrafficSource src[INB_MAX_SRC];
+  uint8_t *valid, *det;         /* out [E,R,M], sorted by (slot, column); invalid entries last */
+  float *nbytes;
+  int64_t *slot, *tag, *prio;
+  double *dline;
+} InbTrafficArgs;
+int inb_traffic_step(const InbTrafficArgs *args, void *cuda_stream);
 
 /* ABI version of the loaded library (INB_ABI_VERSION). */
 int inb_abi_version(void);

@@ -7,9 +7,32 @@ Public API (a drop-in for ``isaac_net.make_engine("L2", ...)`` on the uplink pat
     make_engine(level, E, R, device, config, backend="b200", *, seed=None) -> NRB200Engine
     NRConfig, TrafficModel, Requests
 """
+import importlib as _importlib
+import importlib.abc as _abc
+import importlib.util as _util
 import sys as _sys
 
-_sys.modules.setdefault("isaac_net_b200", _sys.modules[__name__])
+_ALIAS, _REAL = "isaac_net_b200", __name__
+
+
+class _SubmoduleAlias(_abc.MetaPathFinder, _abc.Loader):
+    """Resolves ``isaac_net_b200.<sub>`` to the one ``isaac-net_b200.<sub>`` module object (never a second copy)."""
+
+    def find_spec(self, name, path=None, target=None):
+        if name.startswith(_ALIAS + ".") and _REAL != _ALIAS:
+            return _util.spec_from_loader(name, self)
+        return None
+
+    def create_module(self, spec):
+        return _importlib.import_module(_REAL + spec.name[len(_ALIAS):])
+
+    def exec_module(self, module):
+        pass
+
+
+_sys.modules.setdefault(_ALIAS, _sys.modules[__name__])
+if not any(isinstance(f, _SubmoduleAlias) for f in _sys.meta_path):
+    _sys.meta_path.insert(0, _SubmoduleAlias())
 
 from .config import NRConfig  # noqa: E402
 from .traffic import Requests, TrafficModel  # noqa: E402

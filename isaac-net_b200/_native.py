@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_ROWS = 64
 NCTR = 64
 CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
@@ -81,7 +81,27 @@ class InbResetArgs(ctypes.Structure):
                 + [(n, P) for n in ("mask", "env_id", "episode", "rng_ctr")] + [("s", InbState)])
 
 
-EXPORTS = ("inb_nr_step", "inb_nr_reset", "inb_rng_draw", "inb_abi_version")
+MAX_SRC = 8
+u64 = ctypes.c_uint64
+
+
+class InbTrafficSource(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("kind", "width", "col", "nb", "loops", "burst", "gop_n", "det")]
+                + [("tag", i64), ("prio", i64)]
+                + [(n, f64) for n in ("dline", "size", "gop_i", "gop_p", "period", "jitter", "on_ms", "off_ms", "iat")]
+                + [(n, P) for n in ("mask", "nom", "nxt", "cnt", "on", "t_tog", "t_bur", "deferred")])
+
+
+TRAFFIC_OUT = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
+
+
+class InbTrafficArgs(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("E", "R", "M", "N", "n_src")] + [("seed", u64), ("off0", u64)]
+                + [(n, i64) for n in ("stride", "inc", "ndraws")] + [("step_ms", f64), ("inv_slot_ms", f64)]
+                + [("calls", P), ("src", InbTrafficSource * MAX_SRC)] + [(n, P) for n in TRAFFIC_OUT])
+
+
+EXPORTS = ("inb_nr_step", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step", "inb_abi_version")
 _lib = None
 
 
@@ -104,6 +124,8 @@ def lib():
     L.inb_nr_reset.argtypes = [ctypes.POINTER(InbResetArgs), P]
     L.inb_rng_draw.restype = ctypes.c_int
     L.inb_rng_draw.argtypes = [i32, i32, u32, u32, u32, P, P, P, i32, P, P]
+    L.inb_traffic_step.restype = ctypes.c_int
+    L.inb_traffic_step.argtypes = [ctypes.POINTER(InbTrafficArgs), P]
     _lib = L
     return L
 
@@ -114,4 +136,4 @@ def check(rc, what):
 
 
 __all__ = ["lib", "check", "InbStepArgs", "InbResetArgs", "InbParams", "InbState", "InbOutputs", "InbArrivals",
-           "InbTables", "EXPORTS", "LIB_PATH"]
+           "InbTables", "InbTrafficArgs", "InbTrafficSource", "EXPORTS", "LIB_PATH"]

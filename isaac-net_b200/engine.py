@@ -24,7 +24,7 @@ import torch
 from . import _native as nat
 from .config import NRConfig
 from .phy import PhyTables
-from .traffic import Requests, TrafficGen, generates
+from .traffic import DeviceTrafficGen, Requests, TrafficGen, generates
 
 # counter-RNG constants (isaac_net/core/proto/rng.py:33-38, nr_rng.py:34, radio.py:53-56)
 M32 = 0xFFFFFFFF
@@ -128,6 +128,9 @@ class NRB200Engine:
             tseed = (int(self.seed) * 6364136223846793005 + 1442695040888963407) % 2 ** 62
             self.traffic = TrafficGen(cfg.traffic, E, R, dev, cfg.control_step_ms, self.N, seed=tseed)
             self._extras = True
+        # the arrivals of periodic / video / bursty models come from one kernel that replays the torch.Generator
+        # stream; event models (host triggers) keep the torch path
+        self.dtraffic = DeviceTrafficGen(self.traffic, self.L) if DeviceTrafficGen.supports(self.traffic) else None
         self._fields = None
         self._gnb = torch.tensor(cfg.gnb_xy(), dtype=torch.float32, device=dev).contiguous()
         self._sched = {}
@@ -502,7 +505,12 @@ class NRB200Engine:
         keep = []                                   # tensors whose pointers the launch reads
         gen = None
         if self.traffic is not None:
-            arr = self.traffic.step(self.clock, triggers) if _arrivals is None else _arrivals
+            if _arrivals is not None:
+                arr = _arrivals
+            elif self.dtraffic is not None:
+                arr = self.dtraffic.step()
+            else:
+                arr = self.traffic.step(self.clock, triggers)
             self.last_arrivals = arr
             M = arr.valid.shape[-1]
             if M > 64:
@@ -597,12 +605,13 @@ class NRB200Engine:
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
-        if self.traffic is not None:
+        if self.traffic is not None and self.dtraffic is None:
             g.register_generator_state(self.traffic.gen)
         arr = None
         with torch.cuda.graph(g, pool=self._pool):
             if self.traffic is not None:
-                arr = self.traffic.step(self._T_dev - self.epoch, None)
+                arr = self.dtraffic.step() if self.dtraffic is not None else self.traffic.step(self._T_dev - self.epoch,
+                                                                                               None)
                 for n in nat.ARR_FIELDS:
                     setattr(a.a, n, getattr(arr, n).data_ptr())
                 p.M = arr.valid.shape[-1]

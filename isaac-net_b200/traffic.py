@@ -178,6 +178,14 @@ class _Source:
         self.deferred = torch.zeros((), dtype=torch.long, device=dev)
         self._gen = gens[0]
 
+    def loops(self):
+        """Iterations of a bursty model's event loop per step (bursts plus two toggles per ON/OFF period)."""
+        md, T = self.m, self.step_ms
+        nb = self.width // md.burst_size
+        on_ms, off_ms = md.on_off[0] * 1000.0, md.on_off[1] * 1000.0
+        loops = nb + 2 * (int(math.ceil(T / max(min(on_ms, off_ms if off_ms > 0 else on_ms), 1e-9))) + 1)
+        return min(loops, nb + 64)
+
     def _u(self):
         return torch.rand(self.E, self.R, generator=self._gen, device=self.dev, dtype=torch.float64)
 
@@ -245,8 +253,7 @@ class _Source:
             nb = W // md.burst_size
             on_ms, off_ms = md.on_off[0] * 1000.0, md.on_off[1] * 1000.0
             iat = 1000.0 / md.rate_hz
-            loops = nb + 2 * (int(math.ceil(T / max(min(on_ms, off_ms if off_ms > 0 else on_ms), 1e-9))) + 1)
-            loops = min(loops, nb + 64)
+            loops = self.loops()
             cnt = torch.zeros(E, R, dtype=torch.long, device=self.dev)
             times = torch.full((E, R, nb), math.inf, dtype=torch.float64, device=self.dev)
             slots = torch.arange(nb, device=self.dev)
@@ -348,4 +355,77 @@ class TrafficGen:
                         g(torch.cat(cols["dl"], -1)), g(torch.cat(cols["det"], -1)))
 
 
-__all__ = ["Requests", "TrafficModel", "TrafficGen", "Arrivals", "normalize_traffic", "generates"]
+class DeviceTrafficGen:
+    """TrafficGen.step as one kernel (inb_traffic_step) for periodic, video and bursty models.
+
+    The kernel reproduces the torch.Generator stream TrafficGen.step would consume: it owns the step generator's
+    position from construction on (a per-robot step counter on the device, so captured CUDA graphs replay
+    correctly) and leaves the torch generator object untouched; resets keep running TrafficGen.reset on the reset
+    generator.  The model state buffers are TrafficGen's own (updated in place by both)."""
+
+    KINDS = {"periodic": 0, "video": 1, "bursty": 2}
+
+    @classmethod
+    def supports(cls, tg):
+        from . import _native as nat
+        return (tg is not None and 0 < len(tg.sources) <= nat.MAX_SRC and 0 < tg.M <= 64
+                and all(s.m.kind in cls.KINDS for s in tg.sources) and tg.dev.type == "cuda")
+
+    def __init__(self, tg, lib):
+        from . import _native as nat
+        self.nat, self.L, self.tg = nat, lib, tg
+        E, R, M, d = tg.E, tg.R, tg.M, tg.dev
+        numel = E * R
+        props = torch.cuda.get_device_properties(d)
+        # torch's launch for a float64 uniform fill of numel elements (ATen DistributionTemplates.h): 256-thread
+        # blocks, at most (threads per SM / 256) blocks per SM, two doubles per curand_uniform2_double call
+        blocks = min((numel + 255) // 256, props.multi_processor_count * (props.max_threads_per_multi_processor // 256))
+        stride = 256 * blocks
+        a = nat.InbTrafficArgs()
+        a.E, a.R, a.M, a.N, a.n_src = E, R, M, tg.N, len(tg.sources)
+        a.seed, a.off0 = tg.gen.initial_seed(), tg.gen.get_offset()
+        a.stride, a.inc = stride, ((numel - 1) // (stride * 2) + 1) * 4
+        a.step_ms, a.inv_slot_ms = tg.step_ms, 1.0 / tg.slot_ms
+        self._keep = []
+        col, nd = 0, 0
+        for k, s in enumerate(tg.sources):
+            m, c = s.m, a.src[k]
+            c.kind, c.width, c.col = self.KINDS[m.kind], s.width, col
+            c.det, c.tag, c.prio, c.dline, c.size = int(m.det), int(s.tag), int(m.priority), float(m.deadline_ms), \
+                float(m.size_bytes)
+            mask = s.mask[0].to(torch.uint8).contiguous()
+            self._keep.append(mask)
+            c.mask, c.deferred = mask.data_ptr(), s.deferred.data_ptr()
+            if m.kind in ("periodic", "video"):
+                c.period, c.jitter = m.period_ms, m.jitter_ms
+                if m.kind == "video" and m.gop is not None:
+                    c.gop_i, c.gop_p, c.gop_n = float(m.gop[0]), float(m.gop[1]), int(m.gop[2])
+                c.nom, c.nxt, c.cnt = s.nom.data_ptr(), s.nxt.data_ptr(), s.cnt.data_ptr()
+                nd += s.width
+            else:
+                c.nb, c.burst, c.loops = s.width // m.burst_size, m.burst_size, s.loops()
+                c.on_ms, c.off_ms, c.iat = m.on_off[0] * 1000.0, m.on_off[1] * 1000.0, 1000.0 / m.rate_hz
+                assert s.on.dtype == torch.bool and s.on.element_size() == 1
+                c.on, c.t_tog, c.t_bur = s.on.data_ptr(), s.t_tog.data_ptr(), s.t_bur.data_ptr()
+                nd += c.loops * (4 if c.off_ms > 0 else 3)
+            col += s.width
+        a.ndraws = nd
+        self.calls = torch.zeros(E, R, dtype=torch.long, device=d)
+        a.calls = self.calls.data_ptr()
+        z = lambda dt: torch.zeros(E, R, M, dtype=dt, device=d)
+        self.out = Arrivals(valid=z(torch.bool), nbytes=z(torch.float32), slot=z(torch.long), tag=z(torch.long),
+                            prio=z(torch.long), dline=z(torch.float64), det=z(torch.bool))
+        for n in nat.TRAFFIC_OUT:
+            setattr(a, n, getattr(self.out, n).data_ptr())
+        self.args = a
+
+    def step(self):
+        """Arrivals of the next step, written into the same [E,R,M] buffers every step (views returned)."""
+        import ctypes
+        st = torch.cuda.current_stream(self.tg.dev).cuda_stream
+        self.nat.check(self.L.inb_traffic_step(ctypes.byref(self.args), ctypes.c_void_p(st)), "inb_traffic_step")
+        return self.out
+
+
+__all__ = ["Requests", "TrafficModel", "TrafficGen", "DeviceTrafficGen", "Arrivals", "normalize_traffic",
+           "generates"]

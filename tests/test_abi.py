@@ -31,7 +31,8 @@ def test_library_loads_and_exports_every_symbol():
 
 STRUCTS = {"InbState": nat.InbState, "InbOutputs": nat.InbOutputs, "InbArrivals": nat.InbArrivals,
            "InbTables": nat.InbTables, "InbParams": nat.InbParams, "InbStepArgs": nat.InbStepArgs,
-           "InbResetArgs": nat.InbResetArgs}
+           "InbResetArgs": nat.InbResetArgs, "InbTrafficSource": nat.InbTrafficSource,
+           "InbTrafficArgs": nat.InbTrafficArgs}
 
 
 def _c_layout(tmp_path):
