@@ -139,9 +139,12 @@ typedef struct {
   int64_t *trace;               /* optional per-slot trace [K_rows, E, R, 8] (NULL = off): bsr after the SR grant,
                                    need, won RBG mask, new-TB MCS, flags (has_rx | new_el << 1 | tx_rx << 2 |
                                    tx_new << 3 | ok << 4), send pointer after the slot, PHR cap, bits of `left` */
+  float *gain;                  /* scratch [n_ul + 1, E*R, S] float32 (n_ul = UL rows of the step): row 0 = the CSI
+                                   before the step, row u + 1 = the fading gain (dB) of the u-th UL row */
+  int64_t gain_cap;             /* elements available at `gain` */
 } InbStepArgs;
 
-/* One control step of the NR uplink engine. */
+/* One control step of the NR uplink engine: the fading launch, then the MAC launch, on `cuda_stream`. */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 
 /* Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial

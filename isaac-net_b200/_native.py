@@ -72,7 +72,7 @@ class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
                 ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
-                ("trace", P)]
+                ("trace", P), ("gain", P), ("gain_cap", i64)]
 
 
 class InbResetArgs(ctypes.Structure):

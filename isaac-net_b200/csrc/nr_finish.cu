@@ -1,0 +1,244 @@
+// End of a control step (NRNet._finish, isaac_net/core/nr_engine.py:843-888; MacLink.end_step / compact, mac.py:585-616;
+// FrameQueue.remove / floor, queues.py:105-143; the step-dict outputs of NREngine.step, engine.py:575-594, 918-960),
+// after the slot loop of the MAC kernel.
+//
+// One block per env; each robot is served by FW lanes with one frame per lane (two when F > FW), so every load and
+// store of the [E,R,F] frame arrays is coalesced.  Per frame: delivered / timed-out / dropped masks and the frame
+// outputs.  Per robot (segmented shuffles): the in-order pointer, the newest delivered capture, the FIFO compaction
+// (kept frames first in order, then the freed slots in index order, each lane fetching its source frame from the
+// owning lane's registers), the stream floor, the send pointer, HARQ processes that only hold purged bytes, BSR and the
+// queue outputs.  Per env: det_env.
+#include <cmath>
+#include <cstdint>
+
+#include "nr_common.cuh"
+
+namespace inb {
+
+template <int FW>
+struct Seg {  // the FW lanes of one robot inside a warp
+  static __device__ __forceinline__ unsigned mask_bits(bool v) {
+    const unsigned b = __ballot_sync(0xFFFFFFFFu, v);
+    if constexpr (FW == 32) {
+      return b;
+    } else {
+      return (b >> ((threadIdx.x & 31) / FW * FW)) & ((1u << FW) - 1u);
+    }
+  }
+  static __device__ __forceinline__ long long min_ll(long long x) {
+#pragma unroll
+    for (int o = FW / 2; o > 0; o >>= 1) {
+      const long long y = __shfl_xor_sync(0xFFFFFFFFu, x, o, FW);
+      x = y < x ? y : x;
+    }
+    return x;
+  }
+  static __device__ __forceinline__ long long max_ll(long long x) {
+#pragma unroll
+    for (int o = FW / 2; o > 0; o >>= 1) {
+      const long long y = __shfl_xor_sync(0xFFFFFFFFu, x, o, FW);
+      x = y > x ? y : x;
+    }
+    return x;
+  }
+  template <typename V>
+  static __device__ __forceinline__ V from(V v, int src_lane) {   // lane index within the segment
+    return __shfl_sync(0xFFFFFFFFu, v, src_lane, FW);
+  }
+};
+
+// index of the n-th set bit (0-based; n < popcount(m)) of a 64-bit mask, by halving with population counts
+__device__ __forceinline__ int nth_set64(unsigned long long m, int n) {
+  unsigned w = (unsigned)m;
+  int pos = 0;
+  const int c32 = __popc(w);
+  if (n >= c32) { n -= c32; w = (unsigned)(m >> 32); pos = 32; }
+  const int c16 = __popc(w & 0xFFFFu);
+  if (n >= c16) { n -= c16; w >>= 16; pos += 16; }
+  const int c8 = __popc(w & 0xFFu);
+  if (n >= c8) { n -= c8; w >>= 8; pos += 8; }
+  const int c4 = __popc(w & 0xFu);
+  if (n >= c4) { n -= c4; w >>= 4; pos += 4; }
+  const int c2 = __popc(w & 0x3u);
+  if (n >= c2) { n -= c2; w >>= 2; pos += 2; }
+  if (n >= (int)(w & 1u)) pos += 1;
+  return pos;
+}
+
+template <int FW, int FPL>                     // lanes per robot, frames per lane (F <= FW * FPL)
+__global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) {
+  const InbParams& p = A.p;
+  const InbState& st = A.s;
+  const InbOutputs& o = A.o;
+  const int R = p.R, F = p.F, P = p.P;
+  const long long e = blockIdx.x;
+  const int seg = threadIdx.x / FW, l = threadIdx.x % FW;
+  const int segs = blockDim.x / FW;
+  const long long T = (A.T_dev != nullptr) ? *A.T_dev : p.T;
+  const long long epoch = A.epoch[e], last_hid = A.last_hid[e];
+  const double lim = da((double)(T + 1), 1e-9);
+  bool det_hit = false;
+  const int passes = (R + segs - 1) / segs;
+  for (int ps = 0; ps < passes; ++ps) {        // same trip count in every lane of the block
+    const int r = ps * segs + seg;
+    const bool act = r < R;
+    const long long er = act ? e * R + r : 0;
+    const long long eP = er * P, eF = er * F;
+    long long sent = 0, floor_ = 0, enq = 0, bsr = 0;
+    if (act) {
+      sent = st.sent[er]; floor_ = st.floor_[er]; enq = st.enq[er]; bsr = st.bsr[er];
+    }
+    // ---- HARQ processes: lane q holds process q (P <= FW)
+    const bool hq = act && l < P;
+    long long h_hi = 0, h_lo = 0;
+    bool pend = false;
+    if (hq) {
+      pend = st.h_state[eP + l] == 1;
+      h_hi = st.h_hi[eP + l];
+      h_lo = st.h_lo[eP + l];
+    }
+    // in-order pointer (MacLink.ack_ptr, mac.py:194-197)
+    auto ack_of = [&](bool pd, long long fl, long long sn) {
+      long long v = (pd && h_hi > fl) ? (h_lo > fl ? h_lo : fl) : sn;
+      v = Seg<FW>::min_ll(v);
+      return v < sn ? v : sn;
+    };
+    const long long ack_end = ack_of(pend, floor_, sent);
+    // ---- frames: lane l holds frames l and l + FW
+    long long cap[FPL], start[FPL], end_[FPL], cls[FPL], hid[FPL], tag[FPL], prio[FPL];
+    double fin[FPL], off[FPL], dline[FPL];
+    uint8_t lost[FPL], det[FPL];
+    unsigned long long gone = 0ull;
+    long long newest = -1;
+#pragma unroll
+    for (int j = 0; j < FPL; ++j) {
+      const int f = l + j * FW;
+      const bool fv = act && f < F;
+      const long long at = eF + f;
+      cap[j] = fv ? st.cap[at] : -1;
+      start[j] = fv ? st.start[at] : 0;
+      end_[j] = fv ? st.end_[at] : 0;
+      cls[j] = fv ? st.cls[at] : 0;
+      hid[j] = fv ? st.hid[at] : 0;
+      tag[j] = fv ? st.tag[at] : 0;
+      prio[j] = fv ? st.prio[at] : 0;
+      lost[j] = fv ? st.lost[at] : 0;
+      det[j] = fv ? st.det[at] : 0;
+      fin[j] = fv ? st.fin[at] : INFINITY;
+      off[j] = fv ? st.off[at] : 0.0;
+      dline[j] = fv ? st.dline[at] : INFINITY;
+      const bool valid = cap[j] >= 0;
+      const bool delivered = valid && fin[j] <= lim;
+      const bool timed = p.purge && valid && isinf(fin[j]) && ((T + 1 - cap[j]) >= p.timeout);
+      const bool dropped = valid && lost[j] && (end_[j] <= ack_end) && !timed;
+      if (delivered && cap[j] > newest) newest = cap[j];
+      if (delivered && det[j] && hid[j] == last_hid) det_hit = true;
+      if (fv) {
+        o.delivered[at] = delivered;
+        o.timed_out[at] = timed;
+        o.dropped[at] = dropped;
+        o.cap[at] = valid ? cap[j] - epoch : -1;
+        o.cls[at] = valid ? cls[j] : 0;
+        const float delay = (float)dsb(dsb(fin[j], (double)cap[j]), off[j]);
+        o.delay[at] = delivered ? delay : NAN;
+        o.arrival[at] = valid ? da((double)(cap[j] - epoch), off[j]) : NAN;
+        o.arrival_slot[at] = valid ? (long long)rint(dm(off[j], (double)p.N)) : -1;
+        o.tag[at] = valid ? tag[j] : 0;
+        o.priority[at] = valid ? prio[j] : 0;
+        o.bytes[at] = valid ? end_[j] - start[j] : 0;
+        const bool late = delivered && (dm((double)delay, p.ctl_ms) > dline[j]);
+        o.deadline_miss[at] = late || ((timed || dropped) && isfinite(dline[j]));
+      }
+      const bool g_ = !fv || delivered || timed || dropped || !valid;
+      gone |= (unsigned long long)Seg<FW>::mask_bits(g_) << (j * FW);
+    }
+    newest = Seg<FW>::max_ll(newest);
+    // ---- compaction: surviving frames first (stable), then the freed slots in index order (queues.py:105-110)
+    const unsigned long long all = F >= 64 ? ~0ull : ((1ull << F) - 1ull);
+    gone &= all;
+    const unsigned long long keep = ~gone & all;
+    const int n_keep = __popcll(keep);
+    long long floor_new = enq;
+#pragma unroll
+    for (int j = 0; j < FPL; ++j) {
+      const int f = l + j * FW;
+      const int src = f < F ? (f < n_keep ? nth_set64(keep, f) : nth_set64(gone, f - n_keep)) : 0;
+      const int sl = src % FW, sj = src / FW;
+      // every lane takes part in each shuffle; the value comes from register sj of lane sl
+      auto pick64 = [&](const long long* v) {
+        const long long a = Seg<FW>::from(v[0], sl);
+        if constexpr (FPL == 1) return a;
+        const long long b = Seg<FW>::from(v[FPL - 1], sl);
+        return sj == 0 ? a : b;
+      };
+      auto pickd = [&](const double* v) {
+        const double a = Seg<FW>::from(v[0], sl);
+        if constexpr (FPL == 1) return a;
+        const double b = Seg<FW>::from(v[FPL - 1], sl);
+        return sj == 0 ? a : b;
+      };
+      auto pick8 = [&](const uint8_t* v) {
+        const int a = Seg<FW>::from((int)v[0], sl);
+        if constexpr (FPL == 1) return (uint8_t)a;
+        const int b = Seg<FW>::from((int)v[FPL - 1], sl);
+        return (uint8_t)(sj == 0 ? a : b);
+      };
+      const long long c_src = pick64(cap);   // every lane shuffles; the freed slots get cap -1
+      const long long n_cap = ((gone >> src) & 1ull) ? -1 : c_src;
+      const long long n_start = pick64(start), n_end = pick64(end_), n_cls = pick64(cls), n_hid = pick64(hid);
+      const long long n_tag = pick64(tag), n_prio = pick64(prio);
+      const uint8_t n_lost = pick8(lost), n_det = pick8(det);
+      const double n_fin = pickd(fin), n_off = pickd(off), n_dline = pickd(dline);
+      if (j == 0) {
+        const long long s0 = Seg<FW>::from(n_start, 0);
+        if (n_keep > 0) floor_new = s0;
+      }
+      if (act && f < F) {
+        const long long at = eF + f;
+        st.cap[at] = n_cap; st.start[at] = n_start; st.end_[at] = n_end; st.cls[at] = n_cls; st.hid[at] = n_hid;
+        st.tag[at] = n_tag; st.prio[at] = n_prio; st.lost[at] = n_lost; st.det[at] = n_det;
+        st.fin[at] = n_fin; st.off[at] = n_off; st.dline[at] = n_dline;
+      }
+    }
+    // ---- stream floor, send pointer, HARQ processes holding only purged bytes (MacLink.compact, mac.py:598-616)
+    floor_ = floor_new;
+    sent = sent > floor_ ? sent : floor_;
+    if (hq && pend && h_hi <= floor_ && h_hi > h_lo) {
+      st.h_state[eP + l] = 0; st.h_ready[eP + l] = 0; st.h_ntx[eP + l] = 0; st.h_comb[eP + l] = 0.0f;
+      pend = false;
+    }
+    bsr = bsr < enq - sent ? bsr : enq - sent;
+    const long long qb = enq - ack_of(pend, floor_, sent);
+    if (act && l == 0) {
+      o.newest[er] = newest >= 0 ? newest - epoch : -1;
+      o.queue_len[er] = n_keep;
+      o.queue_bytes[er] = (float)(qb > 0 ? qb : 0);
+      st.sent[er] = sent;
+      st.floor_[er] = floor_;
+      st.bsr[er] = bsr;
+    }
+  }
+  const int any = __syncthreads_or(det_hit ? 1 : 0);
+  if (threadIdx.x == 0) o.det_env[e] = any ? 1 : 0;
+}
+
+cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream) {
+  const InbParams& p = a.p;
+  const int FW = (p.P > 16 || p.F > 32) ? 32 : 16;   // lanes per robot: P <= FW, F <= 2 FW
+  const int FPL = p.F > FW ? 2 : 1;
+  int rp = 1;
+  while (rp < p.R) rp <<= 1;
+  int threads = rp * FW;
+  threads = threads < 32 ? 32 : (threads > 512 ? 512 : threads);
+  if (FW == 16 && FPL == 1)
+    nr_finish_kernel<16, 1><<<p.E, threads, 0, stream>>>(a);
+  else if (FW == 16)
+    nr_finish_kernel<16, 2><<<p.E, threads, 0, stream>>>(a);
+  else if (FPL == 1)
+    nr_finish_kernel<32, 1><<<p.E, threads, 0, stream>>>(a);
+  else
+    nr_finish_kernel<32, 2><<<p.E, threads, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
+}  // namespace inb

@@ -1,11 +1,14 @@
-// C entry point of the fused NR uplink step: argument checks and dispatch to the kernel variant of the group width
-// (nr_step_g16.cu ... nr_step_g128.cu; the kernel itself is in nr_step.cuh).
+// C entry point of the NR uplink step: argument checks, then three launches on the caller's stream: the fading
+// (nr_fading.cu), the MAC kernel variant of the group width (nr_step_g16.cu ... nr_step_g128.cu; the kernel is in
+// nr_step.cuh) and the end-of-step finish (nr_finish.cu).
 #include "nr_common.cuh"
 namespace inb {
 cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
 }  // namespace inb
 
 extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
@@ -21,8 +24,12 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
   if (a.pos == nullptr && a.pathgain_in == nullptr) return -4;
   if (a.pos != nullptr && a.pathgain_in == nullptr && (a.t.fk == nullptr || a.t.fphi == nullptr || a.t.gnb == nullptr))
     return -5;
+  int n_ul = 0;
+  for (int k = 0; k < p.K_rows; ++k) n_ul += p.rows[k][1] > 0 ? 1 : 0;
+  if (a.gain == nullptr || a.gain_cap < (long long)(n_ul + 1) * p.S * p.E * p.R) return -6;
   cudaStream_t s = (cudaStream_t)cuda_stream;
-  cudaError_t err;
+  cudaError_t err = inb::launch_fading(a, s);
+  if (err != cudaSuccess) return -100 - (int)err;
   if (p.R <= 16)
     err = inb::launch_step_g16(a, s);
   else if (p.R <= 32)
@@ -31,6 +38,7 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
     err = inb::launch_step_g64(a, s);
   else
     err = inb::launch_step_g128(a, s);
+  if (err == cudaSuccess) err = inb::launch_finish(a, s);
   return err == cudaSuccess ? 0 : -100 - (int)err;
 }
 

@@ -10,9 +10,12 @@
 // schedule of a control step is the same for every env.  A branch that holds a collective is taken on a warp-uniform
 // condition, so full-mask shuffles are always reached by all 32 lanes at the same call site.
 //
-// Per-robot per-RBG vectors (fading state, CSI / gain, rate, link-adaptation SINR) live in shared memory, laid out
-// [vector][RBG][thread] so a warp touches 32 consecutive words (no bank conflicts); the RBG loops are not unrolled,
-// which keeps the kernel small enough for the instruction cache and its register count low.
+// The AR(1) fading of the step runs before this kernel (nr_fading.cu): the CSI and the fading gain of the u-th UL
+// row are rows u and u + 1 of the gain buffer [n_ul + 1][E R][S].  Per-RBG work (rates, link adaptation, the decode
+// SINR) is only needed for the few robots that want or use RBGs in a slot, so a warp serves those robots one at a
+// time with a lane per RBG (or per MCS); their per-RBG vectors (rate, PF metric, link-adaptation SINR, the optional
+// per-RBG SNR input) live in shared memory, laid out [vector][RBG][thread] with an odd row stride, so a warp reading
+// a row or a column is conflict-free.  Counters accumulate in shared memory, one block of words per env.
 //
 // Semantics follow isaac-net v0.2.0 (file:line in the comments); reductions over the RBG axis are left-to-right sums
 // (the oracle's "seq" mode), ties in every argmax resolve to the lowest robot / process index (torch.max / argmin),
@@ -66,6 +69,17 @@ struct Grp {
     }
   }
   __device__ static bool any(bool v, SmemGroup* sm, int& par) { return max_u64(v ? 1ull : 0ull, sm, par) != 0ull; }
+  // true on every lane of the warp (GW <= 32) or block (GW > 32) when some group there has two or more lanes with v
+  __device__ static bool two_or_more_uniform(bool v) {
+    if constexpr (GW > 32) {
+      return __syncthreads_count(v) >= 2;
+    } else {
+      const unsigned b = __ballot_sync(0xFFFFFFFFu, v);
+      const int lane = threadIdx.x & 31;
+      const unsigned gm = GW == 32 ? 0xFFFFFFFFu : (((1u << GW) - 1u) << (lane / GW * GW));
+      return __ballot_sync(0xFFFFFFFFu, __popc(b & gm) >= 2) != 0u;
+    }
+  }
   // condition of a branch that contains collectives: uniform over the whole warp (GW < 32 packs several envs in a
   // warp, and full-mask shuffles must be reached by every lane of the warp at the same call site)
   __device__ static bool any_uniform(bool v, SmemGroup* sm, int& par) {
@@ -76,6 +90,17 @@ struct Grp {
     }
   }
 };
+
+// Out-of-line calls of CUDA's math functions: each appears once in the kernel instead of at every call site, which
+// keeps the (long, branchy) kernel within the instruction cache.  The results are the functions' own.
+static __device__ __noinline__ float x_powf(float a, float b) { return powf(a, b); }
+static __device__ __noinline__ float x_log10f(float a) { return log10f(a); }
+static __device__ __noinline__ float x_logf(float a) { return logf(a); }
+static __device__ __noinline__ float x_expf(float a) { return expf(a); }
+static __device__ __noinline__ float x_cosf(float a) { return cosf(a); }
+static __device__ __noinline__ float x_sqrtf(float a) { return sqrtf(a); }
+static __device__ __noinline__ float x_fdv(float a, float b) { return fdv(a, b); }      // IEEE a / b
+static __device__ __noinline__ double x_ddv(double a, double b) { return ddv(a, b); }  // IEEE a / b
 
 // ------------------------------------------------------------------------------------------------ PHY helpers
 // PHY.bler_lookup (isaac_net/core/phy.py:271-285), CUDA torch semantics: division by a python scalar is a multiply
@@ -135,16 +160,16 @@ __device__ __forceinline__ void segment(long long tbs, float r32, float& cbs, fl
   bool bg2 = (t <= 292.0) || ((t <= 3824.0) && (r <= 0.67)) || (r <= 0.25);
   double kcb = bg2 ? 3840.0 : 8448.0;
   double b = da(t, t > 3824.0 ? 24.0 : 16.0);
-  double c = (b <= kcb) ? 1.0 : ceil(ddv(b, dsb(kcb, 24.0)));
+  double c = (b <= kcb) ? 1.0 : ceil(x_ddv(b, dsb(kcb, 24.0)));
   double bp = (c > 1.0) ? da(b, dm(24.0, c)) : b;
-  cbs = (float)ddv(bp, c);
+  cbs = (float)x_ddv(bp, c);
   ncb = (float)c;
 }
 
 // linear -> dB with the reference's NaN / inf mapping (phy.py:137-139)
 __device__ __forceinline__ float db_of(float lin) {
   if (isnan(lin)) return -30.0f;
-  float v = fm(10.0f, log10f(fmaxf(lin, 1e-6f)));
+  float v = fm(10.0f, x_log10f(fmaxf(lin, 1e-6f)));
   if (isnan(v)) return -30.0f;
   if (isinf(v)) return v > 0.0f ? 60.0f : -30.0f;
   return v;
@@ -152,47 +177,55 @@ __device__ __forceinline__ float db_of(float lin) {
 
 // EESM effective SINR (dB) of one MCS over the won RBGs (PHY.eff_sinr / eff_sinr_all, phy.py:311-336):
 // x_s = -lin_s / beta + log(w_s) on won RBGs (-inf elsewhere), logsumexp as max + left-to-right sum of exp(x - max),
-// eff = -beta (lse - lnw).  negl[s * NT] = -lin_s.
-static __device__ __noinline__ float eesm_db(const float* negl, int NT, const float* __restrict__ lw, uint32_t won, int S,
+// eff = -beta (lse - lnw).  negl[s * ld] = -lin_s.
+static __device__ __noinline__ float eesm_db(const float* negl, int ld, const float* __restrict__ lw, uint32_t won, int S,
                                       float beta, float lnw) {
   float mx = -INFINITY;
+#pragma unroll 1
   for (int s = 0; s < S; ++s)
-    if ((won >> s) & 1u) mx = fmaxf(mx, fa(fdv(negl[s * NT], beta), lw[s]));
+    if ((won >> s) & 1u) mx = fmaxf(mx, fa(x_fdv(negl[s * ld], beta), lw[s]));
   const float m0 = isinf(mx) ? 0.0f : mx;
   float sum = 0.0f;
+#pragma unroll 1
   for (int s = 0; s < S; ++s) {
-    float e = ((won >> s) & 1u) ? expf(fs(fa(fdv(negl[s * NT], beta), lw[s]), m0)) : 0.0f;
+    float e = ((won >> s) & 1u) ? x_expf(fs(fa(x_fdv(negl[s * ld], beta), lw[s]), m0)) : 0.0f;
     sum = s == 0 ? e : fa(sum, e);
   }
-  const float lse = fa(logf(sum), m0);
+  const float lse = fa(x_logf(sum), m0);
   return db_of(fm(-beta, fs(lse, lnw)));
 }
 
-// logsumexp of log(w) over the won RBGs (the EESM normalization)
-__device__ __forceinline__ float lnw_of(const float* __restrict__ lw, uint32_t won, int S) {
-  float mx = -INFINITY;
-  for (int s = 0; s < S; ++s)
-    if ((won >> s) & 1u) mx = fmaxf(mx, lw[s]);
-  const float m0 = isinf(mx) ? 0.0f : mx;
-  float sum = 0.0f;
-  for (int s = 0; s < S; ++s) {
-    float e = ((won >> s) & 1u) ? expf(fs(lw[s], m0)) : 0.0f;
-    sum = s == 0 ? e : fa(sum, e);
+// warp-wide max (fmaxf: order-independent) and the sum of lane values over the set bits of `won` in ascending lane
+// order (the left-to-right RBG sum of the serial code; lanes outside `won` would add +0.0, which changes nothing)
+__device__ __forceinline__ float warp_max(float x) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
+  return x;
+}
+__device__ __forceinline__ float ordered_sum(float e, uint32_t won) {
+  float acc = 0.0f;
+  bool first = true;
+  for (uint32_t m = won; m; m &= m - 1u) {
+    const float v = __shfl_sync(0xFFFFFFFFu, e, __ffs(m) - 1);
+    acc = first ? v : fa(acc, v);
+    first = false;
   }
-  return fa(logf(sum), m0);
+  return acc;
 }
 
-// the in-order pointer: lowest byte still owned by an undecoded process, or `sent` (MacLink.ack_ptr, mac.py:194-197)
-__device__ __forceinline__ long long ack_ptr(const InbState& st, long long eP, int P, long long sent, long long floor_) {
+// the in-order pointer: lowest byte still owned by an undecoded process, or `sent` (MacLink.ack_ptr, mac.py:194-197);
+// pend = bit mask of the processes in state 1
+__device__ __forceinline__ long long ack_ptr(const InbState& st, long long eP, uint32_t pend, long long sent,
+                                             long long floor_) {
   long long ack = sent;
-  for (int q = 0; q < P; ++q) {
-    if (st.h_state[eP + q] == 1) {
-      const long long hh = st.h_hi[eP + q];
-      if (hh > floor_) {
-        long long ll = st.h_lo[eP + q];
-        ll = ll > floor_ ? ll : floor_;
-        ack = ll < ack ? ll : ack;
-      }
+  while (pend) {
+    const int q = __ffs(pend) - 1;
+    pend &= pend - 1u;
+    const long long hh = st.h_hi[eP + q];
+    if (hh > floor_) {
+      long long ll = st.h_lo[eP + q];
+      ll = ll > floor_ ? ll : floor_;
+      ack = ll < ack ? ll : ack;
     }
   }
   return ack;
@@ -218,13 +251,16 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 
 // ------------------------------------------------------------------------------------------------ the step kernel
 template <int GW>
-__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr_step_kernel(const InbStepArgs A) {
+__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 768 / GW : 6) nr_step_kernel(const InbStepArgs A) {
   constexpr int NT = GW > 32 ? GW : 128;
+  constexpr int NP = NT + 1;   // row stride of the shared vectors: a warp reading one column across rows is
+                               // conflict-free as well as a warp reading one row
   const InbParams& p = A.p;
   __shared__ SmemGroup smem_all[GW > 32 ? 1 : 128 / GW];
   __shared__ float s_lw[INB_MAX_S], s_lw10[INB_MAX_S], s_w[INB_MAX_S];
   __shared__ float s_thr[INB_MAX_MCS], s_se[INB_MAX_MCS], s_beta[INB_MAX_MCS], s_rate[INB_MAX_MCS];
-  extern __shared__ float dyn[];   // [5 or 6][S][NT]: hr, hi, csi/gain ping-pong (2), rate / -lin, ref (optional)
+  __shared__ unsigned long long s_ctr[GW > 32 ? 1 : 128 / GW][INB_NCTR];
+  extern __shared__ float dyn[];   // [2 or 3][S][NP]: rate / -lin, PF metric, ref (optional)
   const int tid = threadIdx.x;
   const int gpb = GW > 32 ? 1 : 128 / GW;
   const int gi = GW > 32 ? 0 : tid / GW;
@@ -246,12 +282,16 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     s_beta[i] = A.t.beta[i];
     s_rate[i] = A.t.rate[i];
   }
-  float* v_hr = dyn + tid;
-  float* v_hi = dyn + (size_t)S * NT + tid;
-  float* v_cg0 = dyn + (size_t)2 * S * NT + tid;
-  float* v_cg1 = dyn + (size_t)3 * S * NT + tid;
-  float* v_x = dyn + (size_t)4 * S * NT + tid;
-  float* v_ref = dyn + (size_t)5 * S * NT + tid;
+  float* const d_x = dyn;                            // rate (bytes per RBG), later -SINR_lin of the grant
+  float* const d_m = dyn + (size_t)S * NP;           // PF metric rate / max(avg, 1e-9)
+  float* const d_ref = dyn + (size_t)2 * S * NP;     // per-RBG reference SINR input
+  float* v_x = d_x + tid;
+  float* v_m = d_m + tid;
+  float* v_ref = d_ref + tid;
+  unsigned long long* const sc = s_ctr[gi];
+  for (int i = r; i < INB_NCTR; i += GW) sc[i] = 0ull;
+  const int lane = tid & 31;
+  const int wbase = tid - lane;                      // thread index of lane 0 of this warp
   const bool ref_vec = A.ul_ref_in != nullptr;
   __syncthreads();
 
@@ -261,7 +301,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
   const long long T = (A.T_dev != nullptr) ? *A.T_dev : p.T;
 #ifdef INB_CHECK
   const long long NER = (long long)p.E * R, NERF = NER * F, NERP = NER * P, NERS = NER * S, NERM = NER * p.M;
-  const long long NFK = (long long)p.E * p.Kf, NLA = (long long)(p.nprb + 1) * p.MCS;
+  const long long NFK = (long long)p.E * p.Kf, NLA = (long long)(p.nprb + 1) * p.MCS, GCAP = A.gain_cap;
 #define CK(i, n, code) ck((i), (n), (code), A.status)
 #else
 #define CK(i, n, code) (i)
@@ -274,7 +314,15 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     sent = st.sent[CK(er, NER, 1)]; floor_ = st.floor_[CK(er, NER, 1)]; bsr = st.bsr[CK(er, NER, 1)]; sr_t = st.sr_t[CK(er, NER, 1)]; last_tx = st.last_tx[CK(er, NER, 1)];
     enq = st.enq[CK(er, NER, 1)]; olla = st.olla[CK(er, NER, 1)]; avg = st.avg[CK(er, NER, 1)];
   }
-  const long long epoch = env_ok ? A.epoch[CK(e, p.E, 10)] : 0;
+  // HARQ process states as bit masks (state 1: holds a TB awaiting its retransmission or ACK; state 0: free)
+  uint32_t pend = 0u, freem = 0u;
+  if (act) {
+    for (int q = 0; q < P; ++q) {
+      const long long hs = st.h_state[CK(eP + q, NERP, 4)];
+      if (hs == 1) pend |= 1u << q;
+      else if (hs == 0) freem |= 1u << q;
+    }
+  }
   const long long last_hid = env_ok ? A.last_hid[CK(e, p.E, 10)] : 0;
 
   // ---------------- traffic enqueue (NREngine._inject / _enqueue, engine.py:191-244; FrameQueue.add, queues.py:87-103)
@@ -325,27 +373,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     } else if (A.pos != nullptr) {
       const float px = A.pos[CK(er * 2, NER * 2, 2)], py = A.pos[CK(er * 2 + 1, NER * 2, 2)];
       const float dx = fs(px, A.t.gnb[0]), dy = fs(py, A.t.gnb[1]);
-      const float d2 = fmaxf(sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
+      const float d2 = fmaxf(x_sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
       // shadowing: amp * sum_k cos(k . x + phi) (channels/fields.py:61-64), the field of (env, cell 0)
       float cs = 0.0f;
       for (int k = 0; k < p.Kf; ++k) {
         const long long fo = e * p.Kf + k;
         const float arg = fa(fa(fm(px, A.t.fk[CK(fo * 2, NFK * 2, 8)]), fm(py, A.t.fk[CK(fo * 2 + 1, NFK * 2, 8)])), A.t.fphi[CK(fo, NFK, 8)]);
-        const float c = cosf(arg);
+        const float c = x_cosf(arg);
         cs = k == 0 ? c : fa(cs, c);
       }
       const float field = fm(p.amp, cs);
       if (p.radio_model <= 1) {
         // TR 38.901 UMi / UMa LOS path loss (channels/tr38901.py:148-170) + sigma_SF * unit field
-        const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
-        const float lg = log10f(d3);
+        const float d3 = x_sqrtf(fa(fm(d2, d2), p.hh2));
+        const float lg = x_log10f(d3);
         const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
                                        : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
         const float rx = fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
         pg = fs(rx, p.ue_tx);
       } else {
         // log-distance (radio.py:265-273)
-        const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
+        const float pl = fa(p.pl_const, fm(p.pl_10n, x_log10f(d2)));
         pg = fs(fs(fs(p.ue_tx, pl), field), p.ue_tx);
       }
     }
@@ -354,34 +402,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
   const float ref_pg = fs(fa(p.ul_ref0, pg), p.noise_prb);
   const float sinr_obs = fs(fa(pg, p.ue_tx), p.sub_noise);
   if (ref_vec) {
-    for (int s = 0; s < S; ++s) v_ref[s * NT] = act ? A.ul_ref_in[CK(eS + s, NERS, 5)] : 0.0f;
+    for (int s = 0; s < S; ++s) v_ref[s * NP] = act ? A.ul_ref_in[CK(eS + s, NERS, 5)] : 0.0f;
   }
-#define REF(s) (ref_vec ? v_ref[(s) * NT] : ref_pg)
+#define REF(s) (ref_vec ? v_ref[(s) * NP] : ref_pg)
 
-  // ---------------- fading state and CSI into shared memory
-  for (int s = 0; s < S; ++s) {
-    float a = 0.0f, b = 0.0f, c = 0.0f;
-    if (act) {
-      a = st.h[CK((eS + s) * 2, NERS * 2, 6)];
-      b = st.h[CK((eS + s) * 2 + 1, NERS * 2, 6)];
-      c = st.csi[CK(eS + s, NERS, 5)];
-    }
-    v_hr[s * NT] = a;
-    v_hi[s * NT] = b;
-    v_cg0[s * NT] = c;
-  }
-  float* csi = v_cg0;   // CSI of the previous PUSCH
-  float* gain = v_cg1;  // fading gain of this slot
-  float kb = 1.0f, ar_ = 0.0f, ai_ = 0.0f;
-  if (p.rician && act) {
-    // |sqrt(K/(K+1)) e^{j phi} + sqrt(1/(K+1)) h|^2 (NRNet._gain, nr_engine.py:602-611)
-    const float k_lin = st.k_lin[CK(er, NER, 1)];
-    const float kinv = fdv(1.0f, fa(k_lin, 1.0f));
-    const float ka = sqrtf(fm(k_lin, kinv));
-    kb = sqrtf(kinv);
-    ar_ = fm(ka, st.spec[CK(er * 2, NER * 2, 2)]);
-    ai_ = fm(ka, st.spec[CK(er * 2 + 1, NER * 2, 2)]);
-  }
+  // ---------------- CSI / fading gain rows of the step (written by the fading kernel)
+  const long long NERr = (long long)p.E * R;
+  const long long plane = (long long)S * NERr;
+  int u = 0;   // UL rows done
   // PHR cap n_max = floor(snr_ref_prbs * 10^((mean(ul_ref) - phr_min) / 10) / w[0]).clamp(1, S) (mac_ul.py:165-168),
   // the mean as a left-to-right sum times float32(1 / S)
   int n_max = S;
@@ -389,21 +417,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     float sum = 0.0f;
     for (int s = 0; s < S; ++s) sum = s == 0 ? REF(0) : fa(sum, REF(s));
     const float x = fm(fs(fm(sum, p.inv_S), p.phr_min), 0.1f);
-    const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
-    n_max = (int)clampf_t(floorf(fdv(nmp, s_w[0])), 1.0f, (float)S);
+    const float nmp = fm((float)p.ref_prbs, x_powf(10.0f, x));
+    n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
   }
 
   const uint32_t kenv = env_ok ? key_env(p.s0, A.env_id[CK(e, p.E, 10)], A.episode[CK(e, p.E, 10)], CH_STEP, A.rng_ctr[CK(e, p.E, 10)]) : 0u;
-  const float two_pi = 6.28318548202514648438f;
   const bool thr_mono = p.thr_mono != 0;
   const BlerGrid bgrid = {A.t.bler, p.C_axis, p.G_axis, p.MCS, p.s0_snr, p.inv_ds, A.status};
 
-  long long c_v[10];
-#pragma unroll
-  for (int i = 0; i < 10; ++i) c_v[i] = 0;
-  int c_hist[3][16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) { c_hist[0][i] = 0; c_hist[1][i] = 0; c_hist[2][i] = 0; }
 
   // first frame not yet finished (RLC scan start); frames are in stream order
   const int nvalid = cnt_q;
@@ -414,36 +435,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
 
   // ======================================================================= slot loop (nr_engine.py:656-667)
   for (int k = 0; k < p.K_rows; ++k) {
-    const int rel = p.rows[k][0], uls = p.rows[k][1], srf = p.rows[k][2], fad = p.rows[k][3];
+    const int rel = p.rows[k][0], uls = p.rows[k][1], srf = p.rows[k][2];
     const long long g = T * p.N + rel;
-    // ---- AR(1) fading step and gain (NRNet._evolve / _gain, nr_engine.py:570-611)
-    if (p.fading) {
-      const uint32_t base_f = key_stream(kenv, (uint32_t)((SITE_FADING << 16) | rel));
-      const float rho = p.rowf[k][0], c1 = p.rowf[k][1];
-#pragma unroll 1
-      for (int s = 0; s < S; ++s) {
-        float hr = v_hr[s * NT], hi = v_hi[s * NT];
-        if (fad) {
-          const uint32_t j = (uint32_t)((r * S + s) * 2);
-          const float zr = normal_at(base_f, j, two_pi);
-          const float zi = normal_at(base_f, j + 1u, two_pi);
-          hr = fa(fm(rho, hr), fm(fm(c1, zr), p.inv_sqrt2));
-          hi = fa(fm(rho, hi), fm(fm(c1, zi), p.inv_sqrt2));
-          v_hr[s * NT] = hr;
-          v_hi[s * NT] = hi;
-        }
-        float pw;
-        if (p.rician) {
-          const float xr = fa(ar_, fm(kb, hr)), xi = fa(ai_, fm(kb, hi));
-          pw = fa(fm(xr, xr), fm(xi, xi));
-        } else {
-          pw = fa(fm(hr, hr), fm(hi, hi));
-        }
-        gain[s * NT] = fm(10.0f, log10f(clamp_min_t(pw, 1e-6f)));
-      }
-    } else {
-      for (int s = 0; s < S; ++s) gain[s * NT] = 0.0f;
-    }
     // ---- arrival gate (NREngine._open_gate, engine.py:176-183)
     if ((srf || uls) && M > 0 && act) {
       long long vis = base;
@@ -459,49 +452,60 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
 
     // =================================================================== UL data slot (MacLink.slot, mac.py:228-508)
     const long long unsent = enq - sent;
+    // the CSI of this decision is gain row u (the gain of the previous UL row), this row's fading gain is row u + 1
+    const long long g_csi = (long long)u * plane, g_gain = g_csi + plane;
     // lumped SR grant (mac_ul.py:140-147)
     if (sr_t >= 0 && g - sr_t >= p.sr_delay) {
       bsr = bsr < 1 ? 1 : bsr;
       sr_t = -1;
     }
     // candidates: earliest ready NACKed process, else the first free one (mac.py:241-253)
-    int rx_p = 0, p_new = -1;
+    int rx_p = 0, p_new = freem ? __ffs(freem) - 1 : -1;
     long long best_ready = BIGI;
-    bool has_rx = false, pending = false;
-    if (act) {
-      for (int q = 0; q < P; ++q) {
-        const long long hs = st.h_state[CK(eP + q, NERP, 4)];
-        if (hs == 1) {
-          pending = true;
-          const long long rd = st.h_ready[CK(eP + q, NERP, 4)];
-          if (rd <= g) {
-            has_rx = true;
-            if (rd < best_ready) { best_ready = rd; rx_p = q; }
-          }
-        } else if (hs == 0 && p_new < 0) {
-          p_new = q;
-        }
+    bool has_rx = false;
+    const bool pending = pend != 0u;
+    for (uint32_t m_ = pend; m_; m_ &= m_ - 1u) {
+      const int q = __ffs(m_) - 1;
+      const long long rd = st.h_ready[CK(eP + q, NERP, 4)];
+      if (rd <= g) {
+        has_rx = true;
+        if (rd < best_ready) { best_ready = rd; rx_p = q; }
       }
     }
     const bool any_free = p_new >= 0;
     if (p_new < 0) p_new = 0;
     const long long need = bsr < unsent ? bsr : unsent;
     const bool new_el = act && any_free && need > 0 && !has_rx;
-    const int rx_nsb = act ? (int)st.h_nsb[CK(eP + rx_p, NERP, 4)] : 0;
-    // scheduler estimate with OLLA -> rate (bytes per RBG) (mac.py:255-266, mac_ul.py:154-171)
+    const int rx_nsb = has_rx ? (int)st.h_nsb[CK(eP + rx_p, NERP, 4)] : 0;
+    // scheduler estimate with OLLA -> rate (bytes per RBG) (mac.py:255-266, mac_ul.py:154-171) and the scheduler
+    // metric per RBG: PF rate / avg, maxCI rate, RR slot age (mac.py:267-275).  Only robots that may want RBGs use
+    // them; those are few, so the warp evaluates one such robot at a time with one lane per RBG.
     const float re_prb = (float)min(12 * uls - p.dmrs - p.oh, 156);
-    float* rate = v_x;
-#pragma unroll 1
-    for (int s = 0; s < S; ++s) {
-      const float est = fa(fs(REF(s), s_lw10[s]), csi[s * NT]);
-      const float eo = p.olla_on ? fa(est, olla) : fa(est, 0.0f);
-      const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
-      rate[s * NT] = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
-    }
-    // scheduler metric per RBG: PF rate / avg, maxCI rate, RR slot age (mac.py:267-275)
     const float avg_den = fmaxf(avg, 1e-9f);
     const float rr_metric = (float)(g - last_tx);
-#define METRIC(s) (p.sched == 2 ? rr_metric : (p.sched == 1 ? rate[(s) * NT] : fdv(rate[(s) * NT], avg_den)))
+    {
+      for (uint32_t wm = __ballot_sync(0xFFFFFFFFu, has_rx || new_el); wm; wm &= wm - 1u) {
+        const int a = __ffs(wm) - 1;
+        const int ta = wbase + a;
+        const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
+        const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
+        const float olla_a = __shfl_sync(0xFFFFFFFFu, olla, a);
+        const float avgd_a = __shfl_sync(0xFFFFFFFFu, avg_den, a);
+        if (lane < S) {
+          const int s = lane;
+          const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
+          const float est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+          const float eo = p.olla_on ? fa(est, olla_a) : fa(est, 0.0f);
+          const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
+          const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
+          d_x[s * NP + ta] = rt;
+          if (p.sched == 0) d_m[s * NP + ta] = x_fdv(rt, avgd_a);
+        }
+      }
+      __syncwarp();
+    }
+#define RATE(s) v_x[(s) * NP]
+#define METRIC(s) (p.sched == 2 ? rr_metric : (p.sched == 1 ? RATE(s) : v_m[(s) * NP]))
     // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit (mac.py:300-312)
     if (Grp<GW>::any_uniform(has_rx, sm, par)) {
       float rkey = -1.0f;
@@ -513,6 +517,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
       const int mine = has_rx ? rx_nsb : 0;
       int before = 0;
       if constexpr (GW <= 32) {
+#pragma unroll 1
         for (int j = 0; j < GW; ++j) {
           const float kj = __shfl_sync(0xFFFFFFFFu, rkey, j, GW);
           const int nj = __shfl_sync(0xFFFFFFFFu, mine, j, GW);
@@ -522,6 +527,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
         sm->rkey[r] = rkey;
         sm->rnsb[r] = mine;
         __syncthreads();
+#pragma unroll 1
         for (int j = 0; j < GW; ++j) {
           const float kj = sm->rkey[j];
           if (kj > rkey || (kj == rkey && j < r)) before += sm->rnsb[j];
@@ -533,48 +539,67 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     const int want_cnt = has_rx ? rx_nsb : (new_el ? n_max : 0);
     const bool lex = p.retx_priority != 0;
     const float prio = lex ? fm(1e9f, has_rx ? 1.0f : 0.0f) : 0.0f;
-    // greedy allocation RBG by RBG (mac.py:322-351); key = (retx wanting, metric + prio, lowest robot)
+    // greedy allocation RBG by RBG (mac.py:322-351); key = (retx wanting, metric + prio, lowest robot).  RBGs only
+    // move while at least one robot wants them, so where no group of the warp (block) has two candidates the only
+    // candidate takes each RBG it still wants, which is what the argmax rounds give; else the rounds run.
     uint32_t won = 0u;
     int cnt = 0;
     float left = (float)need;
-#pragma unroll 1
-    for (int s = 0; s < S; ++s) {
-      const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
-      const float mkey = want ? fa(METRIC(s), prio) : -1.0f;
-      const bool wr = lex && want && has_rx;
-      const unsigned long long key = ((unsigned long long)(wr ? 1u : 0u) << 40) |
-                                     ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
-      const unsigned long long mx = Grp<GW>::max_u64(key, sm, par);
-      const bool oh = (255 - (int)(mx & 0xFFull) == r) && (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f);
-      if (oh) {
-        won |= 1u << s;
-        cnt += 1;
-      }
-      left = fs(left, fm(fm(rate[s * NT], oh ? 1.0f : 0.0f), has_rx ? 0.0f : 1.0f));
-    }
-    if (!lex) {
-      // retransmissions that won fewer RBGs than their TB needs release them to the new-data robots (mac.py:353-379)
-      const bool short_ = has_rx && (__popc(won) != rx_nsb);
-      const uint32_t rel_rs = short_ ? won : 0u;
-      if (short_) won = 0u;
-      cnt = __popc(won);
+    if (Grp<GW>::two_or_more_uniform(act && want_cnt > 0)) {
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
-        const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
-        const float mkey = want ? METRIC(s) : -1.0f;
-        const unsigned long long key = ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
+        const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
+        const float mkey = want ? fa(METRIC(s), prio) : -1.0f;
+        const bool wr = lex && want && has_rx;
+        const unsigned long long key = ((unsigned long long)(wr ? 1u : 0u) << 40) |
+                                       ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
         const unsigned long long mx = Grp<GW>::max_u64(key, sm, par);
-        const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u, sm, par);
-        const bool oh = (255 - (int)(mx & 0xFFull) == r) &&
-                        (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f) && av;
+        const bool oh = (255 - (int)(mx & 0xFFull) == r) && (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f);
         if (oh) {
           won |= 1u << s;
           cnt += 1;
+          if (!has_rx) left = fs(left, RATE(s));
         }
-        left = fs(left, fm(rate[s * NT], oh ? 1.0f : 0.0f));
       }
+      if (!lex) {
+        // retransmissions that won fewer RBGs than their TB needs release them to the new-data robots (mac.py:353-379)
+        const bool short_ = has_rx && (__popc(won) != rx_nsb);
+        const uint32_t rel_rs = short_ ? won : 0u;
+        if (short_) won = 0u;
+        cnt = __popc(won);
+#pragma unroll 1
+        for (int s = 0; s < S; ++s) {
+          const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
+          const float mkey = want ? METRIC(s) : -1.0f;
+          const unsigned long long key = ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
+          const unsigned long long mx = Grp<GW>::max_u64(key, sm, par);
+          const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u, sm, par);
+          const bool oh = (255 - (int)(mx & 0xFFull) == r) &&
+                          (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f) && av;
+          if (oh) {
+            won |= 1u << s;
+            cnt += 1;
+            left = fs(left, RATE(s));
+          }
+        }
+      }
+    } else {
+      if (act && want_cnt > 0) {
+#pragma unroll 1
+        for (int s = 0; s < S && cnt < want_cnt; ++s) {
+          if (!(has_rx || left > 0.0f)) break;
+          if (fa(METRIC(s), prio) >= 0.0f) {
+            won |= 1u << s;
+            cnt += 1;
+            if (!has_rx) left = fs(left, RATE(s));
+          }
+        }
+      }
+      // a short retransmission releases its RBGs; with no other candidate nobody takes them
+      if (!lex && has_rx && (__popc(won) != rx_nsb)) won = 0u;
     }
 #undef METRIC
+#undef RATE
     const int n_sb = __popc(won);
     float n_prb = 0.0f;
     for (int s = 0; s < S; ++s)
@@ -583,29 +608,54 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    const float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
-    float* negl = v_x;    // -10^(clamp(sinr, -30, 60) / 10) per RBG (the rates are no longer needed)
-    const float lnw = tx ? lnw_of(s_lw, won, S) : 0.0f;
-    // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): highest passing MCS, scanned downward
+    const float split = fm(10.0f, x_log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
+    // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
+    float lnw = 0.0f;
     int mcs_new = 0;
     long long tbs_new = 0;
-    if (tx_new) {
-      const long long trow = (long long)(int)n_prb * p.MCS;
-      for (int s = 0; s < S; ++s) {
-        const float est_tx = fa(fs(REF(s), split), csi[s * NT]);
-        negl[s * NT] = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+    for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+      const int a = __ffs(tm) - 1;
+      const int ta = wbase + a;
+      const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
+      const uint32_t won_a = __shfl_sync(0xFFFFFFFFu, won, a);
+      const bool in = lane < S && ((won_a >> lane) & 1u);
+      const float lw_l = lane < S ? s_lw[lane] : 0.0f;
+      // logsumexp of log(w) over the grant
+      const float lmx = warp_max(in ? lw_l : -INFINITY);
+      const float lm0 = isinf(lmx) ? 0.0f : lmx;
+      const float lnw_a = fa(x_logf(ordered_sum(in ? x_expf(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
+      if (lane == a) lnw = lnw_a;
+      if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
+        // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
+        // whose TB BLER at the EESM SINR (+ OLLA) meets the target, else 0; lane m evaluates MCS m
+        const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
+        const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
+        const float off_a = __shfl_sync(0xFFFFFFFFu, p.olla_on ? olla : 0.0f, a);
+        const float nprb_a = __shfl_sync(0xFFFFFFFFu, n_prb, a);
+        if (lane < S) {   // -10^(clamp(est, -30, 60) / 10) per RBG into the robot's column (rates are done)
+          const int s = lane;
+          const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
+          const float est_tx = fa(fs(refs, split_a), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+          d_x[s * NP + ta] = -x_powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+        }
+        __syncwarp();
+        const long long trow = (long long)(int)nprb_a * p.MCS;
+        bool pass = false;
+        if (lane <= p.mcs_max && A.t.la_tbs[CK(trow + lane, NLA, 9)] > 0) {
+          const int m = lane;
+          const float eff = fa(eesm_db(d_x + ta, NP, s_lw, won_a, S, s_beta[m], lnw_a), off_a);
+          const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
+          const float tbler = fs(1.0f, x_powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+          pass = tbler <= p.target;
+        }
+        const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
+        if (lane == a) {
+          mcs_new = pm ? 31 - __clz(pm) : 0;
+          tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
+        }
+        __syncwarp();
       }
-      const float off = p.olla_on ? olla : 0.0f;
-      int chosen = -1;
-      for (int m = p.mcs_max; m >= 0; --m) {
-        if (A.t.la_tbs[CK(trow + m, NLA, 9)] <= 0) continue;
-        const float eff = fa(eesm_db(negl, NT, s_lw, won, S, s_beta[m], lnw), off);
-        const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-        const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
-        if (tbler <= p.target) { chosen = m; break; }
-      }
-      mcs_new = chosen < 0 ? 0 : chosen;
-      tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
     }
     long long cap_b = tbs_new / 8 - p.tb_oh;
     cap_b = cap_b < 1 ? 1 : cap_b;
@@ -622,37 +672,67 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
       st.h_ntx[CK(hp, NERP, 4)] = 0;
       st.h_comb[CK(hp, NERP, 4)] = 0.0f;
       st.h_state[CK(hp, NERP, 4)] = 1;
+      pend |= 1u << p_tx;
+      freem &= ~(1u << p_tx);
       sent += byt_new;
     }
     // ---- decode on the actual channel, HARQ update (mac.py:424-477)
     bool ok = false, fail = false, exh = false;
     long long served = 0;
     int ntx = 0;
+    int mcs = 0;
+    long long tbs = 0;
     if (tx) {
-      const int mcs = (int)st.h_mcs[CK(hp, NERP, 4)];
-      const long long tbs = st.h_tbs[CK(hp, NERP, 4)];
+      mcs = (int)st.h_mcs[CK(hp, NERP, 4)];
+      tbs = st.h_tbs[CK(hp, NERP, 4)];
       ntx = (int)st.h_ntx[CK(hp, NERP, 4)] + 1;
-      for (int s = 0; s < S; ++s) {
-        const float a_ = fa(fs(REF(s), split), gain[s * NT]);
-        negl[s * NT] = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+    }
+    // EESM SINR of the TB's MCS on this row's channel (PHY.eff_sinr, phy.py:311-321), one lane per RBG
+    float eff_tx = 0.0f;
+    for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+      const int a = __ffs(tm) - 1;
+      const int ta = wbase + a;
+      const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
+      const uint32_t won_a = __shfl_sync(0xFFFFFFFFu, won, a);
+      const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
+      const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
+      const float lnw_a = __shfl_sync(0xFFFFFFFFu, lnw, a);
+      const float beta = s_beta[__shfl_sync(0xFFFFFFFFu, mcs, a)];
+      const bool in = lane < S && ((won_a >> lane) & 1u);
+      float x = -INFINITY;
+      if (in) {
+        const int s = lane;
+        const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
+        const float a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
+        const float negl = -x_powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+        x = fa(x_fdv(negl, beta), s_lw[s]);
       }
-      const float eff = eesm_db(negl, NT, s_lw, won, S, s_beta[mcs], lnw);
-      const float lin = powf(10.0f, fm(eff, 0.1f));
+      const float mx = warp_max(x);
+      const float m0 = isinf(mx) ? 0.0f : mx;
+      const float lse = fa(x_logf(ordered_sum(in ? x_expf(fs(x, m0)) : 0.0f, won_a)), m0);
+      const float eff = db_of(fm(-beta, fs(lse, lnw_a)));
+      if (lane == a) eff_tx = eff;
+    }
+    if (tx) {
+      const float eff = eff_tx;
+      const float lin = x_powf(10.0f, fm(eff, 0.1f));
       const float comb = p.comb_cc ? fa(st.h_comb[CK(hp, NERP, 4)], lin) : lin;
-      const float eff_used = fm(10.0f, log10f(clamp_min_t(comb, 1e-9f)));
+      const float eff_used = fm(10.0f, x_log10f(clamp_min_t(comb, 1e-9f)));
       float cbs, ncb;
       segment(tbs, s_rate[mcs], cbs, ncb);
       int i0;
       float wi;
       cidx(p, cbs, i0, wi);
       const float b = bler_lookup(bgrid, mcs, eff_used, i0, wi);
-      const float p_err = fs(1.0f, powf(fs(1.0f, b), ncb));
+      const float p_err = fs(1.0f, x_powf(fs(1.0f, b), ncb));
       const float u = uniform_at(key_stream(kenv, (uint32_t)((SITE_BLER_UL << 16) | rel)), (uint32_t)r);
       ok = u >= p_err;
       fail = !ok;
       exh = fail && ntx >= p.max_tx;
       if (ok) {
         st.h_state[CK(hp, NERP, 4)] = 0;
+        pend &= ~(1u << p_tx);
+        freem |= 1u << p_tx;
         st.h_ready[CK(hp, NERP, 4)] = g;
       }
       st.h_ntx[CK(hp, NERP, 4)] = ntx;
@@ -666,10 +746,12 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
           st.h_ready[CK(hp, NERP, 4)] = g + p.rlc_retx;
         } else {
           st.h_state[CK(hp, NERP, 4)] = 0;
+          pend &= ~(1u << p_tx);
+          freem |= 1u << p_tx;
           for (int f = 0; f < F; ++f) {
             const long long at = eF + f;
             if (st.cap[CK(at, NERF, 3)] >= 0 && st.start[CK(at, NERF, 3)] < hi_tx && st.end_[CK(at, NERF, 3)] > lo_tx) {
-              if (!st.lost[CK(at, NERF, 3)]) c_v[9] += 1;
+              if (!st.lost[CK(at, NERF, 3)]) atomicAdd(sc + INB_CTR_LOST_FRAMES, 1ull);
               st.lost[CK(at, NERF, 3)] = 1;
             }
           }
@@ -689,30 +771,36 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
       olla = clampf_t(fs(fa(olla, up), dn), -10.0f, 10.0f);
     }
     if (tx) bsr = enq - sent;
-    {
-      float* t_ = csi;    // the gain of this slot is the CSI of the next decision
-      csi = gain;
-      gain = t_;
-    }
+    ++u;   // the gain of this row is the CSI of the next decision
     avg = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, (float)served)), 1e-9f);
     if (p.sched == 2 && tx) last_tx = g;
-    if (act) {
-      c_v[0] += tx_new; c_v[1] += tx_rx; c_v[2] += ok; c_v[3] += fail; c_v[4] += exh;
-      c_v[5] += served; c_v[6] += tx_new ? byt_new : 0; c_v[7] += (tx_new && pending);
-      c_v[8] += tx ? (long long)n_prb : 0;
-      if (tx) {
-        int kx = ntx < p.max_tx ? ntx : p.max_tx;
-        kx = kx < 15 ? kx : 15;
-        c_hist[1][kx] += 1;
-        if (ok) c_hist[0][kx] += 1;
-        if (fail) c_hist[2][kx] += 1;
+    if (tx) {   // counters (only transmitting robots have any to add)
+      if (tx_new) {
+        atomicAdd(sc + INB_CTR_TB_NEW, 1ull);
+        atomicAdd(sc + INB_CTR_BYTES_NEW, (unsigned long long)byt_new);
+        if (pending) atomicAdd(sc + INB_CTR_NEW_WHILE_PENDING, 1ull);
       }
+      if (tx_rx) atomicAdd(sc + INB_CTR_TB_RETX, 1ull);
+      if (ok) {
+        atomicAdd(sc + INB_CTR_TB_OK, 1ull);
+        atomicAdd(sc + INB_CTR_BYTES_OK, (unsigned long long)served);
+      }
+      if (fail) atomicAdd(sc + INB_CTR_TB_FAIL, 1ull);
+      if (exh) atomicAdd(sc + INB_CTR_EXHAUST, 1ull);
+      atomicAdd(sc + INB_CTR_PRB_USED, (unsigned long long)(long long)n_prb);
+      int kx = ntx < p.max_tx ? ntx : p.max_tx;
+      kx = kx < 15 ? kx : 15;
+      atomicAdd(sc + INB_CTR_RV_TX + kx, 1ull);
+      if (ok) atomicAdd(sc + INB_CTR_NTX_HIST + kx, 1ull);
+      if (fail) atomicAdd(sc + INB_CTR_RV_FAIL + kx, 1ull);
     }
     // ---- RLC in-order delivery (mac.py:499-503): frames are in stream order, so the completed ones are a prefix
     if (act) {
+#ifdef INB_CHECK
       CK(eP + P - 1, NERP, 12);
-      const long long ack = ack_ptr(st, eP, P, sent, floor_);
-      const double fin_val = da(da((double)T, ddv((double)(rel + 1), (double)p.N)), p.proc_off);
+#endif
+      const long long ack = ack_ptr(st, eP, pend, sent, floor_);
+      const double fin_val = da(da((double)T, x_ddv((double)(rel + 1), (double)p.N)), p.proc_off);
       for (int f = f_scan; f < nvalid; ++f) {
         const long long at = eF + f;
         if (st.end_[CK(at, NERF, 3)] > ack) break;
@@ -722,122 +810,25 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 512 / GW : 4) nr
     }
   }
 
-  // ======================================================================= finish (nr_engine.py:843-888)
+  // ======================================================================= step state and outputs
+  // (the end-of-step queue work runs in the finish kernel, nr_finish.cu)
   if (M > 0) enq = full_enq;
-  bool det_hit = false;
   if (act) {
     const InbOutputs& o = A.o;
-    const long long ack_end = ack_ptr(st, eP, P, sent, floor_);
-    const double lim = da((double)(T + 1), 1e-9);
-    long long newest = -1;
-    uint64_t gone_mask = 0ull;
-    for (int f = 0; f < F; ++f) {
-      const long long at = eF + f;
-      const long long cap = st.cap[CK(at, NERF, 3)];
-      const bool valid = cap >= 0;
-      const double fin = st.fin[CK(at, NERF, 3)];
-      const bool delivered = valid && fin <= lim;
-      const bool timed = p.purge && valid && isinf(fin) && ((T + 1 - cap) >= p.timeout);
-      const bool dropped = valid && st.lost[CK(at, NERF, 3)] && (st.end_[CK(at, NERF, 3)] <= ack_end) && !timed;
-      if (delivered && cap > newest) newest = cap;
-      if (delivered && st.det[CK(at, NERF, 3)] && st.hid[CK(at, NERF, 3)] == last_hid) det_hit = true;
-      const double off = st.off[CK(at, NERF, 3)];
-      o.delivered[CK(at, NERF, 3)] = delivered;
-      o.timed_out[CK(at, NERF, 3)] = timed;
-      o.dropped[CK(at, NERF, 3)] = dropped;
-      o.cap[CK(at, NERF, 3)] = valid ? cap - epoch : -1;
-      o.cls[CK(at, NERF, 3)] = valid ? st.cls[CK(at, NERF, 3)] : 0;
-      const float delay = (float)dsb(dsb(fin, (double)cap), off);
-      o.delay[CK(at, NERF, 3)] = delivered ? delay : NAN;
-      o.arrival[CK(at, NERF, 3)] = valid ? da((double)(cap - epoch), off) : NAN;
-      o.arrival_slot[CK(at, NERF, 3)] = valid ? (long long)rint(dm(off, (double)p.N)) : -1;
-      o.tag[CK(at, NERF, 3)] = valid ? st.tag[CK(at, NERF, 3)] : 0;
-      o.priority[CK(at, NERF, 3)] = valid ? st.prio[CK(at, NERF, 3)] : 0;
-      o.bytes[CK(at, NERF, 3)] = valid ? st.end_[CK(at, NERF, 3)] - st.start[CK(at, NERF, 3)] : 0;
-      const double dl = st.dline[CK(at, NERF, 3)];
-      const bool late = delivered && (dm((double)delay, p.ctl_ms) > dl);
-      o.deadline_miss[CK(at, NERF, 3)] = late || ((timed || dropped) && isfinite(dl));
-      if (delivered || timed || dropped || !valid) gone_mask |= 1ull << f;
-    }
-    // compaction: surviving frames first (stable), then the freed slots in index order (queues.py:105-110)
-    int order[INB_MAX_F];
-    int n_keep = 0;
-    for (int f = 0; f < F; ++f)
-      if (!((gone_mask >> f) & 1ull)) order[n_keep++] = f;
-    {
-      int n = n_keep;
-      for (int f = 0; f < F; ++f)
-        if ((gone_mask >> f) & 1ull) order[n++] = f;
-    }
-    if (gone_mask != ((F >= 64) ? ~0ull : ((1ull << F) - 1ull)) || n_keep > 0) {
-      auto perm64 = [&](int64_t* a, bool is_cap) {
-        long long tmp[INB_MAX_F];
-        for (int f = 0; f < F; ++f) {
-          const int src = order[f];
-          tmp[f] = (is_cap && ((gone_mask >> src) & 1ull)) ? -1 : a[CK(eF + src, NERF, 3)];
-        }
-        for (int f = 0; f < F; ++f) a[CK(eF + f, NERF, 3)] = tmp[f];
-      };
-      auto permd = [&](double* a) {
-        double tmp[INB_MAX_F];
-        for (int f = 0; f < F; ++f) tmp[f] = a[CK(eF + order[f], NERF, 3)];
-        for (int f = 0; f < F; ++f) a[CK(eF + f, NERF, 3)] = tmp[f];
-      };
-      auto perm8 = [&](uint8_t* a) {
-        uint8_t tmp[INB_MAX_F];
-        for (int f = 0; f < F; ++f) tmp[f] = a[CK(eF + order[f], NERF, 3)];
-        for (int f = 0; f < F; ++f) a[CK(eF + f, NERF, 3)] = tmp[f];
-      };
-      perm64(st.cap, true);
-      perm64(st.start, false); perm64(st.end_, false); perm64(st.cls, false); perm64(st.hid, false);
-      perm64(st.tag, false); perm64(st.prio, false);
-      perm8(st.lost); perm8(st.det);
-      permd(st.fin); permd(st.off); permd(st.dline);
-    } else {
-      for (int f = 0; f < F; ++f) st.cap[CK(eF + f, NERF, 3)] = -1;
-    }
-    // stream floor, send pointer, HARQ processes holding only purged bytes (MacLink.compact, mac.py:598-616)
-    floor_ = n_keep > 0 ? st.start[CK(eF, NERF, 3)] : enq;
-    sent = sent > floor_ ? sent : floor_;
-    for (int q = 0; q < P; ++q) {
-      const long long hq = eP + q;
-      if (st.h_state[CK(hq, NERP, 4)] == 1 && st.h_hi[CK(hq, NERP, 4)] <= floor_ && st.h_hi[CK(hq, NERP, 4)] > st.h_lo[CK(hq, NERP, 4)]) {
-        st.h_state[CK(hq, NERP, 4)] = 0; st.h_ready[CK(hq, NERP, 4)] = 0; st.h_ntx[CK(hq, NERP, 4)] = 0; st.h_comb[CK(hq, NERP, 4)] = 0.0f;
-      }
-    }
-    bsr = bsr < enq - sent ? bsr : enq - sent;
-    const long long qb = enq - ack_ptr(st, eP, P, sent, floor_);
-    o.newest[CK(er, NER, 1)] = newest >= 0 ? newest - epoch : -1;
-    o.queue_len[CK(er, NER, 1)] = n_keep;
-    o.queue_bytes[CK(er, NER, 1)] = (float)(qb > 0 ? qb : 0);
     o.sinr_db[CK(er, NER, 1)] = sinr_obs;
     if (o.pathgain) o.pathgain[CK(er, NER, 1)] = pg;
     o.gen_accepted[CK(er, NER, 1)] = n_acc;
     o.gen_bytes[CK(er, NER, 1)] = full_enq - n0;
-    // ---- state back to memory
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
-    for (int s = 0; s < S; ++s) {
-      st.csi[CK(eS + s, NERS, 5)] = csi[s * NT];
-      st.h[CK((eS + s) * 2, NERS * 2, 6)] = v_hr[s * NT];
-      st.h[CK((eS + s) * 2 + 1, NERS * 2, 6)] = v_hi[s * NT];
-    }
   }
 #undef REF
-  // det_env and counters: group reductions, then one writer per group
-  const bool det_any = Grp<GW>::any(det_hit, sm, par);
-  if (env_ok && r == 0) A.o.det_env[CK(e, p.E, 10)] = det_any ? 1 : 0;
-  if (act) {
+  // counters: one writer per word and env
+  __syncthreads();
+  if (env_ok) {
     int64_t* c = A.ctr + CK(e, p.E, 10) * INB_NCTR;
-#pragma unroll
-    for (int i = 0; i < 10; ++i)
-      if (c_v[i]) atomicAdd((unsigned long long*)&c[i], (unsigned long long)c_v[i]);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      if (c_hist[0][i]) atomicAdd((unsigned long long*)&c[INB_CTR_NTX_HIST + i], (unsigned long long)c_hist[0][i]);
-      if (c_hist[1][i]) atomicAdd((unsigned long long*)&c[INB_CTR_RV_TX + i], (unsigned long long)c_hist[1][i]);
-      if (c_hist[2][i]) atomicAdd((unsigned long long*)&c[INB_CTR_RV_FAIL + i], (unsigned long long)c_hist[2][i]);
-    }
+    for (int i = r; i < INB_NCTR; i += GW)
+      if (sc[i]) atomicAdd((unsigned long long*)&c[i], sc[i]);
   }
   if (env_ok && r == 0) A.rng_ctr[CK(e, p.E, 10)] += 1;
 #undef CK

@@ -6,8 +6,8 @@ template <int GW>
 cudaError_t launch_gw(const InbStepArgs& a, cudaStream_t stream) {
   constexpr int NT = GW > 32 ? GW : 128;
   const int gpb = GW > 32 ? 1 : 128 / GW;
-  const int vecs = a.ul_ref_in != nullptr ? 6 : 5;
-  const size_t smem = (size_t)vecs * a.p.S * NT * sizeof(float);
+  const int vecs = a.ul_ref_in != nullptr ? 3 : 2;
+  const size_t smem = (size_t)vecs * a.p.S * (NT + 1) * sizeof(float);
   static size_t configured = 0;   // dynamic shared memory above 48 KB needs an opt-in, once per size
   if (smem > 48 * 1024 && smem > configured) {
     cudaError_t e = cudaFuncSetAttribute(nr_step_kernel<GW>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

@@ -246,6 +246,9 @@ class NRB200Engine:
         a.env_id, a.episode, a.rng_ctr = self.env_id.data_ptr(), self.episode.data_ptr(), self.rng_ctr.data_ptr()
         a.epoch, a.last_hid, a.ctr, a.status = (self.epoch.data_ptr(), self._last_hid.data_ptr(),
                                                 self.ctr.data_ptr(), self.status.data_ptr())
+        # fading-gain rows of one step: the CSI before the step + one row per UL slot (at most slots_per_step)
+        self._gain = torch.empty((self.N + 1) * self.S * self.E * self.R, dtype=torch.float32, device=self.dev)
+        a.gain, a.gain_cap = self._gain.data_ptr(), self._gain.numel()
 
     def _stream(self):
         return ctypes.c_void_p(torch.cuda.current_stream(self.dev).cuda_stream)
