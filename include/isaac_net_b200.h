@@ -144,8 +144,19 @@ typedef struct {
   int64_t gain_cap;             /* elements available at `gain` */
 } InbStepArgs;
 
-/* One control step of the NR uplink engine: the fading launch, then the MAC launch, on `cuda_stream`. */
+/* One control step of the NR uplink engine: the fading, MAC and finish launches, on `cuda_stream`. */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
+
+/* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array
+ * inside the library (INB_NOALLOC_GAIN_MAX float32 elements per device), so `gain` / `gain_cap` are ignored and
+ * nothing is allocated at call time.  No counterpart in the reference (its torch backends allocate per call).
+ *   -7: (UL rows + 1) x S x E x R exceeds INB_NOALLOC_GAIN_MAX (use inb_nr_step with a caller buffer);
+ *   -8 / -9: no current CUDA device / the array's device address could not be resolved.
+ * The array's address is resolved on the first call on each device: make that call before capturing a CUDA graph.
+ * The array needs no initial value (each step writes every row it reads), but all calls on one device share it, so
+ * calls on one device must not overlap: issue them on one stream (or order the streams). */
+#define INB_NOALLOC_GAIN_MAX (1 << 25)
+int inb_nr_step_noalloc(const InbStepArgs *args, void *cuda_stream);
 
 /* Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial
  * values, fading state h = N(0,1)/sqrt(2) draws (site H0), Rician phasor (site KPHI) and K. */

@@ -101,7 +101,9 @@ class InbTrafficArgs(ctypes.Structure):
                 + [("calls", P), ("src", InbTrafficSource * MAX_SRC)] + [(n, P) for n in TRAFFIC_OUT])
 
 
-EXPORTS = ("inb_nr_step", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step", "inb_abi_version")
+EXPORTS = ("inb_nr_step", "inb_nr_step_noalloc", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step",
+           "inb_abi_version")
+NOALLOC_GAIN_MAX = 1 << 25
 _lib = None
 
 
@@ -120,6 +122,8 @@ def lib():
         raise RuntimeError(f"{LIB_PATH} has ABI {L.inb_abi_version()}, expected {ABI_VERSION}: rebuild it")
     L.inb_nr_step.restype = ctypes.c_int
     L.inb_nr_step.argtypes = [ctypes.POINTER(InbStepArgs), P]
+    L.inb_nr_step_noalloc.restype = ctypes.c_int
+    L.inb_nr_step_noalloc.argtypes = [ctypes.POINTER(InbStepArgs), P]
     L.inb_nr_reset.restype = ctypes.c_int
     L.inb_nr_reset.argtypes = [ctypes.POINTER(InbResetArgs), P]
     L.inb_rng_draw.restype = ctypes.c_int

@@ -1,6 +1,8 @@
-// C entry point of the NR uplink step: argument checks, then three launches on the caller's stream: the fading
+// C entry points of the NR uplink step: argument checks, then three launches on the caller's stream: the fading
 // (nr_fading.cu), the MAC kernel variant of the group width (nr_step_g16.cu ... nr_step_g128.cu; the kernel is in
 // nr_step.cuh) and the end-of-step finish (nr_finish.cu).
+#include <mutex>
+
 #include "nr_common.cuh"
 namespace inb {
 cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
@@ -9,13 +11,10 @@ cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
-}  // namespace inb
 
-extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
-  if (args == nullptr) return -1;
-  const InbStepArgs& a = *args;
+// argument checks shared by both entry points; *gain_need = float32 elements of the step's gain rows
+static int check_args(const InbStepArgs& a, long long* gain_need) {
   const InbParams& p = a.p;
-  if (p.E <= 0) return 0;
   if (p.R < 1 || p.R > 128 || p.S < 1 || p.S > INB_MAX_S || p.P < 1 || p.P > INB_MAX_P || p.F < 1 ||
       p.F > INB_MAX_F || p.M < 0 || p.M > INB_MAX_M || p.MCS < 1 || p.MCS > INB_MAX_MCS || p.K_rows < 0 ||
       p.K_rows > INB_MAX_ROWS || p.max_tx < 1 || p.mcs_max < 0 || p.mcs_max >= p.MCS)
@@ -26,20 +25,73 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
     return -5;
   int n_ul = 0;
   for (int k = 0; k < p.K_rows; ++k) n_ul += p.rows[k][1] > 0 ? 1 : 0;
-  if (a.gain == nullptr || a.gain_cap < (long long)(n_ul + 1) * p.S * p.E * p.R) return -6;
-  cudaStream_t s = (cudaStream_t)cuda_stream;
-  cudaError_t err = inb::launch_fading(a, s);
+  *gain_need = (long long)(n_ul + 1) * p.S * p.E * p.R;
+  return 0;
+}
+
+static int launch_all(const InbStepArgs& a, cudaStream_t s) {
+  const InbParams& p = a.p;
+  cudaError_t err = launch_fading(a, s);
   if (err != cudaSuccess) return -100 - (int)err;
   if (p.R <= 16)
-    err = inb::launch_step_g16(a, s);
+    err = launch_step_g16(a, s);
   else if (p.R <= 32)
-    err = inb::launch_step_g32(a, s);
+    err = launch_step_g32(a, s);
   else if (p.R <= 64)
-    err = inb::launch_step_g64(a, s);
+    err = launch_step_g64(a, s);
   else
-    err = inb::launch_step_g128(a, s);
-  if (err == cudaSuccess) err = inb::launch_finish(a, s);
+    err = launch_step_g128(a, s);
+  if (err == cudaSuccess) err = launch_finish(a, s);
   return err == cudaSuccess ? 0 : -100 - (int)err;
+}
+
+// Gain-row scratch of inb_nr_step_noalloc: a fixed array in the library's device image (one per device the library
+// runs on), resolved to a device address once per device.  Its contents need no initial value: the fading launch of
+// a step writes every row the MAC launch of that step reads.
+__device__ __align__(256) float g_gain_scratch[INB_NOALLOC_GAIN_MAX];
+constexpr int kMaxDevices = 64;
+static float* g_scratch_addr[kMaxDevices];
+static std::mutex g_scratch_mu;
+
+static int scratch_of_current_device(float** out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -8;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (g_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_gain_scratch) != cudaSuccess || p == nullptr) return -9;
+    g_scratch_addr[dev] = static_cast<float*>(p);
+  }
+  *out = g_scratch_addr[dev];
+  return 0;
+}
+}  // namespace inb
+
+extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
+  if (args == nullptr) return -1;
+  const InbStepArgs& a = *args;
+  if (a.p.E <= 0) return 0;
+  long long need = 0;
+  const int rc = inb::check_args(a, &need);
+  if (rc != 0) return rc;
+  if (a.gain == nullptr || a.gain_cap < need) return -6;
+  return inb::launch_all(a, (cudaStream_t)cuda_stream);
+}
+
+extern "C" int inb_nr_step_noalloc(const InbStepArgs* args, void* cuda_stream) {
+  if (args == nullptr) return -1;
+  if (args->p.E <= 0) return 0;
+  long long need = 0;
+  const int rc = inb::check_args(*args, &need);
+  if (rc != 0) return rc;
+  if (need > (long long)INB_NOALLOC_GAIN_MAX) return -7;
+  float* scratch = nullptr;
+  const int sr = inb::scratch_of_current_device(&scratch);
+  if (sr != 0) return sr;
+  InbStepArgs a = *args;
+  a.gain = scratch;
+  a.gain_cap = INB_NOALLOC_GAIN_MAX;
+  return inb::launch_all(a, (cudaStream_t)cuda_stream);
 }
 
 extern "C" int inb_abi_version(void) { return INB_ABI_VERSION; }
