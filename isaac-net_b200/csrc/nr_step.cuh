@@ -251,7 +251,7 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 
 // ------------------------------------------------------------------------------------------------ the step kernel
 template <int GW>
-__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 768 / GW : 6) nr_step_kernel(const InbStepArgs A) {
+__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr int NT = GW > 32 ? GW : 128;
   constexpr int NP = NT + 1;   // row stride of the shared vectors: a warp reading one column across rows is
                                // conflict-free as well as a warp reading one row
@@ -823,8 +823,12 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 768 / GW : 6) nr
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
   }
 #undef REF
-  // counters: one writer per word and env
-  __syncthreads();
+  // counters: one writer per word and env (an env's counter words are shared by its group only)
+  if constexpr (GW > 32) {
+    __syncthreads();
+  } else {
+    __syncwarp();
+  }
   if (env_ok) {
     int64_t* c = A.ctr + CK(e, p.E, 10) * INB_NCTR;
     for (int i = r; i < INB_NCTR; i += GW)
