@@ -176,24 +176,8 @@ __device__ __forceinline__ float db_of(float lin) {
 }
 
 // EESM effective SINR (dB) of one MCS over the won RBGs (PHY.eff_sinr / eff_sinr_all, phy.py:311-336):
-// x_s = -lin_s / beta + log(w_s) on won RBGs (-inf elsewhere), logsumexp as max + left-to-right sum of exp(x - max),
-// eff = -beta (lse - lnw).  negl[s * ld] = -lin_s.
-static __device__ __noinline__ float eesm_db(const float* negl, int ld, const float* __restrict__ lw, uint32_t won, int S,
-                                      float beta, float lnw) {
-  float mx = -INFINITY;
-#pragma unroll 1
-  for (int s = 0; s < S; ++s)
-    if ((won >> s) & 1u) mx = fmaxf(mx, fa(x_fdv(negl[s * ld], beta), lw[s]));
-  const float m0 = isinf(mx) ? 0.0f : mx;
-  float sum = 0.0f;
-#pragma unroll 1
-  for (int s = 0; s < S; ++s) {
-    float e = ((won >> s) & 1u) ? x_expf(fs(fa(x_fdv(negl[s * ld], beta), lw[s]), m0)) : 0.0f;
-    sum = s == 0 ? e : fa(sum, e);
-  }
-  const float lse = fa(x_logf(sum), m0);
-  return db_of(fm(-beta, fs(lse, lnw)));
-}
+// x_s = -lin_s / beta + log(w_s) on won RBGs, logsumexp as max + the left-to-right sum of exp(x - max),
+// eff = -beta (lse - lnw).  The kernel evaluates it with one lane per RBG (warp_max, ordered_sum below).
 
 // warp-wide max (fmaxf: order-independent) and the sum of lane values over the set bits of `won` in ascending lane
 // order (the left-to-right RBG sum of the serial code; lanes outside `won` would add +0.0, which changes nothing)
@@ -628,33 +612,41 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (lane == a) lnw = lnw_a;
       if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
         // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
-        // whose TB BLER at the EESM SINR (+ OLLA) meets the target, else 0; lane m evaluates MCS m
+        // whose TB BLER at the EESM SINR (+ OLLA) meets the target, else 0; MCS scanned downward (the first that
+        // passes is the highest), the EESM of each with one lane per RBG
         const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
         const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
         const float off_a = __shfl_sync(0xFFFFFFFFu, p.olla_on ? olla : 0.0f, a);
         const float nprb_a = __shfl_sync(0xFFFFFFFFu, n_prb, a);
-        if (lane < S) {   // -10^(clamp(est, -30, 60) / 10) per RBG into the robot's column (rates are done)
+        float ng = 0.0f;   // -10^(clamp(est, -30, 60) / 10) of this lane's RBG
+        if (in) {
           const int s = lane;
           const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
           const float est_tx = fa(fs(refs, split_a), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
-          d_x[s * NP + ta] = -x_powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+          ng = -x_powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
-        __syncwarp();
         const long long trow = (long long)(int)nprb_a * p.MCS;
-        bool pass = false;
-        if (lane <= p.mcs_max && A.t.la_tbs[CK(trow + lane, NLA, 9)] > 0) {
-          const int m = lane;
-          const float eff = fa(eesm_db(d_x + ta, NP, s_lw, won_a, S, s_beta[m], lnw_a), off_a);
+        int chosen = -1;
+#pragma unroll 1
+        for (int m = p.mcs_max; m >= 0; --m) {
+          if (A.t.la_tbs[CK(trow + m, NLA, 9)] <= 0) continue;
+          const float beta = s_beta[m];
+          const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
+          const float mx = warp_max(x);
+          const float m0 = isinf(mx) ? 0.0f : mx;
+          const float lse = fa(x_logf(ordered_sum(in ? x_expf(fs(x, m0)) : 0.0f, won_a)), m0);
+          const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
           const float tbler = fs(1.0f, x_powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
-          pass = tbler <= p.target;
+          if (tbler <= p.target) {   // the same value on every lane: a warp-uniform exit
+            chosen = m;
+            break;
+          }
         }
-        const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
         if (lane == a) {
-          mcs_new = pm ? 31 - __clz(pm) : 0;
+          mcs_new = chosen < 0 ? 0 : chosen;
           tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
         }
-        __syncwarp();
       }
     }
     long long cap_b = tbs_new / 8 - p.tb_oh;
