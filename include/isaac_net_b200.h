@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 2
+#define INB_ABI_VERSION 3
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
 #define INB_MAX_F 64      /* frame slots per robot */
@@ -142,6 +142,8 @@ typedef struct {
   float *gain;                  /* scratch [n_ul + 1, E*R, S] float32 (n_ul = UL rows of the step): row 0 = the CSI
                                    before the step, row u + 1 = the fading gain (dB) of the u-th UL row */
   int64_t gain_cap;             /* elements available at `gain` */
+  const int64_t *o_base;        /* if set, every pointer in `o` is a byte offset from the address stored here (so a
+                                   captured CUDA graph can write each step's outputs into a new block) */
 } InbStepArgs;
 
 /* One control step of the NR uplink engine: the fading, MAC and finish launches, on `cuda_stream`. */
@@ -218,6 +220,10 @@ typedef struct {
   double *dline;
 } InbTrafficArgs;
 int inb_traffic_step(const InbTrafficArgs *args, void *cuda_stream);
+
+/* Store two int64 values at dst[0], dst[1] in stream order (e.g. the control step and the output block address that
+ * a captured step reads through T_dev / o_base). */
+int inb_store2(int64_t *dst, int64_t v0, int64_t v1, void *cuda_stream);
 
 /* ABI version of the loaded library (INB_ABI_VERSION). */
 int inb_abi_version(void);

@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 2
+ABI_VERSION = 3
 MAX_ROWS = 64
 NCTR = 64
 CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
@@ -72,7 +72,7 @@ class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
                 ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
-                ("trace", P), ("gain", P), ("gain_cap", i64)]
+                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P)]
 
 
 class InbResetArgs(ctypes.Structure):
@@ -102,7 +102,7 @@ class InbTrafficArgs(ctypes.Structure):
 
 
 EXPORTS = ("inb_nr_step", "inb_nr_step_noalloc", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step",
-           "inb_abi_version")
+           "inb_store2", "inb_abi_version")
 NOALLOC_GAIN_MAX = 1 << 25
 _lib = None
 
@@ -128,6 +128,8 @@ def lib():
     L.inb_nr_reset.argtypes = [ctypes.POINTER(InbResetArgs), P]
     L.inb_rng_draw.restype = ctypes.c_int
     L.inb_rng_draw.argtypes = [i32, i32, u32, u32, u32, P, P, P, i32, P, P]
+    L.inb_store2.restype = ctypes.c_int
+    L.inb_store2.argtypes = [P, i64, i64, P]
     L.inb_traffic_step.restype = ctypes.c_int
     L.inb_traffic_step.argtypes = [ctypes.POINTER(InbTrafficArgs), P]
     _lib = L

@@ -68,4 +68,10 @@ __device__ __forceinline__ float normal_at(uint32_t base, uint32_t i, float two_
   return fm(sqrtf(fm(-2.0f, logf(u1))), cosf(fm(two_pi, u2)));
 }
 
+// an output pointer of InbOutputs: absolute, or a byte offset from the block address `base` (InbStepArgs.o_base)
+template <typename T>
+__device__ __forceinline__ T* out_ptr(T* p, long long base) {
+  return reinterpret_cast<T*>(reinterpret_cast<char*>(p) + base);
+}
+
 }  // namespace inb

@@ -69,7 +69,15 @@ template <int FW, int FPL>                     // lanes per robot, frames per la
 __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) {
   const InbParams& p = A.p;
   const InbState& st = A.s;
-  const InbOutputs& o = A.o;
+  const long long ob = A.o_base != nullptr ? *A.o_base : 0;
+  InbOutputs o;   // the output pointers of this step
+  o.delivered = out_ptr(A.o.delivered, ob); o.timed_out = out_ptr(A.o.timed_out, ob);
+  o.dropped = out_ptr(A.o.dropped, ob); o.deadline_miss = out_ptr(A.o.deadline_miss, ob);
+  o.cap = out_ptr(A.o.cap, ob); o.cls = out_ptr(A.o.cls, ob); o.arrival_slot = out_ptr(A.o.arrival_slot, ob);
+  o.tag = out_ptr(A.o.tag, ob); o.priority = out_ptr(A.o.priority, ob); o.bytes = out_ptr(A.o.bytes, ob);
+  o.delay = out_ptr(A.o.delay, ob); o.arrival = out_ptr(A.o.arrival, ob); o.newest = out_ptr(A.o.newest, ob);
+  o.queue_len = out_ptr(A.o.queue_len, ob); o.queue_bytes = out_ptr(A.o.queue_bytes, ob);
+  o.det_env = out_ptr(A.o.det_env, ob);
   const int R = p.R, F = p.F, P = p.P;
   const long long e = blockIdx.x;
   const int seg = threadIdx.x / FW, l = threadIdx.x % FW;

@@ -94,4 +94,17 @@ extern "C" int inb_nr_step_noalloc(const InbStepArgs* args, void* cuda_stream) {
   return inb::launch_all(a, (cudaStream_t)cuda_stream);
 }
 
+namespace inb {
+__global__ void store2_kernel(int64_t* dst, int64_t v0, int64_t v1) {
+  dst[0] = v0;
+  dst[1] = v1;
+}
+}  // namespace inb
+
+extern "C" int inb_store2(int64_t* dst, int64_t v0, int64_t v1, void* cuda_stream) {
+  if (dst == nullptr) return -1;
+  inb::store2_kernel<<<1, 1, 0, (cudaStream_t)cuda_stream>>>(dst, v0, v1);
+  return cudaGetLastError() == cudaSuccess ? 0 : -100;
+}
+
 extern "C" int inb_abi_version(void) { return INB_ABI_VERSION; }

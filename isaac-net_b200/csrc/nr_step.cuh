@@ -807,10 +807,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   if (M > 0) enq = full_enq;
   if (act) {
     const InbOutputs& o = A.o;
-    o.sinr_db[CK(er, NER, 1)] = sinr_obs;
-    if (o.pathgain) o.pathgain[CK(er, NER, 1)] = pg;
-    o.gen_accepted[CK(er, NER, 1)] = n_acc;
-    o.gen_bytes[CK(er, NER, 1)] = full_enq - n0;
+    const long long ob = A.o_base != nullptr ? *A.o_base : 0;
+    out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
+    if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
+    out_ptr(o.gen_accepted, ob)[CK(er, NER, 1)] = n_acc;
+    out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
   }

@@ -139,7 +139,9 @@ class NRB200Engine:
         self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ()))
         self._graphs = {}
         self._pool = None
-        self._T_dev = torch.zeros((), dtype=torch.long, device=dev)
+        # a captured step reads its control step and the address of its output block from here (inb_store2)
+        self._ctl = torch.zeros(2, dtype=torch.long, device=dev)
+        self._T_dev = self._ctl[0]
         self._pos_buf = None
         self._steps_done = 0
         self._args = nat.InbStepArgs()
@@ -601,10 +603,16 @@ class NRB200Engine:
             p.rows[k][0], p.rows[k][1], p.rows[k][2], p.rows[k][3] = r4
             p.rowf[k][0], p.rowf[k][1] = f2
         p.T, p.s0 = 0, self.s0
-        a.T_dev = self._T_dev.data_ptr()
+        a.T_dev = self._ctl.data_ptr()
         a.pos, a.pathgain_in, a.ul_ref_in, a.trace = self._pos_buf.data_ptr(), None, None, None
-        out, o = self._alloc_outputs()
+        # output pointers as offsets from the block address stored at _ctl[1] (never 0: a null pointer means "absent")
+        if getattr(self, "_lay", None) is None:
+            self._lay = self._out_layout(0)
+        o = nat.InbOutputs()
+        for n, dt, shape, off, nb in self._lay[0]:
+            setattr(o, n, self._OFF + off)
         a.o = o
+        a.o_base = self._ctl.data_ptr() + 8
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
@@ -621,13 +629,11 @@ class NRB200Engine:
             else:
                 p.M = 0
             nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
-        ent = {"graph": g, "args": a, "out": out, "arr": arr, "blob": self._blob_of(out)}
+        ent = {"graph": g, "args": a, "arr": arr}
         self._graphs[key] = ent
         return ent
 
-    def _blob_of(self, out):
-        """The storage behind the output views (one allocation, copied in one piece after a replay)."""
-        return out[self._lay[0][0][0]].untyped_storage()
+    _OFF = 256   # bias of the offset-form output pointers
 
     def _graph_step(self, T, x):
         cfg, E, R = self.config, self.E, self.R
@@ -635,18 +641,18 @@ class NRB200Engine:
             self._pos_buf = torch.empty(E, R, 2, dtype=torch.float32, device=self.dev)
         rows, rowf, n_ul = self._rows(T * self.N)
         key = self._rows_key
-        self._pos_buf.copy_(x[..., :2], non_blocking=True)
-        self._T_dev.fill_(T)
         ent = self._graphs.get(key)
         if ent is None:
             ent = self._capture(key, rows, rowf)
+        # a new output block for this step (the caller owns fresh tensors); the graph writes into it through _ctl[1]
+        spec, total = self._lay
+        blob = torch.empty(total, dtype=torch.uint8, device=self.dev)
+        self._pos_buf.copy_(x[..., :2], non_blocking=True)
+        nat.check(self.L.inb_store2(self._ctl.data_ptr(), T, blob.data_ptr() - self._OFF, self._stream()),
+                  "inb_store2")
         ent["graph"].replay()
         self._steps_done += 1
         self.last_arrivals = ent["arr"]
-        # one copy of the static output block, then views of the copy (the caller owns fresh tensors)
-        spec, total = self._lay
-        src = torch.empty(0, dtype=torch.uint8, device=self.dev).set_(ent["blob"], 0, (total,), (1,))
-        blob = src.clone()
         out = {n: blob[off:off + nb].view(dt).view(shape) for n, dt, shape, off, nb in spec}
         self.prb_avail += float(cfg.nprb) * E * n_ul
         self.T = T + 1
