@@ -4,8 +4,10 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N ...
 
-One step = one control step of the engine over its whole batch: traffic generation, the fused kernel (enqueue and
-arrival gate, radio, the K = 10 slots, finish) and the step dict, through the public API (engine.step).  The default
+One step = one control step of the engine over its whole batch, through the public API (engine.step), replayed as a
+CUDA graph of 5 launches: the control words (inb_store2), traffic arrivals (traffic.cu), AR(1) fading (nr_fading.cu),
+the MAC kernel (enqueue and arrival gate, radio, the K = 10 slots; nr_step.cuh) and the frame-parallel finish
+(nr_finish.cu), which writes the step dict into a fresh output block.  The default
 workload is BASELINE config 2 (4096 envs x 32 robots, 100 MHz / 18 RBGs, PF, Rician K = 5 dB, mixed periodic +
 Poisson traffic) per GPU; with N GPUs every rank runs its own 4096-env shard (global env ids rank * 4096 + i, no
 collective inside the step), so per-GPU work is fixed ("scaling": "weak").
@@ -14,9 +16,11 @@ collective inside the step), so per-GPU work is fixed ("scaling": "weak").
           with CUDA events, max over ranks;
   e2e     the same through the public API from pinned host memory: every step copies its poses host -> device and
           reads the per-robot observations (newest, queue_len, queue_bytes, sinr_db) back device -> host;
-  roofline  algorithmic bytes of one fused launch (every per-robot state field read and written once at the
-          reference's widths, the step-dict outputs and the pose input: 6680 B per robot for config 2) / its average
-          duration (CUDA events on the launching stream), against the measured HBM copy bandwidth;
+  roofline  algorithmic bytes of one step (every per-robot state field read and written once at the reference's
+          widths, the step-dict outputs and the pose input: 6680 B per robot for config 2) / the average duration of
+          the step's four kernels (traffic, fading, MAC, finish: CUDA events around them on their stream, eager
+          launches), against the measured HBM copy bandwidth; traffic = DRAM bytes of those four kernels per step
+          from an ncu capture (profiles/nr_step_traffic.json);
   cpu_baseline  the oracle port (oracle/nr_oracle.py, torch on the host cores, the reference's own op sequence) on a
           bounded sample of the same workload.
 The state of one step is ~0.9 GB for config 2, larger than the 126 MB L2, so no L2 flush is needed between steps.
@@ -157,8 +161,15 @@ def wl_id(wl):
     return int(wl.name[3])
 
 
+def arm_config(wl, cfg, world):
+    return {"workload": wl.name, "envs_per_gpu": wl.E, "robots": wl.R, "slots_per_step": cfg.slots_per_step,
+            "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
+            "parallelism": f"env shards x{world}", "l2": "state > L2 (no flush needed)"}
+
+
 def run_reference(a):
-    """--impl reference: the reference's CPU path (the oracle port) on the host cores, rank 0 only."""
+    """--impl reference: the reference's CPU path (the oracle port, the reference's own op sequence) on all host
+    cores, rank 0 only; each step is a bounded sample of the workload's envs, sized so K steps take ~1-2 minutes."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -166,12 +177,13 @@ def run_reference(a):
     wl = presets.workload(a.workload)
     cfg = wl.config()
     steps = max(1, a.steps)
-    res = cpu_baseline(wl, cfg, a.cpu_envs, steps, warm=max(1, min(a.warmup, 2)))
+    envs = max(16, min(a.cpu_envs, (a.cpu_envs * 200 // steps) // 16 * 16))
+    res = cpu_baseline(wl, cfg, envs, steps, warm=max(1, min(a.warmup, 2)))
     v = res["value"]
     line = {"metric": "env-steps/sec", "value": v, "unit": "env-steps/s", "n_gpus": a.gpus, "steps": steps,
-            "warmup": a.warmup, "ms_per_step": a.cpu_envs / v * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-            "config": {"workload": wl.name, "envs": a.cpu_envs, "robots": wl.R, "parallelism": "host cores"},
+            "warmup": a.warmup, "ms_per_step": envs / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
+            "impl": "reference", "config": arm_config(wl, cfg, a.gpus),
             "cpu_baseline": res, "e2e": {"value": v, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -245,7 +257,7 @@ def main():
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1)
-    # duration of the fused launch alone: CUDA events around it on its stream (eager launches, same kernel)
+    # duration of the step's kernels alone: CUDA events around them on their stream (eager launches, same kernels)
     nk = min(a.steps, 20)
     for i in range(nk):
         eng._kernel_events = kev[i]
@@ -262,6 +274,7 @@ def main():
     total_envs = E * world
     value = total_envs * a.steps / (t_ms / 1e3)
     e2e = total_envs * a.steps / (e2e_ms / 1e3)
+    launches = 4 + (1 if eng.dtraffic is not None else 0)   # per graph step: store2, [traffic], fading, MAC, finish
     peak, peak_kind = peaks()
     per_launch = b_env(cfg, R) * E
     achieved = per_launch / (k_ms / 1e3) / 1e9
@@ -276,13 +289,12 @@ def main():
     line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
-            "config": {"workload": wl.name, "envs_per_gpu": E, "robots": R, "slots_per_step": cfg.slots_per_step,
-                       "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
-                       "parallelism": f"env shards x{world}", "l2": "state > L2 (no flush needed)"},
+            "config": arm_config(wl, cfg, world),
             "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": a.steps,
+            "gpu_launches": a.steps * launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
+                         "kernel": "traffic + fading + MAC + finish kernels of one step",
                          "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
             "clocks": clk}
     if rank == 0 and world == 1 and not a.no_cpu:

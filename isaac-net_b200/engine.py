@@ -508,30 +508,6 @@ class NRB200Engine:
             return self._graph_step(T, x)
         self._steps_done += 1
         keep = []                                   # tensors whose pointers the launch reads
-        gen = None
-        if self.traffic is not None:
-            if _arrivals is not None:
-                arr = _arrivals
-            elif self.dtraffic is not None:
-                arr = self.dtraffic.step()
-            else:
-                arr = self.traffic.step(self.clock, triggers)
-            self.last_arrivals = arr
-            M = arr.valid.shape[-1]
-            if M > 64:
-                raise B200Unsupported(f"{M} traffic arrivals per robot per step (at most 64)")
-            fields = {"valid": arr.valid, "det": arr.det, "nbytes": arr.nbytes, "slot": arr.slot, "tag": arr.tag,
-                      "prio": arr.prio, "dline": arr.dline}
-            for n, v in fields.items():
-                v = v.contiguous()
-                keep.append(v)
-                setattr(a.a, n, v.data_ptr())
-            p.M = M
-            gen = arr
-        else:
-            p.M = 0
-            for n in nat.ARR_FIELDS:
-                setattr(a.a, n, None)
         # inputs
         a.pos = a.pathgain_in = a.ul_ref_in = None
         snr_out = None
@@ -566,9 +542,33 @@ class NRB200Engine:
         a.o = o
         tr = getattr(self, "trace_buf", None)
         a.trace = tr.data_ptr() if tr is not None else None
-        ev = getattr(self, "_kernel_events", None)      # optional (start, end) CUDA events around the launch
+        ev = getattr(self, "_kernel_events", None)      # optional (start, end) CUDA events around the launches
         if ev is not None:
             ev[0].record()
+        gen = None
+        if self.traffic is not None:
+            if _arrivals is not None:
+                arr = _arrivals
+            elif self.dtraffic is not None:
+                arr = self.dtraffic.step()
+            else:
+                arr = self.traffic.step(self.clock, triggers)
+            self.last_arrivals = arr
+            M = arr.valid.shape[-1]
+            if M > 64:
+                raise B200Unsupported(f"{M} traffic arrivals per robot per step (at most 64)")
+            fields = {"valid": arr.valid, "det": arr.det, "nbytes": arr.nbytes, "slot": arr.slot, "tag": arr.tag,
+                      "prio": arr.prio, "dline": arr.dline}
+            for n, v in fields.items():
+                v = v.contiguous()
+                keep.append(v)
+                setattr(a.a, n, v.data_ptr())
+            p.M = M
+            gen = arr
+        else:
+            p.M = 0
+            for n in nat.ARR_FIELDS:
+                setattr(a.a, n, None)
         nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
         if ev is not None:
             ev[1].record()
