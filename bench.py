@@ -161,6 +161,23 @@ def wl_id(wl):
     return int(wl.name[3])
 
 
+def shard_seed(seed, rank, cfg):
+    """Seed of shard `rank` (isaac_net/core/sharded.py:95-103): the common seed when every draw is keyed by global env
+    id, else (seed + rank * 0x9E3779B97F4A7C15) mod 2^62 (the traffic models draw from one generator per engine)."""
+    if cfg.traffic:
+        return (int(seed) + rank * 0x9E3779B97F4A7C15) % 2 ** 62
+    return int(seed)
+
+
+def max_over_ranks(vals, dist, dev):
+    """Element-wise max of a list of floats over all ranks (identity without a process group)."""
+    if dist is None:
+        return list(vals)
+    t = torch.tensor(list(vals), dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 def arm_config(wl, cfg, world):
     return {"workload": wl.name, "envs_per_gpu": wl.E, "robots": wl.R, "slots_per_step": cfg.slots_per_step,
             "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
@@ -210,10 +227,8 @@ def main():
     wl = presets.workload(a.workload)
     cfg = wl.config()
     E, R = wl.E, wl.R
-    eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
-    eng.set_env_offset(rank * E)
-    if rank:
-        eng.reset(None)                       # redraw every env under its global id
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
+    eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
     n_all = a.warmup + 2 * a.steps
     host_pos = torch.empty(n_all, E, R, 2, dtype=torch.float32).pin_memory()
@@ -267,10 +282,7 @@ def main():
     k_ms = sum(s.elapsed_time(e) for s, e in kev[:nk]) / nk
     h2d = E * R * 2 * 4
     d2h = sum(host_obs[k].numel() * host_obs[k].element_size() for k in obs_keys)
-    if dist is not None:
-        t = torch.tensor([t_ms, e2e_ms, k_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_ms, e2e_ms, k_ms = t.tolist()
+    t_ms, e2e_ms, k_ms = max_over_ranks([t_ms, e2e_ms, k_ms], dist, dev)
     total_envs = E * world
     value = total_envs * a.steps / (t_ms / 1e3)
     e2e = total_envs * a.steps / (e2e_ms / 1e3)

@@ -355,11 +355,19 @@ class NRB200Engine:
         self._last_hid.index_fill_(0, ids, 0)
         self._reset_radio(m)
 
-    def set_env_offset(self, offset):
-        """Key the counter RNG rows by global env id offset + i (a shard of a larger batch, sharded.py:61-77)."""
+    def set_env_offset(self, offset, redo_reset=True):
+        """Make this engine a shard of a larger batch: key the counter-RNG rows by global env id offset + i and redo
+        the initial reset under those keys with the episode counters rewound first, so every env stays in its first
+        episode and draws what it would draw in one unsharded engine (isaac_net/core/sharded.py:61-77;
+        CounterRNG.set_env_offset, proto/rng.py:103-109).  redo_reset=False only re-keys the rows."""
         offset = int(offset)
+        if offset == self.env_offset:
+            return
         self.env_id.add_(offset - self.env_offset)
         self.env_offset = offset
+        if redo_reset:
+            self.episode.sub_(1)
+            self.reset(None)
 
     # ------------------------------------------------------------------ clocks
     @property
