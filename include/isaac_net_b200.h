@@ -39,6 +39,7 @@ extern "C" {
 #define INB_MAX_M 64      /* traffic arrivals per robot per step */
 #define INB_MAX_MCS 32
 #define INB_MAX_ROWS 64   /* scheduled slots per control step */
+#define INB_MAX_KF 32     /* plane waves per shadowing field */
 #define INB_NCTR 64       /* per-env counter words (int64) */
 
 /* counter words of InbStepArgs.ctr (per env, int64), MacLink.ctr / ntx_hist / rv_tx / rv_fail (mac.py:116-126) */

@@ -371,6 +371,8 @@ class NRConfig:
             out.append(("blockage=True", "blockage is not built yet"))
         if self.los_source != "stochastic":
             out.append((f"los_source={self.los_source!r}", "geometric LOS sources are not built"))
+        if self.shadow_modes > 32:
+            out.append((f"shadow_modes={self.shadow_modes}", "at most 32 plane waves per shadowing field"))
         if self.frame_buffer > 64:
             out.append((f"frame_buffer={self.frame_buffer}", "at most 64 frames per robot"))
         if self.n_harq > 32:

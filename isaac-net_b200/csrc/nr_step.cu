@@ -19,7 +19,7 @@ static int check_args(const InbStepArgs& a, long long* gain_need) {
       p.F > INB_MAX_F || p.M < 0 || p.M > INB_MAX_M || p.MCS < 1 || p.MCS > INB_MAX_MCS || p.K_rows < 0 ||
       p.K_rows > INB_MAX_ROWS || p.max_tx < 1 || p.mcs_max < 0 || p.mcs_max >= p.MCS)
     return -2;
-  if (p.C_axis < 2 || p.G_axis < 2 || p.N < 1) return -3;
+  if (p.C_axis < 2 || p.G_axis < 2 || p.N < 1 || p.Kf < 0 || p.Kf > INB_MAX_KF) return -3;
   if (a.pos == nullptr && a.pathgain_in == nullptr) return -4;
   if (a.pos != nullptr && a.pathgain_in == nullptr && (a.t.fk == nullptr || a.t.fphi == nullptr || a.t.gnb == nullptr))
     return -5;

@@ -68,7 +68,51 @@ struct Grp {
       return x;
     }
   }
-  __device__ static bool any(bool v, SmemGroup* sm, int& par) { return max_u64(v ? 1ull : 0ull, sm, par) != 0ull; }
+  __device__ static unsigned gmask() {   // this lane's group within its warp (GW <= 32)
+    if constexpr (GW >= 32) {
+      return 0xFFFFFFFFu;
+    } else {
+      return ((1u << GW) - 1u) << ((threadIdx.x & 31) / GW * GW);
+    }
+  }
+  __device__ static bool any(bool v, SmemGroup* sm, int& par) {
+    if constexpr (GW > 32) {
+      return max_u64(v ? 1ull : 0ull, sm, par) != 0ull;
+    } else {
+      return (__ballot_sync(0xFFFFFFFFu, v) & gmask()) != 0u;
+    }
+  }
+  // the group's maximum of `key` (mx) and the lowest lane (robot index) holding it
+  __device__ static int argmax_u32(uint32_t key, uint32_t& mx, SmemGroup* sm, int& par) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (GW <= 32) {
+      uint32_t m = 0u;
+      if constexpr (GW == 32) {
+        m = __reduce_max_sync(0xFFFFFFFFu, key);
+      } else {
+#pragma unroll
+        for (int gq = 0; gq < 32 / GW; ++gq) {   // one full-warp reduction per group; each lane keeps its own
+          const uint32_t v = __reduce_max_sync(0xFFFFFFFFu, lane / GW == gq ? key : 0u);
+          if (lane / GW == gq) m = v;
+        }
+      }
+      const unsigned win = __ballot_sync(0xFFFFFFFFu, key == m) & gmask();
+      mx = m;
+      return __ffs(win) - 1 - (lane / GW * GW) % 32;
+    } else {
+      const int wid = threadIdx.x >> 5;
+      const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, key);
+      const int wl = __ffs(__ballot_sync(0xFFFFFFFFu, key == m)) - 1;
+      if (lane == 0) sm->red[par][wid] = ((unsigned long long)m << 32) | (unsigned)(255 - (wid * 32 + wl));
+      __syncthreads();
+      unsigned long long b = sm->red[par][0];
+#pragma unroll
+      for (int w = 1; w < GW / 32; ++w) b = sm->red[par][w] > b ? sm->red[par][w] : b;
+      par ^= 1;
+      mx = (uint32_t)(b >> 32);
+      return 255 - (int)(b & 0xFFu);
+    }
+  }
   // true on every lane of the warp (GW <= 32) or block (GW > 32) when some group there has two or more lanes with v
   __device__ static bool two_or_more_uniform(bool v) {
     if constexpr (GW > 32) {
@@ -91,14 +135,8 @@ struct Grp {
   }
 };
 
-// Out-of-line calls of CUDA's math functions: each appears once in the kernel instead of at every call site, which
-// keeps the (long, branchy) kernel within the instruction cache.  The results are the functions' own.
-static __device__ __noinline__ float x_powf(float a, float b) { return powf(a, b); }
-static __device__ __noinline__ float x_log10f(float a) { return log10f(a); }
-static __device__ __noinline__ float x_logf(float a) { return logf(a); }
-static __device__ __noinline__ float x_expf(float a) { return expf(a); }
-static __device__ __noinline__ float x_cosf(float a) { return cosf(a); }
-static __device__ __noinline__ float x_sqrtf(float a) { return sqrtf(a); }
+// Out-of-line IEEE divisions (each inline __fdiv_rn / __ddiv_rn carries its own ~2 KB slow path): one copy in the
+// kernel instead of one per call site keeps the (long, branchy) kernel within the instruction cache.
 static __device__ __noinline__ float x_fdv(float a, float b) { return fdv(a, b); }      // IEEE a / b
 static __device__ __noinline__ double x_ddv(double a, double b) { return ddv(a, b); }  // IEEE a / b
 
@@ -169,7 +207,7 @@ __device__ __forceinline__ void segment(long long tbs, float r32, float& cbs, fl
 // linear -> dB with the reference's NaN / inf mapping (phy.py:137-139)
 __device__ __forceinline__ float db_of(float lin) {
   if (isnan(lin)) return -30.0f;
-  float v = fm(10.0f, x_log10f(fmaxf(lin, 1e-6f)));
+  float v = fm(10.0f, log10f(fmaxf(lin, 1e-6f)));
   if (isnan(v)) return -30.0f;
   if (isinf(v)) return v > 0.0f ? 60.0f : -30.0f;
   return v;
@@ -182,9 +220,10 @@ __device__ __forceinline__ float db_of(float lin) {
 // warp-wide max (fmaxf: order-independent) and the sum of lane values over the set bits of `won` in ascending lane
 // order (the left-to-right RBG sum of the serial code; lanes outside `won` would add +0.0, which changes nothing)
 __device__ __forceinline__ float warp_max(float x) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xFFFFFFFFu, x, o));
-  return x;
+  // order-preserving keys (NaN ranks as -inf, which fmaxf would skip; no -0.0 reaches here: every x is a sum with a
+  // non-negative log(w) term), one warp reduction
+  const uint32_t k = __reduce_max_sync(0xFFFFFFFFu, fkey(isnan(x) ? -INFINITY : x));
+  return fkey_inv(k);
 }
 __device__ __forceinline__ float ordered_sum(float e, uint32_t won) {
   float acc = 0.0f;
@@ -244,6 +283,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   __shared__ float s_lw[INB_MAX_S], s_lw10[INB_MAX_S], s_w[INB_MAX_S];
   __shared__ float s_thr[INB_MAX_MCS], s_se[INB_MAX_MCS], s_beta[INB_MAX_MCS], s_rate[INB_MAX_MCS];
   __shared__ unsigned long long s_ctr[GW > 32 ? 1 : 128 / GW][INB_NCTR];
+  __shared__ float s_fld[GW > 32 ? 1 : 128 / GW][INB_MAX_KF][3];   // the env's plane waves: kx, ky, phi
   extern __shared__ float dyn[];   // [2 or 3][S][NP]: rate / -lin, PF metric, ref (optional)
   const int tid = threadIdx.x;
   const int gpb = GW > 32 ? 1 : 128 / GW;
@@ -274,6 +314,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   float* v_ref = d_ref + tid;
   unsigned long long* const sc = s_ctr[gi];
   for (int i = r; i < INB_NCTR; i += GW) sc[i] = 0ull;
+  if (A.pos != nullptr && A.pathgain_in == nullptr && e < p.E) {
+    for (int i = r; i < p.Kf * 3; i += GW) {
+      const long long fo = e * p.Kf + i / 3;
+      const int c = i % 3;
+      s_fld[gi][i / 3][c] = c < 2 ? A.t.fk[fo * 2 + c] : A.t.fphi[fo];
+    }
+  }
   const int lane = tid & 31;
   const int wbase = tid - lane;                      // thread index of lane 0 of this warp
   const bool ref_vec = A.ul_ref_in != nullptr;
@@ -318,6 +365,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   long long n_acc = 0;
   int cnt_q = 0;
   if (act) {
+#pragma unroll 8
     for (int f = 0; f < F; ++f) cnt_q += st.cap[CK(eF + f, NERF, 3)] >= 0 ? 1 : 0;
     for (int m = 0; m < M; ++m) {
       const long long em = er * M + m;
@@ -357,27 +405,28 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     } else if (A.pos != nullptr) {
       const float px = A.pos[CK(er * 2, NER * 2, 2)], py = A.pos[CK(er * 2 + 1, NER * 2, 2)];
       const float dx = fs(px, A.t.gnb[0]), dy = fs(py, A.t.gnb[1]);
-      const float d2 = fmaxf(x_sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
+      const float d2 = fmaxf(sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
       // shadowing: amp * sum_k cos(k . x + phi) (channels/fields.py:61-64), the field of (env, cell 0)
       float cs = 0.0f;
+#pragma unroll 4
       for (int k = 0; k < p.Kf; ++k) {
-        const long long fo = e * p.Kf + k;
-        const float arg = fa(fa(fm(px, A.t.fk[CK(fo * 2, NFK * 2, 8)]), fm(py, A.t.fk[CK(fo * 2 + 1, NFK * 2, 8)])), A.t.fphi[CK(fo, NFK, 8)]);
-        const float c = x_cosf(arg);
+        const float* f3 = s_fld[gi][k];
+        const float arg = fa(fa(fm(px, f3[0]), fm(py, f3[1])), f3[2]);
+        const float c = cosf(arg);
         cs = k == 0 ? c : fa(cs, c);
       }
       const float field = fm(p.amp, cs);
       if (p.radio_model <= 1) {
         // TR 38.901 UMi / UMa LOS path loss (channels/tr38901.py:148-170) + sigma_SF * unit field
-        const float d3 = x_sqrtf(fa(fm(d2, d2), p.hh2));
-        const float lg = x_log10f(d3);
+        const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
+        const float lg = log10f(d3);
         const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
                                        : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
         const float rx = fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
         pg = fs(rx, p.ue_tx);
       } else {
         // log-distance (radio.py:265-273)
-        const float pl = fa(p.pl_const, fm(p.pl_10n, x_log10f(d2)));
+        const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
         pg = fs(fs(fs(p.ue_tx, pl), field), p.ue_tx);
       }
     }
@@ -401,7 +450,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     float sum = 0.0f;
     for (int s = 0; s < S; ++s) sum = s == 0 ? REF(0) : fa(sum, REF(s));
     const float x = fm(fs(fm(sum, p.inv_S), p.phr_min), 0.1f);
-    const float nmp = fm((float)p.ref_prbs, x_powf(10.0f, x));
+    const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
     n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
   }
 
@@ -410,12 +459,17 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   const BlerGrid bgrid = {A.t.bler, p.C_axis, p.G_axis, p.MCS, p.s0_snr, p.inv_ds, A.status};
 
 
-  // first frame not yet finished (RLC scan start); frames are in stream order
+  // RLC scan start: the first frame neither lost nor finished, and its end byte (frames are in stream order, and
+  // within a step a frame's end never changes, so the cached end decides whether a slot can deliver anything)
   const int nvalid = cnt_q;
   int f_scan = 0;
-  if (act) {
+  long long end_scan = LLONG_MAX;
+  bool q_dirty = false;   // frames were marked lost in this slot: the scan start may move
+  auto rescan = [&]() {
     while (f_scan < nvalid && (st.lost[CK(eF + f_scan, NERF, 3)] != 0 || !isinf(st.fin[CK(eF + f_scan, NERF, 3)]))) ++f_scan;
-  }
+    end_scan = f_scan < nvalid ? st.end_[CK(eF + f_scan, NERF, 3)] : LLONG_MAX;
+  };
+  if (act) rescan();
 
   // ======================================================================= slot loop (nr_engine.py:656-667)
   for (int k = 0; k < p.K_rows; ++k) {
@@ -533,12 +587,15 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
-        const float mkey = want ? fa(METRIC(s), prio) : -1.0f;
-        const bool wr = lex && want && has_rx;
-        const unsigned long long key = ((unsigned long long)(wr ? 1u : 0u) << 40) |
-                                       ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
-        const unsigned long long mx = Grp<GW>::max_u64(key, sm, par);
-        const bool oh = (255 - (int)(mx & 0xFFull) == r) && (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f);
+        float mkey = want ? fa(METRIC(s), prio) : -1.0f;
+        if (lex) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
+          const bool wr = want && has_rx;
+          const bool any_wr = Grp<GW>::any(wr, sm, par);   // every lane takes part
+          if (any_wr && !wr) mkey = -1.0f;
+        }
+        uint32_t mx;
+        const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
+        const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f);
         if (oh) {
           won |= 1u << s;
           cnt += 1;
@@ -555,11 +612,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         for (int s = 0; s < S; ++s) {
           const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
           const float mkey = want ? METRIC(s) : -1.0f;
-          const unsigned long long key = ((unsigned long long)fkey(mkey) << 8) | (unsigned long long)(255 - r);
-          const unsigned long long mx = Grp<GW>::max_u64(key, sm, par);
+          uint32_t mx;
+          const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
           const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u, sm, par);
-          const bool oh = (255 - (int)(mx & 0xFFull) == r) &&
-                          (fkey_inv((uint32_t)((mx >> 8) & 0xFFFFFFFFull)) >= 0.0f) && av;
+          const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
           if (oh) {
             won |= 1u << s;
             cnt += 1;
@@ -592,7 +648,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    const float split = fm(10.0f, x_log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    const float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
     float lnw = 0.0f;
@@ -608,7 +664,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       // logsumexp of log(w) over the grant
       const float lmx = warp_max(in ? lw_l : -INFINITY);
       const float lm0 = isinf(lmx) ? 0.0f : lmx;
-      const float lnw_a = fa(x_logf(ordered_sum(in ? x_expf(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
+      const float lnw_a = fa(logf(ordered_sum(in ? expf(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
       if (lane == a) lnw = lnw_a;
       if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
         // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
@@ -623,7 +679,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const int s = lane;
           const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
           const float est_tx = fa(fs(refs, split_a), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
-          ng = -x_powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+          ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
         const long long trow = (long long)(int)nprb_a * p.MCS;
         int chosen = -1;
@@ -634,10 +690,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
           const float mx = warp_max(x);
           const float m0 = isinf(mx) ? 0.0f : mx;
-          const float lse = fa(x_logf(ordered_sum(in ? x_expf(fs(x, m0)) : 0.0f, won_a)), m0);
+          const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
           const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-          const float tbler = fs(1.0f, x_powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+          const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
           if (tbler <= p.target) {   // the same value on every lane: a warp-uniform exit
             chosen = m;
             break;
@@ -655,6 +711,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     // ---- bind the TB to its HARQ process (mac.py:406-423)
     const int p_tx = tx_rx ? rx_p : p_new;
     const long long hp = eP + p_tx;
+    const long long sent_before = sent;
     if (tx_new) {
       st.h_lo[CK(hp, NERP, 4)] = sent;
       st.h_hi[CK(hp, NERP, 4)] = sent + byt_new;
@@ -672,12 +729,19 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     bool ok = false, fail = false, exh = false;
     long long served = 0;
     int ntx = 0;
-    int mcs = 0;
-    long long tbs = 0;
-    if (tx) {
+    // the TB's HARQ fields: a new TB's from registers (just bound), a retransmission's from its process
+    int mcs = mcs_new;
+    long long tbs = tbs_new;
+    float comb0 = 0.0f;
+    long long lo_tx = sent_before, hi_tx = sent_before + byt_new;
+    if (tx_new) ntx = 1;
+    if (tx_rx) {
       mcs = (int)st.h_mcs[CK(hp, NERP, 4)];
       tbs = st.h_tbs[CK(hp, NERP, 4)];
       ntx = (int)st.h_ntx[CK(hp, NERP, 4)] + 1;
+      comb0 = st.h_comb[CK(hp, NERP, 4)];
+      lo_tx = st.h_lo[CK(hp, NERP, 4)];
+      hi_tx = st.h_hi[CK(hp, NERP, 4)];
     }
     // EESM SINR of the TB's MCS on this row's channel (PHY.eff_sinr, phy.py:311-321), one lane per RBG
     float eff_tx = 0.0f;
@@ -696,27 +760,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const int s = lane;
         const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
         const float a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
-        const float negl = -x_powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+        const float negl = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
         x = fa(x_fdv(negl, beta), s_lw[s]);
       }
       const float mx = warp_max(x);
       const float m0 = isinf(mx) ? 0.0f : mx;
-      const float lse = fa(x_logf(ordered_sum(in ? x_expf(fs(x, m0)) : 0.0f, won_a)), m0);
+      const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
       const float eff = db_of(fm(-beta, fs(lse, lnw_a)));
       if (lane == a) eff_tx = eff;
     }
     if (tx) {
       const float eff = eff_tx;
-      const float lin = x_powf(10.0f, fm(eff, 0.1f));
-      const float comb = p.comb_cc ? fa(st.h_comb[CK(hp, NERP, 4)], lin) : lin;
-      const float eff_used = fm(10.0f, x_log10f(clamp_min_t(comb, 1e-9f)));
+      const float lin = powf(10.0f, fm(eff, 0.1f));
+      const float comb = p.comb_cc ? fa(comb0, lin) : lin;
+      const float eff_used = fm(10.0f, log10f(clamp_min_t(comb, 1e-9f)));
       float cbs, ncb;
       segment(tbs, s_rate[mcs], cbs, ncb);
       int i0;
       float wi;
       cidx(p, cbs, i0, wi);
       const float b = bler_lookup(bgrid, mcs, eff_used, i0, wi);
-      const float p_err = fs(1.0f, x_powf(fs(1.0f, b), ncb));
+      const float p_err = fs(1.0f, powf(fs(1.0f, b), ncb));
       const float u = uniform_at(key_stream(kenv, (uint32_t)((SITE_BLER_UL << 16) | rel)), (uint32_t)r);
       ok = u >= p_err;
       fail = !ok;
@@ -730,7 +794,6 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       st.h_ntx[CK(hp, NERP, 4)] = ntx;
       st.h_comb[CK(hp, NERP, 4)] = comb;
       if (fail) st.h_ready[CK(hp, NERP, 4)] = g + p.ul_rtt;
-      const long long lo_tx = st.h_lo[CK(hp, NERP, 4)], hi_tx = st.h_hi[CK(hp, NERP, 4)];
       if (exh) {
         if (!p.harq_drop) {
           st.h_ntx[CK(hp, NERP, 4)] = 0;
@@ -747,6 +810,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
               st.lost[CK(at, NERF, 3)] = 1;
             }
           }
+          q_dirty = true;
         }
       }
       served = ok ? hi_tx - lo_tx : 0;
@@ -787,18 +851,22 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (fail) atomicAdd(sc + INB_CTR_RV_FAIL + kx, 1ull);
     }
     // ---- RLC in-order delivery (mac.py:499-503): frames are in stream order, so the completed ones are a prefix
-    if (act) {
+    // the in-order pointer never passes `sent`, so a slot with end_scan > sent delivers nothing
+    if (act && (q_dirty || end_scan <= sent)) {
 #ifdef INB_CHECK
       CK(eP + P - 1, NERP, 12);
 #endif
-      const long long ack = ack_ptr(st, eP, pend, sent, floor_);
-      const double fin_val = da(da((double)T, x_ddv((double)(rel + 1), (double)p.N)), p.proc_off);
-      for (int f = f_scan; f < nvalid; ++f) {
-        const long long at = eF + f;
-        if (st.end_[CK(at, NERF, 3)] > ack) break;
-        if (!st.lost[CK(at, NERF, 3)] && isinf(st.fin[CK(at, NERF, 3)])) st.fin[CK(at, NERF, 3)] = fin_val;
+      const long long ack = end_scan <= sent ? ack_ptr(st, eP, pend, sent, floor_) : LLONG_MIN;
+      if (end_scan <= ack) {
+        const double fin_val = da(da((double)T, x_ddv((double)(rel + 1), (double)p.N)), p.proc_off);
+        for (int f = f_scan; f < nvalid; ++f) {
+          const long long at = eF + f;
+          if (st.end_[CK(at, NERF, 3)] > ack) break;
+          if (!st.lost[CK(at, NERF, 3)] && isinf(st.fin[CK(at, NERF, 3)])) st.fin[CK(at, NERF, 3)] = fin_val;
+        }
       }
-      while (f_scan < nvalid && (st.lost[CK(eF + f_scan, NERF, 3)] != 0 || !isinf(st.fin[CK(eF + f_scan, NERF, 3)]))) ++f_scan;
+      rescan();
+      q_dirty = false;
     }
   }
 
