@@ -25,7 +25,8 @@ import torch
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 
-# name: (workload id, E, R, steps, resets {step: env ids}, state snapshot every k steps, config overrides).
+# name: (workload id, E, R, steps, resets {step: env ids}, state snapshot every k steps, config overrides
+#        [, speed factor of the pose generator]).
 # The "s" cases stress the retransmission paths: a weak link (HARQ failures, exhaustion and RLC resends), short
 # deadlines (purged frames) and a small frame buffer (refused messages).
 CASES = {
@@ -35,6 +36,13 @@ CASES = {
     "1s": (1, 4, 16, 40, {20: [2]}, 1, dict(ue_tx_dbm=-12.0, timeout_steps=5, frame_buffer=8, max_harq_tx=2,
                                             rlc_retx_slots=7)),
     "2s": (2, 3, 32, 32, {11: [0]}, 2, dict(ue_tx_dbm=-8.0, n_harq=4, timeout_steps=6, frame_buffer=6)),
+    # several cells (config 3: 3 hex cells, log-distance shadowing, A3 handover, UL power control and inter-cell
+    # interference); "3s" makes handovers frequent (short TTT, low hysteresis and interruption) on weak links
+    "3": (3, 3, 64, 24, {10: [1]}, 2, {}),
+    "3s": (3, 3, 64, 24, {9: [2]}, 1, dict(a3_ttt_ms=2.0, a3_hyst_db=0.5, ho_interruption_ms=1.5, ue_tx_dbm=-6.0,
+                                            n_harq=4, max_harq_tx=3, frame_buffer=10, timeout_steps=8), 2000.0),
+    # a TTT of several control steps: A3 candidates carried across steps and fired inside a later one
+    "3t": (3, 2, 64, 24, {14: [0]}, 1, dict(a3_ttt_ms=47.5, a3_hyst_db=1.0, ho_interruption_ms=6.0), 800.0),
 }
 
 
@@ -88,6 +96,11 @@ def ref_state(eng):
             for nm in ("sf_los", "sf_nlos", "los_field"):
                 fld = getattr(ch, nm)
                 st[f"radio.{nm}.k"], st[f"radio.{nm}.phi"] = fld.k, fld.phi
+    if net.C > 1:
+        for n in ("serv", "pending", "a3_cand", "a3_cnt", "ho_end", "n_ho"):
+            st["assoc." + n] = getattr(net.assoc, n)
+        st["net.ni_ul"] = net.ni_ul
+        st["net.pg"] = net._pg
     for k, v in ul.ctr.items():
         st["ctr." + k] = v
     st["ctr.ntx_hist"], st["ctr.rv_tx"], st["ctr.rv_fail"] = ul.ntx_hist, ul.rv_tx, ul.rv_fail
@@ -95,7 +108,7 @@ def ref_state(eng):
     return {k: v.detach().cpu().clone().numpy() for k, v in st.items()}
 
 
-def run_case(i, E, R, steps, resets, every, over):
+def run_case(i, E, R, steps, resets, every, over, speed=1.0):
     from isaac_net import make_engine as ref_make
     b200 = importlib.import_module("isaac-net_b200")
     presets = importlib.import_module("isaac-net_b200.presets")
@@ -111,6 +124,7 @@ def run_case(i, E, R, steps, resets, every, over):
         return a
     eng.traffic.step = grab
     mot = presets.Motion(i, E, R, seed=wl.seed, step_ms=cfg.control_step_ms)
+    mot.speed = mot.speed * speed
     rec = {"E": np.int64(E), "R": np.int64(R), "steps": np.int64(steps), "workload": np.int64(i)}
     st0 = ref_state(eng)
     for k, v in st0.items():
@@ -147,7 +161,7 @@ def main():
     torch.set_num_threads(8)
     for c in a.cases.split(","):
         rec = run_case(*CASES[c])
-        rec["overrides"] = np.array(repr(CASES[c][-1]))
+        rec["overrides"] = np.array(repr(CASES[c][6]))
         path = os.path.join(HERE, f"cfg{c}.npz")
         np.savez_compressed(path, **rec)
         print(path, os.path.getsize(path))
