@@ -32,7 +32,8 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 3
+#define INB_ABI_VERSION 4
+#define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
 #define INB_MAX_F 64      /* frame slots per robot */
@@ -49,18 +50,24 @@ enum {
   INB_CTR_NTX_HIST = 16, INB_CTR_RV_TX = 32, INB_CTR_RV_FAIL = 48
 };
 
-/* Per-robot state, reference layouts and dtypes ([E,R], [E,R,S], [E,R,P], [E,R,F]); bool = uint8. */
+/* Per-robot state, reference layouts and dtypes ([E,R], [E,R,S], [E,R,P], [E,R,F]); bool = uint8.  With C > 1 cells
+ * the fading state and the Rician phasor have a cell axis after R ([E,R,C,S,2], [E,R,C,2], [E,R,C]). */
 typedef struct {
   int64_t *sent, *floor_, *bsr, *sr_t, *last_tx, *enq;     /* [E,R] */
   float *olla, *avg;                                       /* [E,R] */
   float *csi;                                              /* [E,R,S] */
-  float *h;                                                /* [E,R,S,2] AR(1) fading state */
-  float *spec, *k_lin;                                     /* Rician: [E,R,2] phasor, [E,R] K (NULL: Rayleigh) */
+  float *h;                                                /* [E,R,(C,)S,2] AR(1) fading state */
+  float *spec, *k_lin;                                     /* Rician: [E,R,(C,)2] phasor, [E,R,(C)] K (NULL: Rayleigh) */
   int64_t *h_state, *h_lo, *h_hi, *h_ready, *h_ntx, *h_mcs, *h_tbs, *h_nsb;   /* [E,R,P] */
   float *h_comb;                                           /* [E,R,P] */
   int64_t *cap, *start, *end_, *cls, *hid, *tag, *prio;    /* [E,R,F] */
   uint8_t *lost, *det;                                     /* [E,R,F] */
   double *fin, *off, *dline;                               /* [E,R,F] */
+  /* several cells (NULL with one): CellAssociation (serving cell, A3 candidate and its count in slots, end slot of
+   * the handover interruption, handovers), initial association pending per env, the gNBs' N+I per PRB (mW) */
+  int64_t *serv, *a3_cand, *a3_cnt, *ho_end, *n_ho;        /* [E,R] */
+  uint8_t *pending;                                        /* [E] */
+  float *ni_ul;                                            /* [E,C,S] */
 } InbState;
 
 /* Step outputs (the step dict of NREngine.step), [E,R,F] unless noted. */
@@ -70,8 +77,10 @@ typedef struct {
   float *delay;
   double *arrival;
   int64_t *newest, *queue_len, *gen_accepted, *gen_bytes;  /* [E,R] */
-  float *queue_bytes, *sinr_db, *pathgain;                 /* [E,R] */
+  float *queue_bytes, *sinr_db;                            /* [E,R] */
+  float *pathgain;                                         /* [E,R,C] path gain of every link (dB) */
   uint8_t *det_env;                                        /* [E] */
+  int64_t *serving_cell;                                   /* [E,R] (NULL with one cell) */
 } InbOutputs;
 
 /* Traffic arrivals of this step [E,R,M] (TrafficGen.step, sorted by slot), or M = 0. */
@@ -119,6 +128,16 @@ typedef struct {
   int32_t radio_model;
   float h_bs, h_ut, dbp, fc_term, pl_a, pl_n1, pl_b_term, sigma_sf, amp, hh2;
   float pl_const, pl_10n;
+  /* several cells (C = 1: unused) */
+  int32_t C;                    /* cells */
+  int32_t ttt, ho_int;          /* A3 time-to-trigger and handover interruption, slots */
+  int32_t has_floor, ho_flush, pc_on;
+  float a3_off, a3_hyst, floor_rx;   /* A3: best > (serving + offset) + hysteresis [and best >= floor_rx] */
+  float noise_mw;               /* noise per PRB at a gNB (mW, float32) */
+  float ue_tx_ref;              /* float32(ue_tx_dbm - 10 log10(snr_ref_prbs)) (float64 on the host, as python) */
+  float ref_db;                 /* 10 log10(snr_ref_prbs) */
+  float pc_p0, pc_alpha;        /* fractional UL power control: backoff = ue_tx - (P0 + alpha (ue_tx - RSRP)) */
+  float li_alpha, li_beta;      /* N+I filter: ni = alpha ni_now + beta ni (beta = float32(1 - alpha)) */
 } InbParams;
 
 typedef struct {
@@ -140,8 +159,9 @@ typedef struct {
   int64_t *trace;               /* optional per-slot trace [K_rows, E, R, 8] (NULL = off): bsr after the SR grant,
                                    need, won RBG mask, new-TB MCS, flags (has_rx | new_el << 1 | tx_rx << 2 |
                                    tx_new << 3 | ok << 4), send pointer after the slot, PHR cap, bits of `left` */
-  float *gain;                  /* scratch [n_ul + 1, E*R, S] float32 (n_ul = UL rows of the step): row 0 = the CSI
-                                   before the step, row u + 1 = the fading gain (dB) of the u-th UL row */
+  float *gain;                  /* scratch float32 (n_ul = UL rows of the step): one cell [n_ul + 1, E*R, S], row 0 =
+                                   the CSI before the step, row u + 1 = the fading gain (dB) of the u-th UL row;
+                                   C > 1 cells [n_ul, E*R, C, S], row u = the gain of every link in UL row u */
   int64_t gain_cap;             /* elements available at `gain` */
   const int64_t *o_base;        /* if set, every pointer in `o` is a byte offset from the address stored here (so a
                                    captured CUDA graph can write each step's outputs into a new block) */
@@ -153,7 +173,7 @@ int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array
  * inside the library (INB_NOALLOC_GAIN_MAX float32 elements per device), so `gain` / `gain_cap` are ignored and
  * nothing is allocated at call time.  No counterpart in the reference (its torch backends allocate per call).
- *   -7: (UL rows + 1) x S x E x R exceeds INB_NOALLOC_GAIN_MAX (use inb_nr_step with a caller buffer);
+ *   -10: the step's gain rows exceed INB_NOALLOC_GAIN_MAX (use inb_nr_step with a caller buffer);
  *   -8 / -9: no current CUDA device / the array's device address could not be resolved.
  * The array's address is resolved on the first call on each device: make that call before capturing a CUDA graph.
  * The array needs no initial value (each step writes every row it reads), but all calls on one device share it, so
@@ -162,7 +182,8 @@ int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 int inb_nr_step_noalloc(const InbStepArgs *args, void *cuda_stream);
 
 /* Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial
- * values, fading state h = N(0,1)/sqrt(2) draws (site H0), Rician phasor (site KPHI) and K. */
+ * values, fading state h = N(0,1)/sqrt(2) draws (site H0, element ((r C + c) S + s) 2 + re/im), Rician phasor (site
+ * KPHI, element r C + c) and K; with C > 1 cells also the association (pending for the next step) and N+I. */
 typedef struct {
   int32_t E, R, S, P, F;
   uint32_t s0;
@@ -172,6 +193,8 @@ typedef struct {
   const int64_t *env_id;
   int64_t *episode, *rng_ctr;
   InbState s;
+  int32_t C;                    /* cells: the fading / Rician state has a cell axis when C > 1 */
+  float noise_mw;               /* initial N+I per PRB at each gNB (C > 1) */
 } InbResetArgs;
 int inb_nr_reset(const InbResetArgs *args, void *cuda_stream);
 

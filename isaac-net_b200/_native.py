@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 3
+ABI_VERSION = 4
 MAX_ROWS = 64
 NCTR = 64
 CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
@@ -24,10 +24,11 @@ i32, i64, u32, f32, f64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctype
 
 STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg", "csi", "h", "spec", "k_lin",
                 "h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb", "cap", "start",
-                "end_", "cls", "hid", "tag", "prio", "lost", "det", "fin", "off", "dline")
+                "end_", "cls", "hid", "tag", "prio", "lost", "det", "fin", "off", "dline", "serv", "a3_cand", "a3_cnt",
+                "ho_end", "n_ho", "pending", "ni_ul")
 OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
               "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
-              "sinr_db", "pathgain", "det_env")
+              "sinr_db", "pathgain", "det_env", "serving_cell")
 ARR_FIELDS = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
 TAB_FIELDS = ("bler", "thr_ref", "se", "beta", "rate", "w", "lw", "lw10", "la_tbs", "la_i0", "la_wi", "la_ncb", "fk",
               "fphi", "gnb")
@@ -65,7 +66,10 @@ class InbParams(ctypes.Structure):
                 + [("proc_off", f64), ("ctl_ms", f64), ("inv_N_d", f64), ("inv_ref_prbs", f32), ("radio_model", i32)]
                 + [(n, f32) for n in ("h_bs", "h_ut", "dbp", "fc_term", "pl_a", "pl_n1", "pl_b_term", "sigma_sf",
                                       "amp", "hh2")]
-                + [(n, f32) for n in ("pl_const", "pl_10n")])
+                + [(n, f32) for n in ("pl_const", "pl_10n")]
+                + [(n, i32) for n in ("C", "ttt", "ho_int", "has_floor", "ho_flush", "pc_on")]
+                + [(n, f32) for n in ("a3_off", "a3_hyst", "floor_rx", "noise_mw", "ue_tx_ref", "ref_db", "pc_p0",
+                                      "pc_alpha", "li_alpha", "li_beta")])
 
 
 class InbStepArgs(ctypes.Structure):
@@ -78,7 +82,8 @@ class InbStepArgs(ctypes.Structure):
 class InbResetArgs(ctypes.Structure):
     _fields_ = ([(n, i32) for n in ("E", "R", "S", "P", "F")] + [("s0", u32), ("rician", i32)]
                 + [(n, f32) for n in ("k_lin0", "inv_sqrt2", "two_pi")]
-                + [(n, P) for n in ("mask", "env_id", "episode", "rng_ctr")] + [("s", InbState)])
+                + [(n, P) for n in ("mask", "env_id", "episode", "rng_ctr")] + [("s", InbState)]
+                + [("C", i32), ("noise_mw", f32)])
 
 
 MAX_SRC = 8

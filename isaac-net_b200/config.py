@@ -359,8 +359,10 @@ class NRConfig:
             out.append(("discard='pdcp_arrival'", "PDCP arrival discard is not built"))
         if self.rician_mode == "los":
             out.append(("Rician K from the LOS state", "only a fixed rician_k_db is built"))
-        if self.n_cells > 1:
-            out.append((f"n_cells={self.n_cells}", "the multi-cell scheduler is not built yet"))
+        if self.n_cells > 3:
+            out.append((f"n_cells={self.n_cells}", "at most 3 cells (more need an ordered interference sum)"))
+        if self.n_cells > 1 and self.channel not in ("log_distance", "tr38901"):
+            out.append((f"channel={self.channel!r} with several cells", "several cells: log_distance or tr38901"))
         if self.channel == "tr38901" and self.tr38901_los == "stochastic":
             out.append(("tr38901_los='stochastic'", "the spatially consistent LOS state is not built"))
         if self.channel == "tr38901" and self.tr38901_scenario not in ("UMi", "UMa"):

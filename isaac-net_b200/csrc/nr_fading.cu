@@ -8,7 +8,9 @@
 // gain[u + 1][e R + r][s] and copies the CSI of the previous step into gain[0]; so the MAC kernel finds the CSI of
 // its u-th UL row in gain[u] and the row's fading gain in gain[u + 1], a robot's RBGs contiguous.  The new fading
 // state h [E,R,S,2] and the CSI state (the gain of the last UL row, the CSI report rule of MacLink, mac.py:485) are
-// written back in place.
+// written back in place.  With C > 1 cells every link (robot, cell) fades on its own (h [E,R,C,S,2], hash elements
+// ((r C + c) S + s) 2 + {0, 1}) and gain row u is the u-th UL row's gain of every link, [E R][C][S]; the CSI then
+// depends on the serving cell and its handovers, so the MAC kernel keeps it.
 #include <cmath>
 #include <cstdint>
 
@@ -19,33 +21,39 @@ namespace inb {
 __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
   const InbParams& p = A.p;
   const long long NER = (long long)p.E * p.R;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (robot, RBG), RBGs fastest
+  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (robot, cell, RBG), RBGs fastest
   const int S = p.S;
-  const long long plane = NER * S;
+  const int C = p.C > 1 ? p.C : 1;
+  const long long plane = NER * C * S;
   if (t >= plane) return;
-  const long long er = t / S;
-  const int s = (int)(t - er * S);
+  const long long ec = t / S;                  // link (robot, cell)
+  const int s = (int)(t - ec * S);
+  const long long er = ec / C;
+  const int c = (int)(ec - er * C);
   const long long e = er / p.R;
   const int r = (int)(er - e * p.R);
   const InbState& st = A.s;
   const float2 h0 = reinterpret_cast<const float2*>(st.h)[t];
   float hr = h0.x, hi = h0.y;
   float* __restrict__ gout = A.gain + t;
-  float last = st.csi[t];
-  gout[0] = last;
+  float last = 0.0f;
+  if (C == 1) {
+    last = st.csi[t];
+    gout[0] = last;
+  }
   float ar_ = 0.0f, ai_ = 0.0f, kb = 1.0f;
   if (p.rician) {
     // |sqrt(K/(K+1)) e^{j phi} + sqrt(1/(K+1)) h|^2 (NRNet._gain, nr_engine.py:602-611)
-    const float k_lin = st.k_lin[er];
+    const float k_lin = st.k_lin[ec];
     const float kinv = fdv(1.0f, fa(k_lin, 1.0f));
     const float ka = sqrtf(fm(k_lin, kinv));
     kb = sqrtf(kinv);
-    ar_ = fm(ka, st.spec[er * 2]);
-    ai_ = fm(ka, st.spec[er * 2 + 1]);
+    ar_ = fm(ka, st.spec[ec * 2]);
+    ai_ = fm(ka, st.spec[ec * 2 + 1]);
   }
   const uint32_t kenv = key_env(p.s0, A.env_id[e], A.episode[e], CH_STEP, A.rng_ctr[e]);
   const float two_pi = 6.28318548202514648438f;
-  const uint32_t j = (uint32_t)((r * S + s) * 2);
+  const uint32_t j = (uint32_t)(((r * C + c) * S + s) * 2);
   int u = 0;
   for (int k = 0; k < p.K_rows; ++k) {
     const int rel = p.rows[k][0], uls = p.rows[k][1], fad = p.rows[k][3];
@@ -69,17 +77,18 @@ __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
         }
         g = fm(10.0f, log10f(clamp_min_t(pw, 1e-6f)));
       }
-      ++u;
+      if (C == 1) ++u;
       gout[(long long)u * plane] = g;
+      if (C > 1) ++u;
       last = g;
     }
   }
   if (p.fading) reinterpret_cast<float2*>(st.h)[t] = make_float2(hr, hi);
-  st.csi[t] = last;
+  if (C == 1) st.csi[t] = last;
 }
 
 cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream) {
-  const long long n = (long long)a.p.E * a.p.R * a.p.S;
+  const long long n = (long long)a.p.E * a.p.R * (a.p.C > 1 ? a.p.C : 1) * a.p.S;
   const int block = 256;
   nr_fading_kernel<<<(unsigned)((n + block - 1) / block), block, 0, stream>>>(a);
   return cudaGetLastError();

@@ -29,19 +29,33 @@ __global__ void nr_reset_kernel(const InbResetArgs A) {
   st.sent[er] = 0; st.floor_[er] = 0; st.bsr[er] = 0; st.sr_t[er] = -1; st.last_tx[er] = -1; st.enq[er] = 0;
   st.olla[er] = 0.0f; st.avg[er] = 100.0f;
   const uint32_t base_h = key_stream(kenv, (uint32_t)(SITE_H0 << 16));
-  for (int s = 0; s < S; ++s) {
-    st.csi[er * S + s] = 0.0f;
-    for (int c = 0; c < 2; ++c) {
-      uint32_t j = (uint32_t)((r * S + s) * 2 + c);
-      st.h[(er * S + s) * 2 + c] = fm(normal_at(base_h, j, A.two_pi), A.inv_sqrt2);
+  const int C = A.C > 1 ? A.C : 1;
+  for (int s = 0; s < S; ++s) st.csi[er * S + s] = 0.0f;
+  for (int c = 0; c < C; ++c) {
+    const long long ec = er * C + c;            // link (robot, cell)
+    for (int s = 0; s < S; ++s) {
+      for (int q = 0; q < 2; ++q) {
+        const uint32_t j = (uint32_t)(((r * C + c) * S + s) * 2 + q);
+        st.h[(ec * S + s) * 2 + q] = fm(normal_at(base_h, j, A.two_pi), A.inv_sqrt2);
+      }
     }
   }
   if (A.rician) {
     const uint32_t base_k = key_stream(kenv, (uint32_t)(SITE_KPHI << 16));
-    float phi = fm(A.two_pi, uniform_at(base_k, (uint32_t)r));
-    st.spec[er * 2] = cosf(phi);
-    st.spec[er * 2 + 1] = sinf(phi);
-    st.k_lin[er] = A.k_lin0;
+    for (int c = 0; c < C; ++c) {
+      const long long ec = er * C + c;
+      float phi = fm(A.two_pi, uniform_at(base_k, (uint32_t)(r * C + c)));
+      st.spec[ec * 2] = cosf(phi);
+      st.spec[ec * 2 + 1] = sinf(phi);
+      st.k_lin[ec] = A.k_lin0;
+    }
+  }
+  if (A.C > 1) {   // CellAssociation.reset (radio.py:391-396), NRNet._reset_cells (nr_engine.py:424-438)
+    st.serv[er] = 0; st.a3_cand[er] = -1; st.a3_cnt[er] = 0; st.ho_end[er] = 0; st.n_ho[er] = 0;
+    if (r == 0) {
+      st.pending[e] = 1;
+      for (int i = 0; i < A.C * S; ++i) st.ni_ul[e * A.C * S + i] = A.noise_mw;
+    }
   }
   for (int q = 0; q < P; ++q) {
     const long long at = er * P + q;

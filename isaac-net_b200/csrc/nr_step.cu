@@ -20,12 +20,16 @@ static int check_args(const InbStepArgs& a, long long* gain_need) {
       p.K_rows > INB_MAX_ROWS || p.max_tx < 1 || p.mcs_max < 0 || p.mcs_max >= p.MCS)
     return -2;
   if (p.C_axis < 2 || p.G_axis < 2 || p.N < 1 || p.Kf < 0 || p.Kf > INB_MAX_KF) return -3;
+  if (p.C > 1 && (p.C > INB_MAX_C || a.s.serv == nullptr || a.s.a3_cand == nullptr || a.s.a3_cnt == nullptr ||
+                  a.s.ho_end == nullptr || a.s.n_ho == nullptr || a.s.pending == nullptr || a.s.ni_ul == nullptr ||
+                  a.o.serving_cell == nullptr))
+    return -7;
   if (a.pos == nullptr && a.pathgain_in == nullptr) return -4;
   if (a.pos != nullptr && a.pathgain_in == nullptr && (a.t.fk == nullptr || a.t.fphi == nullptr || a.t.gnb == nullptr))
     return -5;
   int n_ul = 0;
   for (int k = 0; k < p.K_rows; ++k) n_ul += p.rows[k][1] > 0 ? 1 : 0;
-  *gain_need = (long long)(n_ul + 1) * p.S * p.E * p.R;
+  *gain_need = p.C > 1 ? (long long)n_ul * p.C * p.S * p.E * p.R : (long long)(n_ul + 1) * p.S * p.E * p.R;
   return 0;
 }
 
@@ -84,7 +88,7 @@ extern "C" int inb_nr_step_noalloc(const InbStepArgs* args, void* cuda_stream) {
   long long need = 0;
   const int rc = inb::check_args(*args, &need);
   if (rc != 0) return rc;
-  if (need > (long long)INB_NOALLOC_GAIN_MAX) return -7;
+  if (need > (long long)INB_NOALLOC_GAIN_MAX) return -10;
   float* scratch = nullptr;
   const int sr = inb::scratch_of_current_device(&scratch);
   if (sr != 0) return sr;

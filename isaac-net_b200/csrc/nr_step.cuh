@@ -33,6 +33,7 @@ struct SmemGroup {
   unsigned long long red[2][4];   // per-warp partial maxima (GW up to 128: 4 warps), double-buffered
   float rkey[128];
   int32_t rnsb[128];
+  int32_t rserv[128];
 };
 
 // float -> order-preserving u32 (non-NaN inputs)
@@ -112,6 +113,12 @@ struct Grp {
       mx = (uint32_t)(b >> 32);
       return 255 - (int)(b & 0xFFu);
     }
+  }
+  // as two_or_more_uniform, counting the lanes of each cell (cell index c < C) separately
+  __device__ static bool two_or_more_in_a_cell_uniform(bool v, int c, int C) {
+    bool multi = false;
+    for (int cc = 0; cc < C; ++cc) multi = two_or_more_uniform(v && c == cc) || multi;
+    return multi;
   }
   // true on every lane of the warp (GW <= 32) or block (GW > 32) when some group there has two or more lanes with v
   __device__ static bool two_or_more_uniform(bool v) {
@@ -273,7 +280,8 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 }
 
 // ------------------------------------------------------------------------------------------------ the step kernel
-template <int GW>
+// MC: several cells (A3 association and handover, per-cell schedulers, UL power control and interference)
+template <int GW, bool MC>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr int NT = GW > 32 ? GW : 128;
   constexpr int NP = NT + 1;   // row stride of the shared vectors: a warp reading one column across rows is
@@ -283,7 +291,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   __shared__ float s_lw[INB_MAX_S], s_lw10[INB_MAX_S], s_w[INB_MAX_S];
   __shared__ float s_thr[INB_MAX_MCS], s_se[INB_MAX_MCS], s_beta[INB_MAX_MCS], s_rate[INB_MAX_MCS];
   __shared__ unsigned long long s_ctr[GW > 32 ? 1 : 128 / GW][INB_NCTR];
-  __shared__ float s_fld[GW > 32 ? 1 : 128 / GW][INB_MAX_KF][3];   // the env's plane waves: kx, ky, phi
+  constexpr int NG = GW > 32 ? 1 : 128 / GW;   // groups (envs) per block
+  constexpr int NC = MC ? INB_MAX_C : 1;
+  __shared__ float s_fld[NG][NC][INB_MAX_KF][3];   // the env's plane waves per cell: kx, ky, phi
+  // several cells: per env, the gNBs' N+I per PRB (mW) and its dB value at the start of the slot, this slot's
+  // interference accumulator and N+I (dB)
+  __shared__ float s_ni[MC ? NG : 1][NC][MC ? INB_MAX_S : 1], s_nidb[MC ? NG : 1][NC][MC ? INB_MAX_S : 1];
+  __shared__ float s_if[MC ? NG : 1][NC][MC ? INB_MAX_S : 1], s_nadb[MC ? NG : 1][NC][MC ? INB_MAX_S : 1];
   extern __shared__ float dyn[];   // [2 or 3][S][NP]: rate / -lin, PF metric, ref (optional)
   const int tid = threadIdx.x;
   const int gpb = GW > 32 ? 1 : 128 / GW;
@@ -314,11 +328,20 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   float* v_ref = d_ref + tid;
   unsigned long long* const sc = s_ctr[gi];
   for (int i = r; i < INB_NCTR; i += GW) sc[i] = 0ull;
+  const int C = MC ? p.C : 1;
   if (A.pos != nullptr && A.pathgain_in == nullptr && e < p.E) {
-    for (int i = r; i < p.Kf * 3; i += GW) {
-      const long long fo = e * p.Kf + i / 3;
-      const int c = i % 3;
-      s_fld[gi][i / 3][c] = c < 2 ? A.t.fk[fo * 2 + c] : A.t.fphi[fo];
+    for (int i = r; i < C * p.Kf * 3; i += GW) {
+      const int cc = i / (p.Kf * 3), k = (i / 3) % p.Kf, q = i % 3;
+      const long long fo = ((long long)cc * p.E + e) * p.Kf + k;
+      s_fld[gi][cc][k][q] = q < 2 ? A.t.fk[fo * 2 + q] : A.t.fphi[fo];
+    }
+  }
+  if constexpr (MC) {
+    if (e < p.E) {
+      for (int i = r; i < C * S; i += GW) {
+        s_ni[gi][i / S][i % S] = A.s.ni_ul[e * C * S + i];
+        s_if[gi][i / S][i % S] = 0.0f;
+      }
     }
   }
   const int lane = tid & 31;
@@ -397,56 +420,116 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   const long long full_enq = enq;
   if (M > 0) enq = base;
 
-  // ---------------- large-scale radio: path gain of the serving link (one cell)
-  float pg = 0.0f;
+  // ---------------- large-scale radio: path gain of every link (one per cell)
+  float pg_c[NC];
+#pragma unroll
+  for (int cc = 0; cc < NC; ++cc) pg_c[cc] = 0.0f;
   if (act) {
     if (A.pathgain_in != nullptr) {
-      pg = A.pathgain_in[CK(er, NER, 1)];
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc)
+        if (cc < C) pg_c[cc] = A.pathgain_in[CK(er * C + cc, NER * C, 1)];
     } else if (A.pos != nullptr) {
       const float px = A.pos[CK(er * 2, NER * 2, 2)], py = A.pos[CK(er * 2 + 1, NER * 2, 2)];
-      const float dx = fs(px, A.t.gnb[0]), dy = fs(py, A.t.gnb[1]);
-      const float d2 = fmaxf(sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
-      // shadowing: amp * sum_k cos(k . x + phi) (channels/fields.py:61-64), the field of (env, cell 0)
-      float cs = 0.0f;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        const float dx = fs(px, A.t.gnb[cc * 2]), dy = fs(py, A.t.gnb[cc * 2 + 1]);
+        const float d2 = fmaxf(sqrtf(fa(fm(dx, dx), fm(dy, dy))), 1.0f);
+        // shadowing: amp * sum_k cos(k . x + phi) (channels/fields.py:61-64), the field of (env, cell)
+        float cs = 0.0f;
 #pragma unroll 4
-      for (int k = 0; k < p.Kf; ++k) {
-        const float* f3 = s_fld[gi][k];
-        const float arg = fa(fa(fm(px, f3[0]), fm(py, f3[1])), f3[2]);
-        const float c = cosf(arg);
-        cs = k == 0 ? c : fa(cs, c);
-      }
-      const float field = fm(p.amp, cs);
-      if (p.radio_model <= 1) {
-        // TR 38.901 UMi / UMa LOS path loss (channels/tr38901.py:148-170) + sigma_SF * unit field
-        const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
-        const float lg = log10f(d3);
-        const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
-                                       : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
-        const float rx = fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
-        pg = fs(rx, p.ue_tx);
-      } else {
-        // log-distance (radio.py:265-273)
-        const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
-        pg = fs(fs(fs(p.ue_tx, pl), field), p.ue_tx);
+        for (int k = 0; k < p.Kf; ++k) {
+          const float* f3 = s_fld[gi][cc][k];
+          const float arg = fa(fa(fm(px, f3[0]), fm(py, f3[1])), f3[2]);
+          const float cv = cosf(arg);
+          cs = k == 0 ? cv : fa(cs, cv);
+        }
+        const float field = fm(p.amp, cs);
+        if (p.radio_model <= 1) {
+          // TR 38.901 UMi / UMa LOS path loss (channels/tr38901.py:148-170) + sigma_SF * unit field
+          const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
+          const float lg = log10f(d3);
+          const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
+                                         : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
+          const float rx = fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
+          pg_c[cc] = fs(rx, p.ue_tx);
+        } else {
+          // log-distance (radio.py:265-273)
+          const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
+          pg_c[cc] = fs(fs(fs(p.ue_tx, pl), field), p.ue_tx);
+        }
       }
     }
   }
-  // ul_ref = ue_tx - 10 log10(snr_ref_prbs) + pg - N_prb (NRNet.step_rx, nr_engine.py:613-632)
-  const float ref_pg = fs(fa(p.ul_ref0, pg), p.noise_prb);
+  float pg = pg_c[0];
+  // ---------------- several cells: association and the A3 plan of this step (CellAssociation.associate / plan,
+  // radio.py:398-432): RSRP rx = pg + ue_tx; fire slot k_ho inside the step (or -1) toward the strongest neighbour
+  int serv = 0, k_ho = -1, tgt = 0, csi_src = -1;   // csi_src: -1 the stored CSI, -2 zeros (after a handover), u row
+  bool fired = false;
+  long long ho_end = 0, n_ho = 0;
+  if constexpr (MC) {
+    if (act) {
+      float rx[NC];
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) rx[cc] = fa(pg_c[cc], p.ue_tx);
+      serv = (int)st.serv[CK(er, NER, 1)];
+      if (A.s.pending[CK(e, p.E, 10)]) {              // argmax, first index on ties
+        serv = 0;
+#pragma unroll
+        for (int cc = 1; cc < NC; ++cc)
+          if (cc < C && rx[cc] > rx[serv]) serv = cc;
+      }
+      ho_end = st.ho_end[CK(er, NER, 1)];
+      n_ho = st.n_ho[CK(er, NER, 1)];
+      float rs = rx[0], best = 0.0f;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) if (cc == serv) rs = rx[cc];
+      int bc = 0;                                     // max over the other cells, first index on ties
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        const float v = cc == serv ? -INFINITY : rx[cc];
+        if (cc == 0 || v > best) { best = v; bc = cc; }
+      }
+      bool cond = best > fa(fa(rs, p.a3_off), p.a3_hyst);
+      if (p.has_floor) cond = cond && (best >= p.floor_rx);
+      const long long cand = st.a3_cand[CK(er, NER, 1)], cnt0 = st.a3_cnt[CK(er, NER, 1)];
+      const long long cnt = (cond && bc == cand) ? cnt0 : 0;
+      long long k_fire = (long long)p.ttt - cnt - 1;
+      k_fire = k_fire < 0 ? 0 : k_fire;
+      const bool fire = cond && k_fire < p.N;
+      st.a3_cnt[CK(er, NER, 1)] = (cond && !fire) ? cnt + p.N : 0;
+      st.a3_cand[CK(er, NER, 1)] = (cond && !fire) ? bc : -1;
+      k_ho = fire ? (int)k_fire : -1;
+      tgt = bc;
+    }
+  }
+  // ul_ref = ue_tx - 10 log10(snr_ref_prbs) + pg - N_prb (NRNet.step_rx, nr_engine.py:613-632); with several cells
+  // ul_ref = (ue_tx - 10 log10(snr_ref_prbs) + pg_serving) - N+I_serving(dB) per RBG (nr_engine.py:770-772), the
+  // first sum kept in ref_pg and the N+I term read from the env's shared row of the slot
+  float ref_pg = MC ? 0.0f : fs(fa(p.ul_ref0, pg), p.noise_prb);
   const float sinr_obs = fs(fa(pg, p.ue_tx), p.sub_noise);
   if (ref_vec) {
     for (int s = 0; s < S; ++s) v_ref[s * NP] = act ? A.ul_ref_in[CK(eS + s, NERS, 5)] : 0.0f;
   }
-#define REF(s) (ref_vec ? v_ref[(s) * NP] : ref_pg)
+#define REF(s) (MC ? fs(ref_pg, s_nidb[MC ? gi : 0][MC ? serv : 0][s]) : (ref_vec ? v_ref[(s) * NP] : ref_pg))
+  // the per-RBG reference of robot a (lane a of this warp) from lane s
+#define REF_A(s, ta, ref_a, serv_a) (MC ? fs(ref_a, s_nidb[MC && GW <= 32 ? (ta) / GW : 0][MC ? (serv_a) : 0][s]) \
+                                        : (ref_vec ? d_ref[(s) * NP + (ta)] : ref_a))
 
   // ---------------- CSI / fading gain rows of the step (written by the fading kernel)
   const long long NERr = (long long)p.E * R;
-  const long long plane = (long long)S * NERr;
+  const long long plane = (long long)S * NERr * C;   // one gain row: [E R][C][S] (C = 1: [E R][S])
   int u = 0;   // UL rows done
+  // several cells: gain-row index of link (robot a, cell c) RBG s in row `row`; the CSI of robot a
+#define GIDX(row, er_a, c, s) ((long long)(row) * plane + ((er_a) * C + (c)) * S + (s))
+#define CSI_A(src, er_a, c, s) ((src) == -1 ? st.csi[CK((er_a) * S + (s), NERS, 5)] \
+                               : ((src) == -2 ? 0.0f : A.gain[CK(GIDX((src), (er_a), (c), (s)), GCAP, 13)]))
   // PHR cap n_max = floor(snr_ref_prbs * 10^((mean(ul_ref) - phr_min) / 10) / w[0]).clamp(1, S) (mac_ul.py:165-168),
   // the mean as a left-to-right sum times float32(1 / S)
   int n_max = S;
-  if (p.phr_cap) {
+  if (p.phr_cap && !MC) {
     float sum = 0.0f;
     for (int s = 0; s < S; ++s) sum = s == 0 ? REF(0) : fa(sum, REF(s));
     const float x = fm(fs(fm(sum, p.inv_S), p.phr_min), 0.1f);
@@ -471,10 +554,59 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   };
   if (act) rescan();
 
+  // ---- handover of this robot at slot g_sw (CellAssociation.switch, radio.py:434-444; MacLink.handover,
+  // mac.py:557-582; UlMac.handover, mac_ul.py:238-243): the target cell serves from g_sw + ho_int on; HARQ combining
+  // restarts (or, under RLC UM or ho_rlc = "flush", the TBs in flight are lost, and flush drops every queued frame
+  // not completed); OLLA, the PF average and the CSI start afresh; a pending SR is dropped; BSR = unsent bytes
+  auto handover = [&](long long g_sw) {
+    serv = tgt;
+    ho_end = g_sw + p.ho_int;
+    n_ho += 1;
+    if (p.harq_drop || p.ho_flush) {
+      for (int f = 0; f < F; ++f) {
+        const long long at = eF + f;
+        const bool valid = st.cap[CK(at, NERF, 3)] >= 0 && isinf(st.fin[CK(at, NERF, 3)]) && !st.lost[CK(at, NERF, 3)];
+        if (!valid) continue;
+        bool ov = p.ho_flush != 0;
+        for (uint32_t m_ = pend; m_ && !ov; m_ &= m_ - 1u) {
+          const int q = __ffs(m_) - 1;
+          ov = st.start[CK(at, NERF, 3)] < st.h_hi[CK(eP + q, NERP, 4)] && st.end_[CK(at, NERF, 3)] > st.h_lo[CK(eP + q, NERP, 4)];
+        }
+        if (ov) {
+          st.lost[CK(at, NERF, 3)] = 1;
+          atomicAdd(sc + INB_CTR_LOST_FRAMES, 1ull);
+        }
+      }
+      if (p.ho_flush) sent = enq;
+      for (uint32_t m_ = pend; m_; m_ &= m_ - 1u) st.h_state[CK(eP + __ffs(m_) - 1, NERP, 4)] = 0;
+      freem |= pend;
+      pend = 0u;
+      q_dirty = true;
+    } else {
+      for (uint32_t m_ = pend; m_; m_ &= m_ - 1u) {
+        const int q = __ffs(m_) - 1;
+        st.h_ntx[CK(eP + q, NERP, 4)] = 0;
+        st.h_comb[CK(eP + q, NERP, 4)] = 0.0f;
+      }
+    }
+    olla = 0.0f;
+    avg = 100.0f;
+    csi_src = -2;
+    sr_t = -1;
+    bsr = enq - sent;
+  };
+
+
   // ======================================================================= slot loop (nr_engine.py:656-667)
   for (int k = 0; k < p.K_rows; ++k) {
     const int rel = p.rows[k][0], uls = p.rows[k][1], srf = p.rows[k][2];
     const long long g = T * p.N + rel;
+    if constexpr (MC) {   // A3 handovers due by this slot fire before it (nr_engine.py:748-752)
+      if (act && k_ho >= 0 && k_ho <= rel && !fired) {
+        handover(T * p.N + k_ho);
+        fired = true;
+      }
+    }
     // ---- arrival gate (NREngine._open_gate, engine.py:176-183)
     if ((srf || uls) && M > 0 && act) {
       long long vis = base;
@@ -513,7 +645,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool any_free = p_new >= 0;
     if (p_new < 0) p_new = 0;
     const long long need = bsr < unsent ? bsr : unsent;
-    const bool new_el = act && any_free && need > 0 && !has_rx;
+    bool new_el = act && any_free && need > 0 && !has_rx;
+    float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
+    if constexpr (MC) {
+      // the env's N+I in dB of this slot, the serving link's reference, power control and the PHR cap
+      for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, log10f(s_ni[gi][i / S][i % S]));
+      float pg_s = pg_c[0];
+#pragma unroll
+      for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
+      ref_pg = fa(pg_s, p.ue_tx_ref);
+      const float rx_s = fa(pg_s, p.ue_tx);
+      if (p.pc_on) pcv = fs(p.ue_tx, fa(p.pc_p0, fm(p.pc_alpha, fs(p.ue_tx, rx_s))));
+      if (p.phr_cap) {
+        const float x = fm(fs(fs(rx_s, p.sub_noise), p.phr_min), 0.1f);
+        const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
+        n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
+      }
+      const bool ok = g >= ho_end;              // outside the handover interruption (mac.py:249-251)
+      has_rx = has_rx && ok;
+      new_el = new_el && ok;
+      if constexpr (GW > 32) __syncthreads(); else __syncwarp();
+    }
     const int rx_nsb = has_rx ? (int)st.h_nsb[CK(eP + rx_p, NERP, 4)] : 0;
     // scheduler estimate with OLLA -> rate (bytes per RBG) (mac.py:255-266, mac_ul.py:154-171) and the scheduler
     // metric per RBG: PF rate / avg, maxCI rate, RR slot age (mac.py:267-275).  Only robots that may want RBGs use
@@ -529,10 +681,18 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
         const float olla_a = __shfl_sync(0xFFFFFFFFu, olla, a);
         const float avgd_a = __shfl_sync(0xFFFFFFFFu, avg_den, a);
+        const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
+        const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
+        const float pc_a = MC ? __shfl_sync(0xFFFFFFFFu, pcv, a) : 0.0f;
         if (lane < S) {
           const int s = lane;
-          const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
-          const float est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+          const float refs = REF_A(s, ta, ref_a, serv_a);
+          float est;
+          if constexpr (MC) {   // one RBG at the power-control PSD (mac_ul.py:160-161)
+            est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), CSI_A(csrc_a, ra / S, serv_a, s));
+          } else {
+            est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+          }
           const float eo = p.olla_on ? fa(est, olla_a) : fa(est, 0.0f);
           const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
           const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
@@ -553,22 +713,24 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         rkey = sum;
       }
       const int mine = has_rx ? rx_nsb : 0;
-      int before = 0;
+      int before = 0;   // several cells: the ranking runs inside each cell (mac.py:313-319)
       if constexpr (GW <= 32) {
 #pragma unroll 1
         for (int j = 0; j < GW; ++j) {
           const float kj = __shfl_sync(0xFFFFFFFFu, rkey, j, GW);
           const int nj = __shfl_sync(0xFFFFFFFFu, mine, j, GW);
-          if (kj > rkey || (kj == rkey && j < r)) before += nj;
+          const int sj = MC ? __shfl_sync(0xFFFFFFFFu, serv, j, GW) : 0;
+          if ((!MC || sj == serv) && (kj > rkey || (kj == rkey && j < r))) before += nj;
         }
       } else {
         sm->rkey[r] = rkey;
         sm->rnsb[r] = mine;
+        sm->rserv[r] = serv;
         __syncthreads();
 #pragma unroll 1
         for (int j = 0; j < GW; ++j) {
           const float kj = sm->rkey[j];
-          if (kj > rkey || (kj == rkey && j < r)) before += sm->rnsb[j];
+          if ((!MC || sm->rserv[j] == serv) && (kj > rkey || (kj == rkey && j < r))) before += sm->rnsb[j];
         }
         __syncthreads();
       }
@@ -583,19 +745,33 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     uint32_t won = 0u;
     int cnt = 0;
     float left = (float)need;
-    if (Grp<GW>::two_or_more_uniform(act && want_cnt > 0)) {
+    // several cells: one scheduler per cell on the same RBGs (mac.py:335-345), the argmax over the cell's robots
+    const bool contested = MC ? Grp<GW>::two_or_more_in_a_cell_uniform(act && want_cnt > 0, serv, C)
+                              : Grp<GW>::two_or_more_uniform(act && want_cnt > 0);
+    if (contested) {
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
         float mkey = want ? fa(METRIC(s), prio) : -1.0f;
         if (lex) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
           const bool wr = want && has_rx;
-          const bool any_wr = Grp<GW>::any(wr, sm, par);   // every lane takes part
+          bool any_wr = false;
+#pragma unroll
+          for (int cc = 0; cc < NC; ++cc) {
+            if (cc >= C) continue;
+            const bool a_ = Grp<GW>::any(wr && serv == cc, sm, par);   // every lane takes part
+            if (cc == serv) any_wr = a_;
+          }
           if (any_wr && !wr) mkey = -1.0f;
         }
-        uint32_t mx;
-        const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
-        const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+        bool oh = false;
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          if (cc >= C) continue;
+          uint32_t mx;
+          const int w = Grp<GW>::argmax_u32(serv == cc ? fkey(mkey) : 0u, mx, sm, par);
+          if (cc == serv) oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+        }
         if (oh) {
           won |= 1u << s;
           cnt += 1;
@@ -612,10 +788,15 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         for (int s = 0; s < S; ++s) {
           const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
           const float mkey = want ? METRIC(s) : -1.0f;
-          uint32_t mx;
-          const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
-          const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u, sm, par);
-          const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
+          bool oh = false;
+#pragma unroll
+          for (int cc = 0; cc < NC; ++cc) {
+            if (cc >= C) continue;
+            uint32_t mx;
+            const int w = Grp<GW>::argmax_u32(serv == cc ? fkey(mkey) : 0u, mx, sm, par);
+            const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u && serv == cc, sm, par);
+            if (cc == serv) oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
+          }
           if (oh) {
             won |= 1u << s;
             cnt += 1;
@@ -648,7 +829,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    const float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    if constexpr (MC) split = fmaxf(split, pcv);   // at least the power-control backoff (mac_ul.py:176-180)
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
     float lnw = 0.0f;
@@ -674,11 +856,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
         const float off_a = __shfl_sync(0xFFFFFFFFu, p.olla_on ? olla : 0.0f, a);
         const float nprb_a = __shfl_sync(0xFFFFFFFFu, n_prb, a);
+        const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
+        const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
         float ng = 0.0f;   // -10^(clamp(est, -30, 60) / 10) of this lane's RBG
         if (in) {
           const int s = lane;
-          const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
-          const float est_tx = fa(fs(refs, split_a), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+          const float refs = REF_A(s, ta, ref_a, serv_a);
+          const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s) : A.gain[CK(g_csi + ra + s, GCAP, 13)];
+          const float est_tx = fa(fs(refs, split_a), csi_s);
           ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
         const long long trow = (long long)(int)nprb_a * p.MCS;
@@ -725,6 +910,43 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       freem &= ~(1u << p_tx);
       sent += byt_new;
     }
+    // ---- several cells: this slot's uplink interference at every gNB from the robots the other cells scheduled on
+    // the same RBG (NRNet._ul_ici, nr_engine.py:799-816): PSD after power split and control, the link's fading.  At
+    // most one robot per cell holds an RBG, so with C <= 3 every (cell, RBG) sum has at most two non-zero terms and
+    // its value does not depend on the order of the shared-memory additions.
+    if constexpr (MC) {
+      for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+        const int a = __ffs(tm) - 1;
+        const int ta = wbase + a;
+        const long long er_a = __shfl_sync(0xFFFFFFFFu, er, a);
+        const uint32_t won_a = __shfl_sync(0xFFFFFFFFu, won, a);
+        const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
+        const int serv_a = __shfl_sync(0xFFFFFFFFu, serv, a);
+        const int gi_a = GW > 32 ? 0 : ta / GW;
+        float pga[NC];
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) pga[cc] = __shfl_sync(0xFFFFFFFFu, pg_c[cc], a);
+        if (lane < S && ((won_a >> lane) & 1u)) {
+          const int s = lane;
+#pragma unroll
+          for (int cc = 0; cc < NC; ++cc) {
+            if (cc >= C || cc == serv_a) continue;
+            const float psd = fs(fs(fa(pga[cc], p.ue_tx), p.ref_db), split_a);
+            const float prx = powf(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er_a, cc, s), GCAP, 13)]), 0.1f));
+            atomicAdd(&s_if[gi_a][cc][s], prx);
+          }
+        }
+      }
+      if constexpr (GW > 32) __syncthreads(); else __syncwarp();
+      for (int i = r; i < C * S; i += GW) {
+        const int cc = i / S, s = i % S;
+        const float ni_now = fa(s_if[gi][cc][s], p.noise_mw);
+        s_nadb[gi][cc][s] = fm(10.0f, log10f(ni_now));
+        s_ni[gi][cc][s] = p.li_alpha == 1.0f ? ni_now : fa(fm(p.li_alpha, ni_now), fm(p.li_beta, s_ni[gi][cc][s]));
+        s_if[gi][cc][s] = 0.0f;
+      }
+      if constexpr (GW > 32) __syncthreads(); else __syncwarp();
+    }
     // ---- decode on the actual channel, HARQ update (mac.py:424-477)
     bool ok = false, fail = false, exh = false;
     long long served = 0;
@@ -753,13 +975,21 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
       const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
       const float lnw_a = __shfl_sync(0xFFFFFFFFu, lnw, a);
+      const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
       const float beta = s_beta[__shfl_sync(0xFFFFFFFFu, mcs, a)];
       const bool in = lane < S && ((won_a >> lane) & 1u);
       float x = -INFINITY;
       if (in) {
         const int s = lane;
-        const float refs = ref_vec ? d_ref[s * NP + ta] : ref_a;
-        const float a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
+        const float refs = REF_A(s, ta, ref_a, serv_a);
+        float a_;
+        if constexpr (MC) {   // this slot's interference replaces the N+I the estimate used (nr_engine.py:815)
+          const int gi_a = GW > 32 ? 0 : ta / GW;
+          a_ = fa(fs(refs, split_a), A.gain[CK(GIDX(u, ra / S, serv_a, s), GCAP, 13)]);
+          a_ = fs(a_, fs(s_nadb[gi_a][serv_a][s], s_nidb[gi_a][serv_a][s]));
+        } else {
+          a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
+        }
         const float negl = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
         x = fa(x_fdv(negl, beta), s_lw[s]);
       }
@@ -827,7 +1057,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       olla = clampf_t(fs(fa(olla, up), dn), -10.0f, 10.0f);
     }
     if (tx) bsr = enq - sent;
-    ++u;   // the gain of this row is the CSI of the next decision
+    if constexpr (MC) csi_src = u;   // the serving link's gain of this row is the CSI of the next decision
+    ++u;
     avg = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, (float)served)), 1e-9f);
     if (p.sched == 2 && tx) last_tx = g;
     if (tx) {   // counters (only transmitting robots have any to add)
@@ -872,18 +1103,49 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 
   // ======================================================================= step state and outputs
   // (the end-of-step queue work runs in the finish kernel, nr_finish.cu)
+  if constexpr (MC) {   // A3 triggers after the last scheduled slot of the step (nr_engine.py:781-784)
+    if (act && k_ho >= 0 && !fired) handover(T * p.N + k_ho);
+  }
   if (M > 0) enq = full_enq;
   if (act) {
     const InbOutputs& o = A.o;
     const long long ob = A.o_base != nullptr ? *A.o_base : 0;
-    out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
-    if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
+    if constexpr (MC) {
+      // serving-link SINR against the gNB's latest N+I, its mean over the RBGs (NRNet.serving_sinr_db,
+      // nr_engine.py:709-713); the CSI, association and path gains of every link
+      float sum = 0.0f, pg_s = pg_c[0];
+#pragma unroll
+      for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
+      for (int s = 0; s < S; ++s) sum = s == 0 ? s_ni[gi][serv][0] : fa(sum, s_ni[gi][serv][s]);
+      const float snr = fs(fs(fa(pg_s, p.ue_tx), p.ref_db), fm(10.0f, log10f(fm(sum, p.inv_S))));
+      out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = snr;
+      out_ptr(o.serving_cell, ob)[CK(er, NER, 1)] = serv;
+      if (o.pathgain) {
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc)
+          if (cc < C) out_ptr(o.pathgain, ob)[CK(er * C + cc, NER * C, 1)] = pg_c[cc];
+      }
+      for (int s = 0; s < S; ++s) st.csi[CK(eS + s, NERS, 5)] = CSI_A(csi_src, er, serv, s);
+      st.serv[CK(er, NER, 1)] = serv;
+      st.ho_end[CK(er, NER, 1)] = ho_end;
+      st.n_ho[CK(er, NER, 1)] = n_ho;
+    } else {
+      out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
+      if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
+    }
     out_ptr(o.gen_accepted, ob)[CK(er, NER, 1)] = n_acc;
     out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
   }
 #undef REF
+  if constexpr (MC) {   // the env's N+I back to memory; the initial association is done
+    if constexpr (GW > 32) __syncthreads(); else __syncwarp();
+    if (env_ok) {
+      for (int i = r; i < C * S; i += GW) A.s.ni_ul[e * C * S + i] = s_ni[gi][i / S][i % S];
+      if (r == 0) A.s.pending[e] = 0;
+    }
+  }
   // counters: one writer per word and env (an env's counter words are shared by its group only)
   if constexpr (GW > 32) {
     __syncthreads();

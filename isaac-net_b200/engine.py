@@ -105,6 +105,7 @@ class NRB200Engine:
             seed = int(torch.randint(0, 2 ** 62, ()).item())
         self.seed = int(seed)
         self.S, self.P, self.F, self.N = cfg.n_subbands, cfg.n_harq, cfg.frame_buffer, cfg.slots_per_step
+        self.C = cfg.n_cells
         self.tab = PhyTables(cfg, cfg.subband_prbs, dev)
         self.rician = cfg.rician_mode == "fixed"
         self._alloc_state()
@@ -146,6 +147,8 @@ class NRB200Engine:
         self._steps_done = 0
         self._args = nat.InbStepArgs()
         self._fill_static()
+        if self.C > 1:
+            self.pathgain = torch.zeros(E, R, self.C, device=dev)     # every link's path gain of the last step
         self._kernel_reset(None)
 
     # ------------------------------------------------------------------ buffers
@@ -158,9 +161,15 @@ class NRB200Engine:
             st[n] = full((E, R), L, v)
         st["olla"], st["avg"] = full((E, R), f32, 0.0), full((E, R), f32, 100.0)
         st["csi"] = full((E, R, S), f32, 0.0)
-        st["h"] = full((E, R, S, 2), f32, 0.0)
+        cd = (self.C,) if self.C > 1 else ()
+        st["h"] = full((E, R, *cd, S, 2), f32, 0.0)
         if self.rician:
-            st["spec"], st["k_lin"] = full((E, R, 2), f32, 0.0), full((E, R), f32, 0.0)
+            st["spec"], st["k_lin"] = full((E, R, *cd, 2), f32, 0.0), full((E, R, *cd), f32, 0.0)
+        if self.C > 1:   # CellAssociation state, the gNBs' N+I per PRB (mW)
+            for n, v in (("serv", 0), ("a3_cand", -1), ("a3_cnt", 0), ("ho_end", 0), ("n_ho", 0)):
+                st[n] = full((E, R), L, v)
+            st["pending"] = full((E,), b, True)
+            st["ni_ul"] = full((E, self.C, S), f32, 0.0)
         for n in ("h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb"):
             st[n] = full((E, R, P), L, 0)
         st["h_comb"] = full((E, R, P), f32, 0.0)
@@ -237,6 +246,24 @@ class NRB200Engine:
             p.radio_model = 2
             p.pl_const, p.pl_10n = _f32(cfg.pl_const_db), _f32(10 * cfg.pathloss_exp)
             p.amp = _f32(cfg.shadow_sigma_db * math.sqrt(2 / K))
+        p.C = self.C
+        if self.C > 1:   # CellAssociation (radio.py:348-359) with the NR slot clock; nr_engine.py:221-222, 671-675
+            slot_ms = cfg.control_step_ms / self.N
+            p.ttt = int(round(cfg.a3_ttt_ms / slot_ms))
+            p.ho_int = int(round(cfg.ho_interruption_ms / slot_ms))
+            p.a3_off, p.a3_hyst = _f32(cfg.a3_offset_db), _f32(cfg.a3_hyst_db)
+            floor = cfg.a3_min_target_rsrp_dbm
+            p.has_floor = int(floor is not None)
+            p.floor_rx = _f32(floor - (cfg.gnb_tx_dbm - 10 * math.log10(12 * cfg.nprb) - cfg.ue_tx_dbm)) \
+                if floor is not None else 0.0
+            p.ho_flush = int(cfg.ho_rlc == "flush")
+            p.pc_on = int(cfg.ul_pc_on)
+            self.noise_mw = 10 ** (cfg.noise_dbm_per_prb("gnb") / 10)
+            p.noise_mw = _f32(self.noise_mw)
+            p.ref_db = _f32(10 * math.log10(cfg.snr_ref_prbs))
+            p.ue_tx_ref = _f32(cfg.ue_tx_dbm - 10 * math.log10(cfg.snr_ref_prbs))
+            p.pc_p0, p.pc_alpha = _f32(cfg.ul_pc_p0_dbm), _f32(cfg.ul_pc_alpha)
+            p.li_alpha, p.li_beta = _f32(cfg.li_alpha), _f32(1 - cfg.li_alpha)
         a.s = self._state_struct()
         t = a.t
         t.bler, t.thr_ref, t.se, t.beta, t.rate = (tab.bler.data_ptr(), tab.thr_ref.data_ptr(), tab.se.data_ptr(),
@@ -248,8 +275,10 @@ class NRB200Engine:
         a.env_id, a.episode, a.rng_ctr = self.env_id.data_ptr(), self.episode.data_ptr(), self.rng_ctr.data_ptr()
         a.epoch, a.last_hid, a.ctr, a.status = (self.epoch.data_ptr(), self._last_hid.data_ptr(),
                                                 self.ctr.data_ptr(), self.status.data_ptr())
-        # fading-gain rows of one step: the CSI before the step + one row per UL slot (at most slots_per_step)
-        self._gain = torch.empty((self.N + 1) * self.S * self.E * self.R, dtype=torch.float32, device=self.dev)
+        # fading-gain rows of one step: the CSI before the step + one row per UL slot (at most slots_per_step); with
+        # several cells one row per UL slot holds every link's gain
+        rows = self.N * self.C if self.C > 1 else self.N + 1
+        self._gain = torch.empty(rows * self.S * self.E * self.R, dtype=torch.float32, device=self.dev)
         a.gain, a.gain_cap = self._gain.data_ptr(), self._gain.numel()
 
     def _stream(self):
@@ -264,7 +293,7 @@ class NRB200Engine:
         return out
 
     def _plane_waves(self, stream, spectrum, dcorr):
-        C, K = 1, self.config.shadow_modes
+        C, K = self.C, self.config.shadow_modes
         rand = lambda i: self._uniforms(stream + i, C * K).view(self.E, C, K)
         ang = rand(0) * 2 * math.pi
         if spectrum == "sos":
@@ -313,6 +342,8 @@ class NRB200Engine:
         a.mask = mask.data_ptr() if mask is not None else None
         a.env_id, a.episode, a.rng_ctr = self.env_id.data_ptr(), self.episode.data_ptr(), self.rng_ctr.data_ptr()
         a.s = self._state_struct()
+        a.C = self.C
+        a.noise_mw = self._args.p.noise_mw
         nat.check(self.L.inb_nr_reset(ctypes.byref(a), self._stream()), "inb_nr_reset")
 
     def _ids(self, env_ids):
@@ -334,6 +365,8 @@ class NRB200Engine:
                 self.traffic.reset(None)
             self._kernel_reset(None)
             self.ctr.zero_()
+            if self.C > 1:
+                self.pathgain = torch.zeros_like(self.pathgain)
             self.prb_avail = 0.0
             self.T = 0
             self.epoch.zero_()
@@ -471,7 +504,9 @@ class NRB200Engine:
                 ("newest", torch.long, (E, R)), ("queue_len", torch.long, (E, R)),
                 ("gen_accepted", torch.long, (E, R)), ("gen_bytes", torch.long, (E, R)),
                 ("queue_bytes", torch.float32, (E, R)), ("sinr_db", torch.float32, (E, R)),
-                ("pathgain", torch.float32, (E, R)), ("det_env", torch.bool, (E,))]
+                ("pathgain", torch.float32, (E, R, self.C) if self.C > 1 else (E, R)), ("det_env", torch.bool, (E,))]
+        if self.C > 1:
+            spec.append(("serving_cell", torch.long, (E, R)))
         off, lay = 0, []
         for n, dt, shape in spec:
             nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
@@ -502,7 +537,11 @@ class NRB200Engine:
         if dl_snr_db is not None:
             raise B200Unsupported("dl_snr_db: the downlink is not built")
         if pathgain_db is not None:
-            raise ValueError("pathgain_db= needs config.n_cells > 1; use x (poses or SNR) with one cell")
+            if self.C == 1:
+                raise ValueError("pathgain_db= needs config.n_cells > 1; use x (poses or SNR) with one cell")
+            _pathgain = pathgain_db
+        if self.C > 1 and _pathgain is None and (snr_db is not None or x is None or x.dim() != 3):
+            raise ValueError("several cells: pass poses [E,R,2|3] or pathgain_db=[E,R,C]")
         if blockers is not None:
             raise B200Unsupported("blockers= (screen blockage) is not built")
         T = self._now(t)
@@ -593,7 +632,8 @@ class NRB200Engine:
             for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
                 res[k] = out[k]
         res["sinr_db"] = sinr
-        res["serving_cell"] = torch.zeros(E, R, dtype=torch.long, device=self.dev)
+        res["serving_cell"] = out["serving_cell"] if self.C > 1 else torch.zeros(E, R, dtype=torch.long,
+                                                                                device=self.dev)
         res["t"] = (T - self.epoch).clone()
         if gen is not None:
             res["gen_accepted"] = out["gen_accepted"]
@@ -673,7 +713,8 @@ class NRB200Engine:
             for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
                 res[k] = out[k]
         res["sinr_db"] = sinr
-        res["serving_cell"] = torch.zeros(E, R, dtype=torch.long, device=self.dev)
+        res["serving_cell"] = out["serving_cell"] if self.C > 1 else torch.zeros(E, R, dtype=torch.long,
+                                                                                device=self.dev)
         res["t"] = (T - self.epoch).clone()
         if self.traffic is not None:
             res["gen_accepted"] = out["gen_accepted"]
@@ -718,7 +759,9 @@ class NRB200Engine:
             "ul.h_mcs": "h_mcs", "ul.h_tbs": "h_tbs", "ul.h_nsb": "h_nsb", "ul.h_comb": "h_comb",
             "q.cap": "cap", "q.start": "start", "q.end": "end_", "q.lost": "lost", "q.fin": "fin", "q.enq": "enq",
             "q.cls": "cls", "q.det": "det", "q.hid": "hid", "q.off": "off", "q.tag": "tag", "q.prio": "prio",
-            "q.dline": "dline", "net.h": "h", "net.spec": "spec", "net.k_lin": "k_lin"}
+            "q.dline": "dline", "net.h": "h", "net.spec": "spec", "net.k_lin": "k_lin", "assoc.serv": "serv",
+            "assoc.a3_cand": "a3_cand", "assoc.a3_cnt": "a3_cnt", "assoc.ho_end": "ho_end", "assoc.n_ho": "n_ho",
+            "assoc.pending": "pending", "net.ni_ul": "ni_ul"}
 
     def reference_state(self):
         """Engine state under the reference's names (ul.*, q.*, net.*, rng.*, eng.*), device tensors (views)."""
@@ -727,6 +770,8 @@ class NRB200Engine:
         out["rng.episode"], out["rng.ctr_step"] = self.episode, self.rng_ctr
         out["eng.T"], out["eng.epoch"] = torch.tensor(self.T), self.epoch
         out["eng.last_snr"], out["eng.last_hid"] = self._last_snr, self._last_hid
+        if self.C > 1 and getattr(self, "pathgain", None) is not None:
+            out["net.pg"] = self.pathgain
         return out
 
     def load_reference_state(self, snap):

@@ -6,9 +6,10 @@
 2. radio path gain of the kernel vs the oracle's torch evaluation of the same fields: |diff| <= 1e-3 dB (the
    reference's einsum / norm / sum reduction orders are not reproducible op by op).
 3. kernel vs the reference's own outputs (CPU goldens) teacher-forced: the engine is loaded with the reference state
-   before each step and fed the reference's poses and arrivals; integer outputs of at most 1 robot-step in 1000 may
-   differ (CUDA vs CPU transcendentals and reduction order move threshold decisions by an ulp), float outputs are
-   within 1e-5 relative elsewhere.
+   before each step and fed the reference's arrivals and path gains (the radio evaluated on the CPU exactly as the
+   reference does; torch itself moves them by up to 1.3e-3 dB between CPU and CUDA on config 3, which shifts SINRs
+   and so delivery slots); at most 1 robot-step in 1000 may differ in any output (CUDA vs CPU transcendentals and
+   reduction order move threshold decisions by an ulp), float outputs within 1e-5 relative / 1e-3 absolute.
 """
 import importlib
 import math
@@ -18,7 +19,7 @@ import pytest
 import torch
 
 from golden_io import CASES, Golden
-from oracle.nr_oracle import OracleEngine
+from oracle.nr_oracle import OracleEngine, Radio
 
 ib = importlib.import_module("isaac-net_b200")
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -73,7 +74,7 @@ def test_kernel_equals_oracle_seq_bitwise(case):
             assert _eq_t(st_k[k], v), f"step {s} state {k}"
 
 
-@pytest.mark.parametrize("case", ("1", "2", "4"))
+@pytest.mark.parametrize("case", ("1", "2", "4", "3"))
 def test_kernel_radio_matches_oracle(case):
     g = Golden(case)
     cfg, wl = g.config(), g.workload()
@@ -88,8 +89,7 @@ def test_kernel_radio_matches_oracle(case):
         assert d <= 1e-3, (s, d)
 
 
-@pytest.mark.parametrize("case", CASES)
-def test_kernel_vs_reference_goldens_teacher_forced(case):
+def _teacher_forced_flips(case):
     g = Golden(case)
     cfg, wl = g.config(), g.workload()
     dev = torch.device("cuda:0")
@@ -99,22 +99,44 @@ def test_kernel_vs_reference_goldens_teacher_forced(case):
     for s in range(1, g.steps):
         if not g.has_state(s - 1) or g.reset_ids(s):
             continue
-        eng.load_reference_state(g.state(s - 1))
-        eng._fields = None                          # radio fields are redrawn from (seed, env, episode)
-        out = eng.step(None, torch.as_tensor(g.pos(s)).to(dev), _arrivals=_Arr(g.arrivals(s), dev))
+        snap = g.state(s - 1)
+        eng.load_reference_state(snap)
+        # the reference's path gains: its radio on the CPU, fields drawn from (seed, env, episode)
+        o = OracleEngine(cfg, g.E, g.R, "cpu", seed=wl.seed, reduce="aten")
+        o.load_reference_state(snap)
+        pg = Radio(cfg, o.rng, g.E, o.dev).pathgain_db(torch.as_tensor(g.pos(s)))
+        pg = pg[..., 0] if eng.C == 1 else pg
+        out = eng.step(None, None, _pathgain=pg.to(dev), _arrivals=_Arr(g.arrivals(s), dev))
         ref = g.outputs(s)
         rows = np.ones((g.E, g.R), dtype=bool)
         for k in INT_OUT:
             if k in ref:
                 eq = out[k].cpu().numpy() == ref[k]
                 rows &= eq[:, None] if eq.ndim == 1 else eq.reshape(g.E, g.R, -1).all(-1)
-        flips += int((~rows).sum())
-        total += g.E * g.R
-        for k in FLOAT_OUT:
+        for k in FLOAT_OUT:            # a float output off by more than the tolerance also counts as a flip
             if k in ref:
                 a, b = out[k].double().cpu().numpy(), ref[k].astype(np.float64)
-                both = np.isfinite(a) & np.isfinite(b) & rows.reshape(g.E, g.R, *([1] * (a.ndim - 2)))
-                assert np.allclose(a[both], b[both], rtol=1e-5, atol=1e-3), f"step {s} {k}"
+                close = np.isclose(a, b, rtol=1e-5, atol=1e-3, equal_nan=True)
+                rows &= close[:, None] if close.ndim == 1 else close.reshape(g.E, g.R, -1).all(-1)
+        flips += int((~rows).sum())
+        total += g.E * g.R
         n += 1
     assert n > 0
+    return flips, total
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c != "3s"])
+def test_kernel_vs_reference_goldens_teacher_forced(case):
+    flips, total = _teacher_forced_flips(case)
     assert flips * 1000 <= total, (flips, total)
+
+
+def test_kernel_vs_reference_handover_stress_teacher_forced():
+    """The handover stress case: PF averages restart at every handover, so equal retransmission ranking keys are
+    common and the reference's CPU argsort orders them its own way, while the kernel ranks ties by robot index.  The
+    kernel may differ from the reference in no more robot-steps than the oracle with the kernel's tie rule does
+    (CPU, teacher-forced), plus the usual 1 in 1000."""
+    from test_oracle_golden import _seq_flips
+    flips, total = _teacher_forced_flips("3s")
+    ties, n = _seq_flips("3s", ties="stable")
+    assert flips <= ties + max(1, total // 1000), (flips, ties, total)

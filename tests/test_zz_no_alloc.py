@@ -74,4 +74,4 @@ def test_noalloc_refuses_oversize_gain_rows():
     a.p.rows[0][1] = 12                           # one UL row
     a.p.E = nat.NOALLOC_GAIN_MAX // (2 * a.p.S * a.p.R) + 1
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    assert eng.L.inb_nr_step_noalloc(ctypes.byref(a), stream) == -7
+    assert eng.L.inb_nr_step_noalloc(ctypes.byref(a), stream) == -10
