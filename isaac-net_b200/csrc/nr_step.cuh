@@ -867,10 +867,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
         const long long trow = (long long)(int)nprb_a * p.MCS;
+        // candidates: MCS <= mcs_max with a TBS; the highest first (one lane per RBG), which is the usual outcome;
+        // if it fails, every other candidate at once (one lane per MCS) and the highest that passes
+        const uint32_t cand = __ballot_sync(0xFFFFFFFFu, lane <= p.mcs_max && lane < p.MCS &&
+                                                         A.t.la_tbs[CK(trow + (lane < p.MCS ? lane : 0), NLA, 9)] > 0);
         int chosen = -1;
-#pragma unroll 1
-        for (int m = p.mcs_max; m >= 0; --m) {
-          if (A.t.la_tbs[CK(trow + m, NLA, 9)] <= 0) continue;
+        if (cand) {
+          const int m = 31 - __clz(cand);
           const float beta = s_beta[m];
           const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
           const float mx = warp_max(x);
@@ -879,10 +882,39 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
           const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
-          if (tbler <= p.target) {   // the same value on every lane: a warp-uniform exit
-            chosen = m;
-            break;
+          if (tbler <= p.target) chosen = m;   // the same value on every lane
+        }
+        const uint32_t rest = chosen < 0 && cand ? cand & ~(1u << (31 - __clz(cand))) : 0u;
+        if (rest) {
+          if (in) d_x[lane * NP + ta] = ng;     // the grant's -SINR_lin into robot a's column (its rates are done)
+          __syncwarp();
+          bool pass = false;
+          if ((rest >> lane) & 1u) {
+            const int m = lane;
+            const float beta = s_beta[m];
+            float mx = -INFINITY;
+            for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
+              const int s = __ffs(bb) - 1;
+              mx = fmaxf(mx, fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]));
+            }
+            const float m0 = isinf(mx) ? 0.0f : mx;
+            float sum = 0.0f;
+            bool first = true;
+            for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
+              const int s = __ffs(bb) - 1;
+              const float e = expf(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
+              sum = first ? e : fa(sum, e);
+              first = false;
+            }
+            const float lse = fa(logf(sum), m0);
+            const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
+            const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
+            const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+            pass = tbler <= p.target;
           }
+          const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
+          chosen = pm ? 31 - __clz(pm) : -1;
+          __syncwarp();
         }
         if (lane == a) {
           mcs_new = chosen < 0 ? 0 : chosen;
