@@ -7,12 +7,16 @@ positions they produce are the engine's pose input.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
 
 from .config import NRConfig
 from .traffic import TrafficModel
+
+_DATA = os.path.join(os.path.dirname(os.path.abspath(__file__)), "data")
+RADIO_MAP_CFG5 = os.path.join(_DATA, "radio_map_cfg5.npz")     # baked by data/make_radio_map.py (build() runs it)
 
 
 @dataclass(frozen=True)
@@ -63,8 +67,9 @@ def workload(i: int) -> Workload:
         return Workload("cfg3_1024x64_3cell", 1024, 64, 500, 2, f)
     if i == 5:
         f = _common(bandwidth_mhz=20, control_step_ms=5.0, n_cells=2, cell_layout="custom",
-                    cell_positions_m=((64.0, 128.0), (192.0, 128.0)), channel="radio_map", blockage=True,
-                    blockage_model="stochastic", scheduler="rr", n_harq=4, msg_sizes=(1500.0,),
+                    cell_positions_m=((64.0, 128.0), (192.0, 128.0)), channel="radio_map",
+                    radio_map_path=RADIO_MAP_CFG5,
+                    blockage=True, blockage_model="stochastic", scheduler="rr", n_harq=4, msg_sizes=(1500.0,),
                     traffic=(TrafficModel.bursty(1500, rate_hz=200, burst_size=1, on_off=(1.0, 0.0)),), seed=4)
         return Workload("cfg5_8192x48_radiomap", 8192, 48, 500, 4, f)
     raise ValueError(f"no workload {i}")

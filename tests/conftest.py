@@ -8,6 +8,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 importlib.import_module("isaac-net_b200")
+# the config-5 radio map is a build product (isaac-net_b200/data/make_radio_map.py); bake it if this tree has none
+importlib.import_module("isaac-net_b200.data.make_radio_map").ensure()
 
 
 def pytest_configure(config):

@@ -43,6 +43,15 @@ CASES = {
                                             n_harq=4, max_harq_tx=3, frame_buffer=10, timeout_steps=8), 2000.0),
     # a TTT of several control steps: A3 candidates carried across steps and fired inside a later one
     "3t": (3, 2, 64, 24, {14: [0]}, 1, dict(a3_ttt_ms=47.5, a3_hyst_db=1.0, ho_interruption_ms=6.0), 800.0),
+    # config 5: two cells on the baked radio map (isaac-net_b200/data/make_radio_map.py) with TR 38.901 blockage
+    # model A; "5s" lowers the UE power so that blockage losses move links across MCS and handover thresholds
+    "5": (5, 4, 48, 24, {10: [1]}, 2, {}),
+    "5s": (5, 3, 48, 24, {12: [0]}, 1, dict(ue_tx_dbm=-20.0, a3_ttt_ms=10.0, a3_hyst_db=1.0, n_harq=4,
+                                            timeout_steps=8), 3.0),
+    # blockage model A on the single-cell TR 38.901 UMi channel: the "outdoor" family, gNB above the UE (zenith
+    # terms active; a 3 m mast puts most links inside the regions' elevation window)
+    "1b": (1, 4, 16, 24, {10: [2]}, 2, dict(blockage=True, blockage_model="stochastic", ue_tx_dbm=-10.0,
+                                            gnb_height_m=3.0)),
 }
 
 
@@ -92,6 +101,11 @@ def ref_state(eng):
         if rad.k is not None:
             st["radio.k"], st["radio.phi"] = rad.k, rad.phi
         ch = rad.ch
+        blk = getattr(rad, "blk_a", None)
+        if blk is not None:
+            st["radio.blk.k"], st["radio.blk.phi"] = blk.field.k, blk.field.phi
+            for n in ("xk", "yk", "vel", "t"):
+                st["radio.blk." + n] = getattr(blk, n)
         if ch is not None and hasattr(ch, "sf_los"):
             for nm in ("sf_los", "sf_nlos", "los_field"):
                 fld = getattr(ch, nm)
@@ -148,6 +162,9 @@ def run_case(i, E, R, steps, resets, every, over, speed=1.0):
                 rec[f"s{s}/st.{k}"] = v
         pos = mot.advance()
     rec["resets"] = reset_rows
+    if cfg.channel == "radio_map":
+        mk = importlib.import_module("isaac-net_b200.data.make_radio_map")
+        rec["radio_map_sha256"] = np.array(mk.gain_digest(np.load(cfg.radio_map_path)["gain_db"]))
     return rec
 
 

@@ -6,7 +6,7 @@ import os
 import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
-CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t")
+CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t", "5", "5s", "1b")
 
 
 class Golden:

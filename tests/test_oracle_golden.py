@@ -69,9 +69,10 @@ def _seq_flips(case, ties):
     for s in range(1, g.steps):
         if not g.has_state(s - 1) or g.reset_ids(s):
             continue
-        o.load_reference_state(g.state(s - 1))
         o.radio = None
-        # the pose input goes through the radio, whose fields are drawn from (seed, env, episode) at first use
+        o.load_reference_state(g.state(s - 1))
+        # the pose input goes through the radio, whose fields are drawn from (seed, env, episode) at first use; the
+        # blockage clock and draws, where the config has them, come from the snapshot
         out = o.step(torch.as_tensor(g.pos(s)), _arr(g, s))
         ref = g.outputs(s)
         rows = np.ones((g.E, g.R), dtype=bool)
@@ -119,3 +120,15 @@ def test_oracle_golden_cases_have_activity():
     gen = sum(int(g.arrivals(s)["valid"].sum()) for s in range(g.steps))
     acc = sum(int(g.outputs(s)["gen_accepted"].sum()) for s in range(g.steps))
     assert acc < gen
+
+
+@pytest.mark.parametrize("case", [c for c in CASES if c.startswith("5")])
+def test_radio_map_is_the_fixture_map(case):
+    """The baked config-5 map (isaac-net_b200/data/make_radio_map.py) is byte for byte the map the reference ran on
+    when the fixture was made."""
+    import importlib
+    mk = importlib.import_module("isaac-net_b200.data.make_radio_map")
+    g = Golden(case)
+    with np.load(g.config().radio_map_path) as z:
+        assert mk.gain_digest(z["gain_db"]) == str(g.d["radio_map_sha256"])
+    assert str(g.d["radio_map_sha256"]) == mk.gain_digest(mk.bake()["gain_db"])
