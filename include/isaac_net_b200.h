@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 4
+#define INB_ABI_VERSION 5
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -41,6 +41,8 @@ extern "C" {
 #define INB_MAX_MCS 32
 #define INB_MAX_ROWS 64   /* scheduled slots per control step */
 #define INB_MAX_KF 32     /* plane waves per shadowing field */
+#define INB_BLK_REGIONS 4 /* blockage model A regions per env (TR 38.901 Sec. 7.6.4.1: K = 4) */
+#define INB_CDF_STRIDE 64 /* blockage CDF table: entries per coarse bucket of the two-level search */
 #define INB_NCTR 64       /* per-env counter words (int64) */
 
 /* counter words of InbStepArgs.ctr (per env, int64), MacLink.ctr / ntx_hist / rv_tx / rv_fail (mac.py:116-126) */
@@ -81,6 +83,9 @@ typedef struct {
   float *pathgain;                                         /* [E,R,C] path gain of every link (dB) */
   uint8_t *det_env;                                        /* [E] */
   int64_t *serving_cell;                                   /* [E,R] (NULL with one cell) */
+  /* obstacle outputs of the serving link (NULL: not produced; only with blockage and poses through the radio) */
+  uint8_t *blocked;                                        /* [E,R] a blockage region is on the direct path */
+  uint8_t *los;                                            /* [E,R] LOS state (InbParams.los_const) */
 } InbOutputs;
 
 /* Traffic arrivals of this step [E,R,M] (TrafficGen.step, sorted by slot), or M = 0. */
@@ -138,7 +143,43 @@ typedef struct {
   float ref_db;                 /* 10 log10(snr_ref_prbs) */
   float pc_p0, pc_alpha;        /* fractional UL power control: backoff = ue_tx - (P0 + alpha (ue_tx - RSRP)) */
   float li_alpha, li_beta;      /* N+I filter: ni = alpha ni_now + beta ni (beta = float32(1 - alpha)) */
+  int32_t los_const;            /* value of the `los` output (the forced tr38901 LOS state) */
+  int32_t field_fma;            /* plane-wave phase k . x as fma(y, k_y, x k_x) (1) or x k_x + y k_y rounded twice (0):
+                                   the rounding of the reference's CPU einsum, which takes its BLAS path (fused) when
+                                   2 R C K >= 400 (C fields of K waves) and its plain loop (two roundings) below */
 } InbParams;
+
+/* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes
+ * the path gain of every link into `pg` and the blocked bits into `blk`, and the MAC reads them in place of its own
+ * tr38901 / log-distance evaluation.  RadioMap._bilinear (isaac_net/core/channels/radio_map.py:101-115) and
+ * BlockageA.loss_db (isaac_net/core/channels/blockage.py:195-221), with the clock advance of RadioMC._blockage_db
+ * (isaac_net/core/radio.py:168-174). */
+typedef struct {
+  int32_t on;                   /* 0: no radio launch (the MAC evaluates the channel itself, or reads pathgain_in) */
+  int32_t map_on;               /* path gain from the radio map (else the tr38901 / log-distance formula of InbParams
+                                   with the shadowing fields of InbTables) */
+  int32_t H, W;                 /* map grid */
+  float x0, y0, sx, sy;         /* float32(x0), float32(y0), float32((W-1)/(x1-x0)), float32((H-1)/(y1-y0)) */
+  float wm1, hm1, wm2, hm2;     /* W-1, H-1, W-2, H-2 */
+  const float *map;             /* [C, H*W] path gain (dB) */
+  int32_t blockage;             /* blockage model A on */
+  int32_t Kb;                   /* plane waves per region field (<= INB_MAX_KF) */
+  int32_t n_table;              /* CDF entries: a multiple of INB_CDF_STRIDE, at most 1024 * INB_CDF_STRIDE */
+  float amp_b;                  /* float32(sqrt(2 / Kb)) */
+  float ck;                     /* float32(pi / lambda * r) of eq. 7.6-23 */
+  float max_db;                 /* cap of the summed loss (blockage_max_db) */
+  float h_ut, h_bs;             /* antenna heights (m) */
+  float dt;                     /* float32(control_step_ms * 1e-3): clock advance per step (s) */
+  float u_den;                  /* float32(n_table + 1) */
+  int32_t fma_b;                /* region-field phase rounding, as InbParams.field_fma: fused when 2 R 4 Kb >= 400 */
+  const float *bk, *bphi;       /* region fields [4, E, Kb, 2] (rad/m), [4, E, Kb] */
+  const float *xk, *yk;         /* [E, 4] azimuth / elevation spans (deg) */
+  const float *vel;             /* [E, 2] blocker drift velocity (m/s) */
+  float *t;                     /* [E] blockage clock (s), advanced by dt in every step */
+  const float *table;           /* [n_table] sorted samples of the unit sum-of-cosines marginal */
+  float *pg;                    /* [E, R, C] out: path gain of every link (dB) */
+  uint8_t *blk;                 /* [E, R] out: bit c = a region is on the direct path to cell c */
+} InbRadio;
 
 typedef struct {
   InbParams p;
@@ -165,9 +206,12 @@ typedef struct {
   int64_t gain_cap;             /* elements available at `gain` */
   const int64_t *o_base;        /* if set, every pointer in `o` is a byte offset from the address stored here (so a
                                    captured CUDA graph can write each step's outputs into a new block) */
+  InbRadio rm;                  /* radio launch (rm.on = 0: none) */
 } InbStepArgs;
 
-/* One control step of the NR uplink engine: the fading, MAC and finish launches, on `cuda_stream`. */
+/* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.
+ * With rm.on and pathgain_in NULL the radio launch evaluates the poses and the MAC reads rm.pg; a pathgain_in
+ * skips it.  -11: a radio pointer or size is missing or out of range, or o.blocked is set without the launch. */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array

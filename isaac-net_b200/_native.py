@@ -12,9 +12,11 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 4
+ABI_VERSION = 5
 MAX_ROWS = 64
 NCTR = 64
+BLK_REGIONS = 4        # INB_BLK_REGIONS
+CDF_STRIDE = 64        # INB_CDF_STRIDE
 CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
              "prb_used", "lost_frames")
 CTR_NTX_HIST, CTR_RV_TX, CTR_RV_FAIL = 16, 32, 48
@@ -28,7 +30,7 @@ STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg"
                 "ho_end", "n_ho", "pending", "ni_ul")
 OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
               "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
-              "sinr_db", "pathgain", "det_env", "serving_cell")
+              "sinr_db", "pathgain", "det_env", "serving_cell", "blocked", "los")
 ARR_FIELDS = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
 TAB_FIELDS = ("bler", "thr_ref", "se", "beta", "rate", "w", "lw", "lw10", "la_tbs", "la_i0", "la_wi", "la_ncb", "fk",
               "fphi", "gnb")
@@ -69,14 +71,25 @@ class InbParams(ctypes.Structure):
                 + [(n, f32) for n in ("pl_const", "pl_10n")]
                 + [(n, i32) for n in ("C", "ttt", "ho_int", "has_floor", "ho_flush", "pc_on")]
                 + [(n, f32) for n in ("a3_off", "a3_hyst", "floor_rx", "noise_mw", "ue_tx_ref", "ref_db", "pc_p0",
-                                      "pc_alpha", "li_alpha", "li_beta")])
+                                      "pc_alpha", "li_alpha", "li_beta")]
+                + [("los_const", i32), ("field_fma", i32)])
+
+
+class InbRadio(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("on", "map_on", "H", "W")]
+                + [(n, f32) for n in ("x0", "y0", "sx", "sy", "wm1", "hm1", "wm2", "hm2")]
+                + [("map", P)]
+                + [(n, i32) for n in ("blockage", "Kb", "n_table")]
+                + [(n, f32) for n in ("amp_b", "ck", "max_db", "h_ut", "h_bs", "dt", "u_den")]
+                + [("fma_b", i32)]
+                + [(n, P) for n in ("bk", "bphi", "xk", "yk", "vel", "t", "table", "pg", "blk")])
 
 
 class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
                 ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
-                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P)]
+                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P), ("rm", InbRadio)]
 
 
 class InbResetArgs(ctypes.Structure):
@@ -147,4 +160,4 @@ def check(rc, what):
 
 
 __all__ = ["lib", "check", "InbStepArgs", "InbResetArgs", "InbParams", "InbState", "InbOutputs", "InbArrivals",
-           "InbTables", "InbTrafficArgs", "InbTrafficSource", "EXPORTS", "LIB_PATH"]
+           "InbTables", "InbRadio", "InbTrafficArgs", "InbTrafficSource", "EXPORTS", "LIB_PATH"]

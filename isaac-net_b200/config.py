@@ -361,16 +361,14 @@ class NRConfig:
             out.append(("Rician K from the LOS state", "only a fixed rician_k_db is built"))
         if self.n_cells > 3:
             out.append((f"n_cells={self.n_cells}", "at most 3 cells (more need an ordered interference sum)"))
-        if self.n_cells > 1 and self.channel not in ("log_distance", "tr38901"):
-            out.append((f"channel={self.channel!r} with several cells", "several cells: log_distance or tr38901"))
+        if self.channel not in ("log_distance", "tr38901", "radio_map"):
+            out.append((f"channel={self.channel!r}", "channels built: log_distance, tr38901, radio_map"))
         if self.channel == "tr38901" and self.tr38901_los == "stochastic":
             out.append(("tr38901_los='stochastic'", "the spatially consistent LOS state is not built"))
         if self.channel == "tr38901" and self.tr38901_scenario not in ("UMi", "UMa"):
             out.append((f"tr38901_scenario={self.tr38901_scenario!r}", "tr38901 scenarios built: UMi, UMa"))
-        if self.channel == "radio_map":
-            out.append(("channel='radio_map'", "the radio-map channel is not built yet"))
-        if self.blockage:
-            out.append(("blockage=True", "blockage is not built yet"))
+        if self.blockage and self.blockage_model != "stochastic":
+            out.append((f"blockage_model={self.blockage_model!r}", "only blockage model A ('stochastic') is built"))
         if self.los_source != "stochastic":
             out.append((f"los_source={self.los_source!r}", "geometric LOS sources are not built"))
         if self.shadow_modes > 32:

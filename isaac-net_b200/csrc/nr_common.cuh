@@ -68,6 +68,29 @@ __device__ __forceinline__ float normal_at(uint32_t base, uint32_t i, float two_
   return fm(sqrtf(fm(-2.0f, logf(u1))), cosf(fm(two_pi, u2)));
 }
 
+// ---------------------------------------------------------------- large-scale channel formulas
+// Received power (dBm) of one link at 2-D distance d2 (floored at 1 m) with the shadowing value `field` (dB, the
+// plane-wave sum times its amplitude): TR 38.901 UMi / UMa LOS path loss (isaac_net/core/channels/tr38901.py:148-170)
+// plus sigma_SF times the unit field (radio_model 0 / 1), or log-distance path loss minus the field (radio_model 2,
+// isaac_net/core/radio.py:265-273), each in the reference's op order.
+__device__ __forceinline__ float formula_rx(const InbParams& p, float d2, float field) {
+  if (p.radio_model <= 1) {
+    const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
+    const float lg = log10f(d3);
+    const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
+                                   : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
+    return fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
+  }
+  const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
+  return fs(fs(p.ue_tx, pl), field);
+}
+
+// Phase k . x of one plane wave at (x, y), rounded as the reference's CPU einsum rounds it: one fused multiply-add
+// over the x product (its BLAS path) or two rounded products and a rounded sum (its plain loop for small matrices)
+__device__ __forceinline__ float wave_phase(float x, float y, float kx, float ky, bool fused) {
+  return fused ? __fmaf_rn(y, ky, fm(x, kx)) : fa(fm(x, kx), fm(y, ky));
+}
+
 // an output pointer of InbOutputs: absolute, or a byte offset from the block address `base` (InbStepArgs.o_base)
 template <typename T>
 __device__ __forceinline__ T* out_ptr(T* p, long long base) {

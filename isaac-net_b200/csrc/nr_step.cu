@@ -1,6 +1,7 @@
-// C entry points of the NR uplink step: argument checks, then three launches on the caller's stream: the fading
-// (nr_fading.cu), the MAC kernel variant of the group width (nr_step_g16.cu ... nr_step_g128.cu; the kernel is in
-// nr_step.cuh) and the end-of-step finish (nr_finish.cu).
+// C entry points of the NR uplink step: argument checks, then the launches on the caller's stream: the radio (radio
+// map / blockage, nr_radio.cu; only with InbStepArgs.rm.on), the fading (nr_fading.cu), the MAC kernel variant of the
+// group width (nr_step_g16.cu ... nr_step_g128.cu; the kernel is in nr_step.cuh) and the end-of-step finish
+// (nr_finish.cu).
 #include <mutex>
 
 #include "nr_common.cuh"
@@ -10,6 +11,7 @@ cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_radio(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
 
 // argument checks shared by both entry points; *gain_need = float32 elements of the step's gain rows
@@ -25,17 +27,37 @@ static int check_args(const InbStepArgs& a, long long* gain_need) {
                   a.o.serving_cell == nullptr))
     return -7;
   if (a.pos == nullptr && a.pathgain_in == nullptr) return -4;
-  if (a.pos != nullptr && a.pathgain_in == nullptr && (a.t.fk == nullptr || a.t.fphi == nullptr || a.t.gnb == nullptr))
+  const InbRadio& rm = a.rm;
+  const bool radio = rm.on && a.pathgain_in == nullptr;   // the radio launch runs (poses through the radio)
+  const bool formula = !(radio && rm.map_on);
+  if (a.pathgain_in == nullptr && formula && (a.t.fk == nullptr || a.t.fphi == nullptr || a.t.gnb == nullptr))
     return -5;
+  if (radio) {
+    if (rm.pg == nullptr || (rm.map_on && (rm.map == nullptr || rm.H < 2 || rm.W < 2)) || a.t.gnb == nullptr)
+      return -11;
+    if (rm.blockage && (rm.blk == nullptr || rm.t == nullptr || rm.table == nullptr || rm.bk == nullptr ||
+                        rm.bphi == nullptr || rm.xk == nullptr || rm.yk == nullptr || rm.vel == nullptr ||
+                        rm.Kb < 1 || rm.Kb > INB_MAX_KF || rm.n_table < INB_CDF_STRIDE ||
+                        rm.n_table % INB_CDF_STRIDE != 0 || rm.n_table > 1024 * INB_CDF_STRIDE))
+      return -11;
+  }
+  if (a.o.blocked != nullptr && !(radio && rm.blockage)) return -11;   // blocked bits exist only after the launch
   int n_ul = 0;
   for (int k = 0; k < p.K_rows; ++k) n_ul += p.rows[k][1] > 0 ? 1 : 0;
   *gain_need = p.C > 1 ? (long long)n_ul * p.C * p.S * p.E * p.R : (long long)(n_ul + 1) * p.S * p.E * p.R;
   return 0;
 }
 
-static int launch_all(const InbStepArgs& a, cudaStream_t s) {
+static int launch_all(const InbStepArgs& args, cudaStream_t s) {
+  InbStepArgs a = args;
   const InbParams& p = a.p;
-  cudaError_t err = launch_fading(a, s);
+  cudaError_t err = cudaSuccess;
+  if (a.rm.on && a.pathgain_in == nullptr) {   // path gains of this step's poses: the MAC reads them
+    err = launch_radio(a, s);
+    if (err != cudaSuccess) return -100 - (int)err;
+    a.pathgain_in = a.rm.pg;
+  }
+  err = launch_fading(a, s);
   if (err != cudaSuccess) return -100 - (int)err;
   if (p.R <= 16)
     err = launch_step_g16(a, s);

@@ -441,24 +441,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll 4
         for (int k = 0; k < p.Kf; ++k) {
           const float* f3 = s_fld[gi][cc][k];
-          const float arg = fa(fa(fm(px, f3[0]), fm(py, f3[1])), f3[2]);
+          const float arg = fa(wave_phase(px, py, f3[0], f3[1], p.field_fma != 0), f3[2]);
           const float cv = cosf(arg);
           cs = k == 0 ? cv : fa(cs, cv);
         }
-        const float field = fm(p.amp, cs);
-        if (p.radio_model <= 1) {
-          // TR 38.901 UMi / UMa LOS path loss (channels/tr38901.py:148-170) + sigma_SF * unit field
-          const float d3 = sqrtf(fa(fm(d2, d2), p.hh2));
-          const float lg = log10f(d3);
-          const float pl = (d2 <= p.dbp) ? fa(fa(p.pl_a, fm(p.pl_n1, lg)), p.fc_term)
-                                         : fs(fa(fa(p.pl_a, fm(40.0f, lg)), p.fc_term), p.pl_b_term);
-          const float rx = fa(p.ue_tx, -fa(pl, fm(p.sigma_sf, field)));
-          pg_c[cc] = fs(rx, p.ue_tx);
-        } else {
-          // log-distance (radio.py:265-273)
-          const float pl = fa(p.pl_const, fm(p.pl_10n, log10f(d2)));
-          pg_c[cc] = fs(fs(fs(p.ue_tx, pl), field), p.ue_tx);
-        }
+        pg_c[cc] = fs(formula_rx(p, d2, fm(p.amp, cs)), p.ue_tx);
       }
     }
   }
@@ -1157,6 +1144,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         for (int cc = 0; cc < NC; ++cc)
           if (cc < C) out_ptr(o.pathgain, ob)[CK(er * C + cc, NER * C, 1)] = pg_c[cc];
       }
+      if (o.blocked) out_ptr(o.blocked, ob)[CK(er, NER, 1)] = (A.rm.blk[CK(er, NER, 1)] >> serv) & 1;
       for (int s = 0; s < S; ++s) st.csi[CK(eS + s, NERS, 5)] = CSI_A(csi_src, er, serv, s);
       st.serv[CK(er, NER, 1)] = serv;
       st.ho_end[CK(er, NER, 1)] = ho_end;
@@ -1164,7 +1152,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     } else {
       out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
       if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
+      if (o.blocked) out_ptr(o.blocked, ob)[CK(er, NER, 1)] = A.rm.blk[CK(er, NER, 1)] & 1;
     }
+    if (o.los) out_ptr(o.los, ob)[CK(er, NER, 1)] = (uint8_t)p.los_const;
     out_ptr(o.gen_accepted, ob)[CK(er, NER, 1)] = n_acc;
     out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;

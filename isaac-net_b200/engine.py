@@ -24,6 +24,7 @@ import torch
 from . import _native as nat
 from .config import NRConfig
 from .phy import PhyTables
+from .radio_map import cdf_table, load_radio_map
 from .traffic import DeviceTrafficGen, Requests, TrafficGen, generates
 
 # counter-RNG constants (isaac_net/core/proto/rng.py:33-38, nr_rng.py:34, radio.py:53-56)
@@ -32,6 +33,12 @@ GOLD = 0x9E3779B9
 CH_RESET = 3
 RADIO_STREAM = 0x52 << 16
 LOG_DISTANCE_STREAM = 10
+BLOCKAGE_STREAM = RADIO_STREAM + 48
+# blockage model A per scenario family (TR 38.901 Tables 7.6.4.1-2 / -4; channels/blockage.py:100-112): azimuth span
+# range (deg), elevation span range (deg), distance r (m), correlation distance (m); 3 km/h blocker drift
+MODEL_A = {"indoor": ((15.0, 45.0), (5.0, 15.0), 2.0, 5.0), "outdoor": ((5.0, 15.0), (5.0, 5.0), 10.0, 10.0)}
+BLOCKER_SPEED_MPS = 3.0 / 3.6
+C_LIGHT_38901 = 3.0e8
 # TR 38.901: (default BS height, SF correlation LOS, SF correlation NLOS, sigma_SF LOS, sigma_SF NLOS, PL a, n1, b)
 SCN = {"UMi": (10.0, 10.0, 13.0, 4.0, 7.82, 32.4, 21.0, 9.5), "UMa": (25.0, 37.0, 50.0, 4.0, 6.0, 28.0, 22.0, 9.0)}
 
@@ -56,6 +63,14 @@ def seed_key(seed):
     """Key of an engine seed (CounterRNG.s0, proto/rng.py:60)."""
     seed = int(seed)
     return _mix32(_mix32(seed & M32) ^ _salt((seed >> 32) & M32))
+
+
+def einsum_fused(R, CK):
+    """Whether the reference's CPU einsum of a plane-wave field ("erx,cekx->cerk", evaluated as a batch over envs of
+    [R,2] x [2, C K] products, CK = fields x waves) takes its BLAS path, which rounds k . x as one fused multiply-add,
+    rather than its plain loop for small products (ATen bmm: 2 R C K < 400), which rounds both products and their
+    sum."""
+    return 2 * R * CK >= 400
 
 
 def _f32(x):
@@ -133,6 +148,7 @@ class NRB200Engine:
         # stream; event models (host triggers) keep the torch path
         self.dtraffic = DeviceTrafficGen(self.traffic, self.L) if DeviceTrafficGen.supports(self.traffic) else None
         self._fields = None
+        self._radio_ready = False          # the radio's draws exist (made at the first step with poses)
         self._gnb = torch.tensor(cfg.gnb_xy(), dtype=torch.float32, device=dev).contiguous()
         self._sched = {}
         # CUDA graphs: one captured step (traffic draws + the fused launch) per schedule key, replayed with the poses
@@ -147,6 +163,7 @@ class NRB200Engine:
         self._steps_done = 0
         self._args = nat.InbStepArgs()
         self._fill_static()
+        self._setup_radio()
         if self.C > 1:
             self.pathgain = torch.zeros(E, R, self.C, device=dev)     # every link's path gain of the last step
         self._kernel_reset(None)
@@ -226,6 +243,7 @@ class NRB200Engine:
         p.inv_ref_prbs = _f32(np.float32(1.0) / np.float32(cfg.snr_ref_prbs))
         K = cfg.shadow_modes
         p.Kf = K
+        p.field_fma = int(einsum_fused(self.R, self.C * K))
         if cfg.channel == "tr38901":
             hbs, _, _, sl, _, pa, n1, bb = SCN[cfg.tr38901_scenario]
             h_bs = float(cfg.gnb_height_m) if cfg.gnb_height_m is not None else hbs
@@ -292,8 +310,8 @@ class NRB200Engine:
         nat.check(rc, "inb_rng_draw")
         return out
 
-    def _plane_waves(self, stream, spectrum, dcorr):
-        C, K = self.C, self.config.shadow_modes
+    def _plane_waves(self, stream, spectrum, dcorr, C=None):
+        C, K = (self.C if C is None else C), self.config.shadow_modes
         rand = lambda i: self._uniforms(stream + i, C * K).view(self.E, C, K)
         ang = rand(0) * 2 * math.pi
         if spectrum == "sos":
@@ -314,9 +332,88 @@ class NRB200Engine:
             return self._plane_waves(RADIO_STREAM + 16, "exp", SCN[cfg.tr38901_scenario][1])
         return self._plane_waves(LOG_DISTANCE_STREAM, cfg.shadow_acf, cfg.shadow_dcorr_m)
 
+    # ------------------------------------------------------------------ radio map and blockage (radio launch)
+    def _setup_radio(self):
+        """Static part of the radio launch: the radio map on the device (RadioMapChannel, channels/models.py:179-199)
+        and the blockage model A constants and CDF table (BlockageA.__init__, channels/blockage.py:157-170)."""
+        cfg, rm = self.config, self._args.rm
+        self._map = self._blk = None
+        self._obstacles = bool(cfg.blockage)
+        rm.on = int(cfg.channel == "radio_map" or cfg.blockage)
+        self._rpg = self._rblk = None
+        if not rm.on:
+            return
+        E, R, C, dev = self.E, self.R, self.C, self.dev
+        self._rpg = torch.zeros(E, R, C, dtype=torch.float32, device=dev)
+        self._rblk = torch.zeros(E, R, dtype=torch.uint8, device=dev)
+        rm.pg, rm.blk = self._rpg.data_ptr(), self._rblk.data_ptr()
+        if cfg.channel == "radio_map":
+            gain, H, W, bounds, meta = load_radio_map(cfg.radio_map_path)
+            if gain.shape[0] != C:
+                raise ValueError(f"the radio map has {gain.shape[0]} cells but the config has n_cells={C}")
+            want = meta.get("gnb_xy")
+            if want is not None:
+                want = np.asarray(want, dtype=np.float32).reshape(-1, 2)
+                have = np.asarray(cfg.gnb_xy(), dtype=np.float32)
+                if want.shape != have.shape or not np.allclose(want, have, atol=0.5, rtol=1e-5):
+                    raise ValueError(f"the radio map was made for gNBs at {want.tolist()}; set cell_positions_m to "
+                                     "match")
+            self._map = gain.to(dev)
+            x0, y0, x1, y1 = bounds
+            rm.map_on, rm.H, rm.W, rm.map = 1, H, W, self._map.data_ptr()
+            rm.x0, rm.y0 = _f32(x0), _f32(y0)
+            rm.sx, rm.sy = _f32((W - 1) / (x1 - x0)), _f32((H - 1) / (y1 - y0))
+            rm.wm1, rm.hm1, rm.wm2, rm.hm2 = float(W - 1), float(H - 1), float(W - 2), float(H - 2)
+        if cfg.blockage:
+            family = "outdoor" if cfg.channel == "tr38901" and cfg.tr38901_scenario in ("UMi", "UMa") else "indoor"
+            self._blk_family = MODEL_A[family]
+            r = self._blk_family[2]
+            lam = C_LIGHT_38901 / (cfg.carrier_ghz * 1e9)
+            K = cfg.shadow_modes
+            self._cdf = cdf_table(K).to(dev)
+            rm.blockage, rm.Kb, rm.n_table = 1, K, self._cdf.numel()
+            rm.amp_b, rm.ck, rm.max_db = _f32(math.sqrt(2 / K)), _f32(math.pi / lam * r), _f32(cfg.blockage_max_db)
+            h_ut = float(cfg.ue_height_m)
+            if cfg.channel == "tr38901":
+                h_bs = float(cfg.gnb_height_m) if cfg.gnb_height_m is not None else SCN[cfg.tr38901_scenario][0]
+            else:
+                h_bs = float(cfg.gnb_height_m) if cfg.gnb_height_m is not None else h_ut
+            rm.h_ut, rm.h_bs = _f32(h_ut), _f32(h_bs)
+            rm.dt, rm.u_den = _f32(cfg.control_step_ms * 1e-3), float(self._cdf.numel() + 1)
+            rm.table = self._cdf.data_ptr()
+            rm.fma_b = int(einsum_fused(self.R, nat.BLK_REGIONS * K))
+            self._blk_t = torch.zeros(E, dtype=torch.float32, device=dev)
+            rm.t = self._blk_t.data_ptr()
+            self._args.p.los_const = int(cfg.channel == "tr38901" and cfg.tr38901_los == "los")
+
+    def _draw_blockage(self):
+        """Model-A draws of every env (BlockageA._draw, channels/blockage.py:172-186): region fields (RESET streams
+        BLOCKAGE_STREAM + 0..2), azimuth / elevation spans (+ 3, + 4), drift direction (+ 5)."""
+        xr, yr, _, dcorr = self._blk_family
+        K = nat.BLK_REGIONS
+        k, phi = self._plane_waves(BLOCKAGE_STREAM, "exp", dcorr, C=K)
+        ux = self._uniforms(BLOCKAGE_STREAM + 3, K)
+        uy = self._uniforms(BLOCKAGE_STREAM + 4, K)
+        ua = self._uniforms(BLOCKAGE_STREAM + 5, 1).view(self.E)
+        xk = xr[0] + (xr[1] - xr[0]) * ux
+        yk = yr[0] + (yr[1] - yr[0]) * uy
+        ang = 2 * math.pi * ua
+        vel = BLOCKER_SPEED_MPS * torch.stack([torch.cos(ang), torch.sin(ang)], -1)
+        return {"k": k, "phi": phi, "xk": xk.contiguous(), "yk": yk.contiguous(), "vel": vel.contiguous()}
+
     def _make_radio(self):
-        self._fields = self._draw_fields()
-        self._bind_fields()
+        cfg = self.config
+        if cfg.channel != "radio_map":
+            self._fields = self._draw_fields()
+            self._bind_fields()
+        if cfg.blockage:
+            self._blk = self._draw_blockage()
+            rm = self._args.rm
+            b = self._blk
+            rm.bk, rm.bphi, rm.xk, rm.yk, rm.vel = (b["k"].data_ptr(), b["phi"].data_ptr(), b["xk"].data_ptr(),
+                                                    b["yk"].data_ptr(), b["vel"].data_ptr())
+            self._blk_t.zero_()
+        self._radio_ready = True
         self._graphs.clear()
 
     def _bind_fields(self):
@@ -324,12 +421,19 @@ class NRB200Engine:
         self._args.t.fk, self._args.t.fphi = k.data_ptr(), phi.data_ptr()
 
     def _reset_radio(self, m):
-        if self._fields is None:
+        if not self._radio_ready:
             return
-        k, phi = self._draw_fields()
-        k0, p0 = self._fields
-        k0.copy_(torch.where(m.view(1, -1, 1, 1), k, k0))
-        p0.copy_(torch.where(m.view(1, -1, 1), phi, p0))
+        if self._fields is not None:
+            k, phi = self._draw_fields()
+            k0, p0 = self._fields
+            k0.copy_(torch.where(m.view(1, -1, 1, 1), k, k0))
+            p0.copy_(torch.where(m.view(1, -1, 1), phi, p0))
+        if self._blk is not None:       # BlockageA.reset (channels/blockage.py:183-189)
+            new = self._draw_blockage()
+            for n, v in new.items():
+                mv = m.view(1, -1, *([1] * (v.dim() - 2))) if n in ("k", "phi") else m.view(-1, *([1] * (v.dim() - 1)))
+                self._blk[n].copy_(torch.where(mv, v, self._blk[n]))
+            self._blk_t.masked_fill_(m, 0.0)
 
     # ------------------------------------------------------------------ resets
     def _kernel_reset(self, mask):
@@ -374,8 +478,7 @@ class NRB200Engine:
             self._last_snr.zero_()
             self._last_hid.zero_()
             self.last_g = None
-            if self._fields is not None:
-                self._reset_radio(torch.ones(self.E, dtype=torch.bool, device=self.dev))
+            self._reset_radio(torch.ones(self.E, dtype=torch.bool, device=self.dev))
             return
         m = torch.zeros(self.E, dtype=torch.bool, device=self.dev)
         m[ids] = True
@@ -507,6 +610,10 @@ class NRB200Engine:
                 ("pathgain", torch.float32, (E, R, self.C) if self.C > 1 else (E, R)), ("det_env", torch.bool, (E,))]
         if self.C > 1:
             spec.append(("serving_cell", torch.long, (E, R)))
+        if self._obstacles:       # obstacle outputs of the serving link (engine.py:437-448)
+            spec.append(("blocked", torch.bool, (E, R)))
+            if self.config.channel == "tr38901":
+                spec.append(("los", torch.bool, (E, R)))
         off, lay = 0, []
         for n, dt, shape in spec:
             nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
@@ -550,7 +657,7 @@ class NRB200Engine:
             self._last_hid.copy_(cur_hid.to(self.dev, torch.long))
         E, R, S, a, p = self.E, self.R, self.S, self._args, self._args.p
         if (self.graphs and self._steps_done > 0 and not legacy and _pathgain is None and _arrivals is None
-                and snr_db is None and x is not None and x.dim() == 3 and self._fields is not None
+                and snr_db is None and x is not None and x.dim() == 3 and self._radio_ready
                 and getattr(self, "trace_buf", None) is None and getattr(self, "_kernel_events", None) is None):
             return self._graph_step(T, x)
         self._steps_done += 1
@@ -573,7 +680,7 @@ class NRB200Engine:
         elif x is not None and x.dim() == 3:
             pos = x[..., :2].to(self.dev, torch.float32).contiguous()
             keep.append(pos)
-            if self._fields is None:
+            if not self._radio_ready:
                 self._make_radio()
             a.pos = pos.data_ptr()
         else:
@@ -586,6 +693,10 @@ class NRB200Engine:
         p.T = T
         p.s0 = self.s0
         out, o = self._alloc_outputs()
+        if self._obstacles and a.pos is None:     # no poses through the radio: no obstacle outputs
+            o.blocked = o.los = None
+            out.pop("blocked", None)
+            out.pop("los", None)
         a.o = o
         tr = getattr(self, "trace_buf", None)
         a.trace = tr.data_ptr() if tr is not None else None
@@ -638,6 +749,9 @@ class NRB200Engine:
         if gen is not None:
             res["gen_accepted"] = out["gen_accepted"]
             res["gen_bytes"] = out["gen_bytes"]
+        for k in ("los", "blocked"):
+            if k in out:
+                res[k] = out[k]
         self._keep = keep                           # the launch is asynchronous: keep its inputs alive
         return res
 
@@ -719,6 +833,9 @@ class NRB200Engine:
         if self.traffic is not None:
             res["gen_accepted"] = out["gen_accepted"]
             res["gen_bytes"] = out["gen_bytes"]
+        for k in ("los", "blocked"):
+            if k in out:
+                res[k] = out[k]
         return res
 
     # ------------------------------------------------------------------ observability
@@ -750,6 +867,10 @@ class NRB200Engine:
                         "bytes": ((E, R, F), "int64"), "deadline_miss": ((E, R, F), "bool")})
         if self.traffic is not None:
             sch.update({"gen_accepted": ((E, R), "int64"), "gen_bytes": ((E, R), "int64")})
+        if self._obstacles:        # with poses through the radio
+            sch["blocked"] = ((E, R), "bool")
+            if self.config.channel == "tr38901":
+                sch["los"] = ((E, R), "bool")
         return {k: {"shape": s, "dtype": d} for k, (s, d) in sch.items()}
 
     # ------------------------------------------------------------------ state exchange (reference names)
@@ -772,13 +893,23 @@ class NRB200Engine:
         out["eng.last_snr"], out["eng.last_hid"] = self._last_snr, self._last_hid
         if self.C > 1 and getattr(self, "pathgain", None) is not None:
             out["net.pg"] = self.pathgain
+        if self._blk is not None:
+            for n, v in self._blk.items():
+                out["radio.blk." + n] = v
+            out["radio.blk.t"] = self._blk_t
         return out
 
     def load_reference_state(self, snap):
-        """Copy a state dict keyed by the reference's names into the engine's buffers (in place)."""
+        """Copy a state dict keyed by the reference's names into the engine's buffers (in place).  The radio's draws
+        are a function of (seed, env id, episode): envs whose episode the snapshot changes get theirs redrawn, and
+        the blockage clock and draws (radio.blk.*) are taken from the snapshot when it has them."""
+        ep0 = self.episode.clone()
+        blk = {}
         for k, v in snap.items():
             t = torch.as_tensor(np.asarray(v) if not torch.is_tensor(v) else v)
-            if k in self._REF and self._REF[k] in self.st:
+            if k.startswith("radio.blk."):
+                blk[k[len("radio.blk."):]] = t
+            elif k in self._REF and self._REF[k] in self.st:
                 self.st[self._REF[k]].copy_(t.to(self.dev))
             elif k == "net.last_g":
                 self.last_g = None if int(t) < 0 else int(t)
@@ -794,6 +925,15 @@ class NRB200Engine:
                 self._last_snr.copy_(t.to(self.dev))
             elif k == "eng.last_hid":
                 self._last_hid.copy_(t.to(self.dev))
+        if self._radio_ready:
+            changed = self.episode != ep0
+            if bool(changed.any()):
+                self._reset_radio(changed)
+        if blk and self.config.blockage:
+            if not self._radio_ready:
+                self._make_radio()
+            for n, t in blk.items():
+                (self._blk_t if n == "t" else self._blk[n]).copy_(t.to(self.dev))
         if torch.any(self.epoch != 0):
             self._uniform_epoch = None
 
