@@ -730,7 +730,7 @@ class NRB200Engine:
         nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
         if ev is not None:
             ev[1].record()
-        self.prb_avail += float(cfg.nprb) * E * n_ul
+        self.prb_avail += float(cfg.nprb) * E * n_ul * self.C     # every cell's PRBs (mac.py:491)
         self.T = T + 1
         sinr = out.pop("sinr_db") if snr_out is None else snr_out.clone()
         self.pathgain = out.pop("pathgain")
@@ -816,7 +816,7 @@ class NRB200Engine:
         self._steps_done += 1
         self.last_arrivals = ent["arr"]
         out = {n: blob[off:off + nb].view(dt).view(shape) for n, dt, shape, off, nb in spec}
-        self.prb_avail += float(cfg.nprb) * E * n_ul
+        self.prb_avail += float(cfg.nprb) * E * n_ul * self.C     # every cell's PRBs (mac.py:491)
         self.T = T + 1
         sinr = out.pop("sinr_db")
         self.pathgain = out.pop("pathgain")

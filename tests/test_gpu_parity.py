@@ -73,6 +73,8 @@ def test_kernel_equals_oracle_seq_bitwise(case):
         st_o, st_k = orc.reference_state(), eng.reference_state()
         for k, v in st_o.items():
             assert _eq_t(st_k[k], v), f"step {s} state {k}"
+    # the PRBs offered over the run (every cell of every env in every UL slot) as the reference counts them
+    assert eng.counters()["ul"]["prb_avail"] == float(g.state(g.steps - 1)["ctr.prb_avail"])
 
 
 @pytest.mark.parametrize("case", ("1", "2", "4", "3"))
