@@ -31,6 +31,8 @@ namespace inb {
 
 struct SmemGroup {
   unsigned long long red[2][4];   // per-warp partial maxima (GW up to 128: 4 warps), double-buffered
+  unsigned long long redc[2][INB_MAX_C][4];   // per-cell partial (max, lowest lane) pairs (GW > 32)
+  uint32_t redf[2][INB_MAX_C][4];             // per-cell partial flags (GW > 32)
   float rkey[128];
   int32_t rnsb[128];
   int32_t rserv[128];
@@ -111,6 +113,52 @@ struct Grp {
       for (int w = 1; w < GW / 32; ++w) b = sm->red[par][w] > b ? sm->red[par][w] : b;
       par ^= 1;
       mx = (uint32_t)(b >> 32);
+      return 255 - (int)(b & 0xFFu);
+    }
+  }
+  // Per cell: the maximum of `key` over the group's lanes of cell c (c < C <= NC) with the lowest lane holding it
+  // (mx, return value), and whether a lane of cell c has `flag` (anyf); the lanes of cell c must have keys > 0.
+  // As argmax_u32 / any of each cell, but with GW > 32 one block barrier serves every cell and both results.
+  template <int NC>
+  __device__ static int argmax_cell(uint32_t key, bool flag, int c, int C, uint32_t& mx, bool& anyf, SmemGroup* sm,
+                                    int& par) {
+    if constexpr (GW <= 32) {
+      int w = 0;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        uint32_t m;
+        const int wi = argmax_u32(c == cc ? key : 0u, m, sm, par);
+        const bool a = any(flag && c == cc, sm, par);
+        if (cc == c) { w = wi; mx = m; anyf = a; }
+      }
+      return w;
+    } else {
+      const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        const uint32_t kk = c == cc ? key : 0u;
+        const uint32_t m = __reduce_max_sync(0xFFFFFFFFu, kk);
+        const unsigned bl = __ballot_sync(0xFFFFFFFFu, c == cc && kk == m);
+        const unsigned fl = __ballot_sync(0xFFFFFFFFu, flag && c == cc);
+        if (lane == 0) {
+          sm->redc[par][cc][wid] = bl ? (((unsigned long long)m << 32) | (unsigned)(255 - (wid * 32 + __ffs(bl) - 1)))
+                                      : 0ull;
+          sm->redf[par][cc][wid] = fl != 0u ? 1u : 0u;
+        }
+      }
+      __syncthreads();
+      unsigned long long b = sm->redc[par][c][0];
+      uint32_t f = sm->redf[par][c][0];
+#pragma unroll
+      for (int w = 1; w < GW / 32; ++w) {
+        b = sm->redc[par][c][w] > b ? sm->redc[par][c][w] : b;
+        f |= sm->redf[par][c][w];
+      }
+      par ^= 1;
+      mx = (uint32_t)(b >> 32);
+      anyf = f != 0u;
       return 255 - (int)(b & 0xFFu);
     }
   }
@@ -661,30 +709,50 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const float avg_den = fmaxf(avg, 1e-9f);
     const float rr_metric = (float)(g - last_tx);
     {
-      for (uint32_t wm = __ballot_sync(0xFFFFFFFFu, has_rx || new_el); wm; wm &= wm - 1u) {
-        const int a = __ffs(wm) - 1;
-        const int ta = wbase + a;
-        const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
-        const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
-        const float olla_a = __shfl_sync(0xFFFFFFFFu, olla, a);
-        const float avgd_a = __shfl_sync(0xFFFFFFFFu, avg_den, a);
-        const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
-        const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
-        const float pc_a = MC ? __shfl_sync(0xFFFFFFFFu, pcv, a) : 0.0f;
-        if (lane < S) {
-          const int s = lane;
-          const float refs = REF_A(s, ta, ref_a, serv_a);
-          float est;
-          if constexpr (MC) {   // one RBG at the power-control PSD (mac_ul.py:160-161)
-            est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), CSI_A(csrc_a, ra / S, serv_a, s));
-          } else {
-            est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+      const uint32_t wm0 = __ballot_sync(0xFFFFFFFFu, has_rx || new_el);
+      if (__popc(wm0) * 4 > S * 3) {
+        // most robots of the warp want RBGs: each lane evaluates its own robot, RBG by RBG (the same expressions)
+        if (has_rx || new_el) {
+          for (int s = 0; s < S; ++s) {
+            float est;
+            if constexpr (MC) {
+              est = fa(fs(REF(s), fmaxf(s_lw10[s], pcv)), CSI_A(csi_src, er, serv, s));
+            } else {
+              est = fa(fs(REF(s), s_lw10[s]), A.gain[CK(g_csi + er * S + s, GCAP, 13)]);
+            }
+            const float eo = p.olla_on ? fa(est, olla) : fa(est, 0.0f);
+            const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
+            const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
+            v_x[s * NP] = rt;
+            if (p.sched == 0) v_m[s * NP] = x_fdv(rt, avg_den);
           }
-          const float eo = p.olla_on ? fa(est, olla_a) : fa(est, 0.0f);
-          const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
-          const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
-          d_x[s * NP + ta] = rt;
-          if (p.sched == 0) d_m[s * NP + ta] = x_fdv(rt, avgd_a);
+        }
+      } else {
+        for (uint32_t wm = wm0; wm; wm &= wm - 1u) {
+          const int a = __ffs(wm) - 1;
+          const int ta = wbase + a;
+          const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
+          const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
+          const float olla_a = __shfl_sync(0xFFFFFFFFu, olla, a);
+          const float avgd_a = __shfl_sync(0xFFFFFFFFu, avg_den, a);
+          const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
+          const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
+          const float pc_a = MC ? __shfl_sync(0xFFFFFFFFu, pcv, a) : 0.0f;
+          if (lane < S) {
+            const int s = lane;
+            const float refs = REF_A(s, ta, ref_a, serv_a);
+            float est;
+            if constexpr (MC) {   // one RBG at the power-control PSD (mac_ul.py:160-161)
+              est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), CSI_A(csrc_a, ra / S, serv_a, s));
+            } else {
+              est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+            }
+            const float eo = p.olla_on ? fa(est, olla_a) : fa(est, 0.0f);
+            const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
+            const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
+            d_x[s * NP + ta] = rt;
+            if (p.sched == 0) d_m[s * NP + ta] = x_fdv(rt, avgd_a);
+          }
         }
       }
       __syncwarp();
@@ -743,21 +811,24 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         if (lex) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
           const bool wr = want && has_rx;
           bool any_wr = false;
-#pragma unroll
-          for (int cc = 0; cc < NC; ++cc) {
-            if (cc >= C) continue;
-            const bool a_ = Grp<GW>::any(wr && serv == cc, sm, par);   // every lane takes part
-            if (cc == serv) any_wr = a_;
+          if constexpr (MC) {
+            uint32_t mx_;
+            Grp<GW>::template argmax_cell<NC>(1u, wr, serv, C, mx_, any_wr, sm, par);   // every lane takes part
+          } else {
+            any_wr = Grp<GW>::any(wr, sm, par);
           }
           if (any_wr && !wr) mkey = -1.0f;
         }
-        bool oh = false;
-#pragma unroll
-        for (int cc = 0; cc < NC; ++cc) {
-          if (cc >= C) continue;
+        bool oh;
+        if constexpr (MC) {
           uint32_t mx;
-          const int w = Grp<GW>::argmax_u32(serv == cc ? fkey(mkey) : 0u, mx, sm, par);
-          if (cc == serv) oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+          bool unused;
+          const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), false, serv, C, mx, unused, sm, par);
+          oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+        } else {
+          uint32_t mx;
+          const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
+          oh = (w == r) && (fkey_inv(mx) >= 0.0f);
         }
         if (oh) {
           won |= 1u << s;
@@ -775,15 +846,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         for (int s = 0; s < S; ++s) {
           const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
           const float mkey = want ? METRIC(s) : -1.0f;
-          bool oh = false;
-#pragma unroll
-          for (int cc = 0; cc < NC; ++cc) {
-            if (cc >= C) continue;
-            uint32_t mx;
-            const int w = Grp<GW>::argmax_u32(serv == cc ? fkey(mkey) : 0u, mx, sm, par);
-            const bool av = Grp<GW>::any(((rel_rs >> s) & 1u) != 0u && serv == cc, sm, par);
-            if (cc == serv) oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
-          }
+          uint32_t mx;
+          bool av;
+          const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), ((rel_rs >> s) & 1u) != 0u, serv, C, mx, av, sm,
+                                                          par);
+          const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
           if (oh) {
             won |= 1u << s;
             cnt += 1;
