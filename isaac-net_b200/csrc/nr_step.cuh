@@ -36,6 +36,7 @@ struct SmemGroup {
   float rkey[128];
   int32_t rnsb[128];
   int32_t rserv[128];
+  uint32_t rmask[4];              // per-warp ballot of the robots with a retransmission (GW > 32)
 };
 
 // float -> order-preserving u32 (non-NaN inputs)
@@ -769,23 +770,32 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       }
       const int mine = has_rx ? rx_nsb : 0;
       int before = 0;   // several cells: the ranking runs inside each cell (mac.py:313-319)
+      // only robots with a retransmission hold RBGs in this count (the others have mine = 0)
       if constexpr (GW <= 32) {
+        const int gb = lane / GW * GW;   // lane of robot 0 of this group
 #pragma unroll 1
-        for (int j = 0; j < GW; ++j) {
-          const float kj = __shfl_sync(0xFFFFFFFFu, rkey, j, GW);
-          const int nj = __shfl_sync(0xFFFFFFFFu, mine, j, GW);
-          const int sj = MC ? __shfl_sync(0xFFFFFFFFu, serv, j, GW) : 0;
-          if ((!MC || sj == serv) && (kj > rkey || (kj == rkey && j < r))) before += nj;
+        for (unsigned hm = __ballot_sync(0xFFFFFFFFu, has_rx); hm; hm &= hm - 1u) {
+          const int jl = __ffs(hm) - 1;
+          const float kj = __shfl_sync(0xFFFFFFFFu, rkey, jl);
+          const int nj = __shfl_sync(0xFFFFFFFFu, mine, jl);
+          const int sj = MC ? __shfl_sync(0xFFFFFFFFu, serv, jl) : 0;
+          const int j = jl - gb;
+          if (jl >= gb && j < GW && (!MC || sj == serv) && (kj > rkey || (kj == rkey && j < r))) before += nj;
         }
       } else {
         sm->rkey[r] = rkey;
         sm->rnsb[r] = mine;
         sm->rserv[r] = serv;
+        const unsigned hm = __ballot_sync(0xFFFFFFFFu, has_rx);
+        if (lane == 0) sm->rmask[r >> 5] = hm;
         __syncthreads();
 #pragma unroll 1
-        for (int j = 0; j < GW; ++j) {
-          const float kj = sm->rkey[j];
-          if ((!MC || sm->rserv[j] == serv) && (kj > rkey || (kj == rkey && j < r))) before += sm->rnsb[j];
+        for (int w = 0; w < GW / 32; ++w) {
+          for (unsigned m_ = sm->rmask[w]; m_; m_ &= m_ - 1u) {
+            const int j = w * 32 + __ffs(m_) - 1;
+            const float kj = sm->rkey[j];
+            if ((!MC || sm->rserv[j] == serv) && (kj > rkey || (kj == rkey && j < r))) before += sm->rnsb[j];
+          }
         }
         __syncthreads();
       }
