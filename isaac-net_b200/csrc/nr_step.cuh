@@ -196,6 +196,26 @@ struct Grp {
 static __device__ __noinline__ float x_fdv(float a, float b) { return fdv(a, b); }      // IEEE a / b
 static __device__ __noinline__ double x_ddv(double a, double b) { return ddv(a, b); }  // IEEE a / b
 
+// The multi-cell kernel calls its math functions out of line: with three cells' worth of scheduling, association
+// and interference its code otherwise overflows the instruction cache.  The single-cell kernel keeps them inline in
+// its hot per-robot chains.  Same functions, same results.
+static __device__ __noinline__ float x_powf(float b, float x) { return powf(b, x); }
+static __device__ __noinline__ float x_logf(float x) { return logf(x); }
+static __device__ __noinline__ float x_expf(float x) { return expf(x); }
+static __device__ __noinline__ float x_log10f(float x) { return log10f(x); }
+template <bool OUT> __device__ __forceinline__ float m_powf(float b, float x) {
+  if constexpr (OUT) return x_powf(b, x); else return powf(b, x);
+}
+template <bool OUT> __device__ __forceinline__ float m_logf(float x) {
+  if constexpr (OUT) return x_logf(x); else return logf(x);
+}
+template <bool OUT> __device__ __forceinline__ float m_expf(float x) {
+  if constexpr (OUT) return x_expf(x); else return expf(x);
+}
+template <bool OUT> __device__ __forceinline__ float m_log10f(float x) {
+  if constexpr (OUT) return x_log10f(x); else return log10f(x);
+}
+
 // ------------------------------------------------------------------------------------------------ PHY helpers
 // PHY.bler_lookup (isaac_net/core/phy.py:271-285), CUDA torch semantics: division by a python scalar is a multiply
 // by the float32 reciprocal.
@@ -329,9 +349,12 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 }
 
 // ------------------------------------------------------------------------------------------------ the step kernel
-// MC: several cells (A3 association and handover, per-cell schedulers, UL power control and interference)
-template <int GW, bool MC>
+// NCT: the number of cells; NCT > 1 (MC) adds the A3 association and handover, per-cell schedulers, UL power control
+// and interference
+template <int GW, int NCT>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
+  constexpr bool MC = NCT > 1;   // several cells
+  constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
   constexpr int NT = GW > 32 ? GW : 128;
   constexpr int NP = NT + 1;   // row stride of the shared vectors: a warp reading one column across rows is
                                // conflict-free as well as a warp reading one row
@@ -341,7 +364,6 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   __shared__ float s_thr[INB_MAX_MCS], s_se[INB_MAX_MCS], s_beta[INB_MAX_MCS], s_rate[INB_MAX_MCS];
   __shared__ unsigned long long s_ctr[GW > 32 ? 1 : 128 / GW][INB_NCTR];
   constexpr int NG = GW > 32 ? 1 : 128 / GW;   // groups (envs) per block
-  constexpr int NC = MC ? INB_MAX_C : 1;
   __shared__ float s_fld[NG][NC][INB_MAX_KF][3];   // the env's plane waves per cell: kx, ky, phi
   // several cells: per env, the gNBs' N+I per PRB (mW) and its dB value at the start of the slot, this slot's
   // interference accumulator and N+I (dB)
@@ -569,7 +591,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     float sum = 0.0f;
     for (int s = 0; s < S; ++s) sum = s == 0 ? REF(0) : fa(sum, REF(s));
     const float x = fm(fs(fm(sum, p.inv_S), p.phr_min), 0.1f);
-    const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
+    const float nmp = fm((float)p.ref_prbs, m_powf<MC>(10.0f, x));
     n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
   }
 
@@ -685,7 +707,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
       // the env's N+I in dB of this slot, the serving link's reference, power control and the PHR cap
-      for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, log10f(s_ni[gi][i / S][i % S]));
+      for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, m_log10f<MC>(s_ni[gi][i / S][i % S]));
       float pg_s = pg_c[0];
 #pragma unroll
       for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
@@ -694,7 +716,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (p.pc_on) pcv = fs(p.ue_tx, fa(p.pc_p0, fm(p.pc_alpha, fs(p.ue_tx, rx_s))));
       if (p.phr_cap) {
         const float x = fm(fs(fs(rx_s, p.sub_noise), p.phr_min), 0.1f);
-        const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
+        const float nmp = fm((float)p.ref_prbs, m_powf<MC>(10.0f, x));
         n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
       }
       const bool ok = g >= ho_end;              // outside the handover interruption (mac.py:249-251)
@@ -894,7 +916,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    float split = fm(10.0f, m_log10f<MC>(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
     if constexpr (MC) split = fmaxf(split, pcv);   // at least the power-control backoff (mac_ul.py:176-180)
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
@@ -911,7 +933,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       // logsumexp of log(w) over the grant
       const float lmx = warp_max(in ? lw_l : -INFINITY);
       const float lm0 = isinf(lmx) ? 0.0f : lmx;
-      const float lnw_a = fa(logf(ordered_sum(in ? expf(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
+      const float lnw_a = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
       if (lane == a) lnw = lnw_a;
       if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
         // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
@@ -929,7 +951,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float refs = REF_A(s, ta, ref_a, serv_a);
           const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s) : A.gain[CK(g_csi + ra + s, GCAP, 13)];
           const float est_tx = fa(fs(refs, split_a), csi_s);
-          ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+          ng = -m_powf<MC>(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
         const long long trow = (long long)(int)nprb_a * p.MCS;
         // candidates: MCS <= mcs_max with a TBS; the highest first (one lane per RBG), which is the usual outcome;
@@ -943,10 +965,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
           const float mx = warp_max(x);
           const float m0 = isinf(mx) ? 0.0f : mx;
-          const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
+          const float lse = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(x, m0)) : 0.0f, won_a)), m0);
           const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-          const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+          const float tbler = fs(1.0f, m_powf<MC>(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
           if (tbler <= p.target) chosen = m;   // the same value on every lane
         }
         const uint32_t rest = chosen < 0 && cand ? cand & ~(1u << (31 - __clz(cand))) : 0u;
@@ -967,14 +989,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             bool first = true;
             for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
-              const float e = expf(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
+              const float e = m_expf<MC>(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
               sum = first ? e : fa(sum, e);
               first = false;
             }
-            const float lse = fa(logf(sum), m0);
+            const float lse = fa(m_logf<MC>(sum), m0);
             const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
             const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-            const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+            const float tbler = fs(1.0f, m_powf<MC>(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
             pass = tbler <= p.target;
           }
           const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
@@ -1029,7 +1051,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           for (int cc = 0; cc < NC; ++cc) {
             if (cc >= C || cc == serv_a) continue;
             const float psd = fs(fs(fa(pga[cc], p.ue_tx), p.ref_db), split_a);
-            const float prx = powf(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er_a, cc, s), GCAP, 13)]), 0.1f));
+            const float prx = m_powf<MC>(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er_a, cc, s), GCAP, 13)]), 0.1f));
             atomicAdd(&s_if[gi_a][cc][s], prx);
           }
         }
@@ -1038,7 +1060,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       for (int i = r; i < C * S; i += GW) {
         const int cc = i / S, s = i % S;
         const float ni_now = fa(s_if[gi][cc][s], p.noise_mw);
-        s_nadb[gi][cc][s] = fm(10.0f, log10f(ni_now));
+        s_nadb[gi][cc][s] = fm(10.0f, m_log10f<MC>(ni_now));
         s_ni[gi][cc][s] = p.li_alpha == 1.0f ? ni_now : fa(fm(p.li_alpha, ni_now), fm(p.li_beta, s_ni[gi][cc][s]));
         s_if[gi][cc][s] = 0.0f;
       }
@@ -1087,27 +1109,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         } else {
           a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
         }
-        const float negl = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+        const float negl = -m_powf<MC>(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
         x = fa(x_fdv(negl, beta), s_lw[s]);
       }
       const float mx = warp_max(x);
       const float m0 = isinf(mx) ? 0.0f : mx;
-      const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
+      const float lse = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(x, m0)) : 0.0f, won_a)), m0);
       const float eff = db_of(fm(-beta, fs(lse, lnw_a)));
       if (lane == a) eff_tx = eff;
     }
     if (tx) {
       const float eff = eff_tx;
-      const float lin = powf(10.0f, fm(eff, 0.1f));
+      const float lin = m_powf<MC>(10.0f, fm(eff, 0.1f));
       const float comb = p.comb_cc ? fa(comb0, lin) : lin;
-      const float eff_used = fm(10.0f, log10f(clamp_min_t(comb, 1e-9f)));
+      const float eff_used = fm(10.0f, m_log10f<MC>(clamp_min_t(comb, 1e-9f)));
       float cbs, ncb;
       segment(tbs, s_rate[mcs], cbs, ncb);
       int i0;
       float wi;
       cidx(p, cbs, i0, wi);
       const float b = bler_lookup(bgrid, mcs, eff_used, i0, wi);
-      const float p_err = fs(1.0f, powf(fs(1.0f, b), ncb));
+      const float p_err = fs(1.0f, m_powf<MC>(fs(1.0f, b), ncb));
       const float u = uniform_at(key_stream(kenv, (uint32_t)((SITE_BLER_UL << 16) | rel)), (uint32_t)r);
       ok = u >= p_err;
       fail = !ok;
@@ -1214,7 +1236,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll
       for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
       for (int s = 0; s < S; ++s) sum = s == 0 ? s_ni[gi][serv][0] : fa(sum, s_ni[gi][serv][s]);
-      const float snr = fs(fs(fa(pg_s, p.ue_tx), p.ref_db), fm(10.0f, log10f(fm(sum, p.inv_S))));
+      const float snr = fs(fs(fa(pg_s, p.ue_tx), p.ref_db), fm(10.0f, m_log10f<MC>(fm(sum, p.inv_S))));
       out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = snr;
       out_ptr(o.serving_cell, ob)[CK(er, NER, 1)] = serv;
       if (o.pathgain) {

@@ -2,7 +2,7 @@
 // Launch of the fused step kernel for one group width GW (robots per env rounded up to a power of two).
 #include "nr_step.cuh"
 namespace inb {
-template <int GW, bool MC>
+template <int GW, int NCT>
 cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
   constexpr int NT = GW > 32 ? GW : 128;
   const int gpb = GW > 32 ? 1 : 128 / GW;
@@ -10,17 +10,19 @@ cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
   const size_t smem = (size_t)vecs * a.p.S * (NT + 1) * sizeof(float);
   static size_t configured = 0;   // dynamic shared memory above 48 KB needs an opt-in, once per size
   if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(nr_step_kernel<GW, MC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(nr_step_kernel<GW, NCT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     configured = smem;
   }
   dim3 grid((a.p.E + gpb - 1) / gpb), block(NT);
-  nr_step_kernel<GW, MC><<<grid, block, smem, stream>>>(a);
+  nr_step_kernel<GW, NCT><<<grid, block, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
 template <int GW>
 cudaError_t launch_gw(const InbStepArgs& a, cudaStream_t stream) {
-  return a.p.C > 1 ? launch_gw_mc<GW, true>(a, stream) : launch_gw_mc<GW, false>(a, stream);
+  if (a.p.C == 2) return launch_gw_mc<GW, 2>(a, stream);
+  if (a.p.C == 3) return launch_gw_mc<GW, 3>(a, stream);
+  return launch_gw_mc<GW, 1>(a, stream);
 }
 }  // namespace inb
