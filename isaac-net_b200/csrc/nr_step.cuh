@@ -196,26 +196,6 @@ struct Grp {
 static __device__ __noinline__ float x_fdv(float a, float b) { return fdv(a, b); }      // IEEE a / b
 static __device__ __noinline__ double x_ddv(double a, double b) { return ddv(a, b); }  // IEEE a / b
 
-// The multi-cell kernel calls its math functions out of line: with three cells' worth of scheduling, association
-// and interference its code otherwise overflows the instruction cache.  The single-cell kernel keeps them inline in
-// its hot per-robot chains.  Same functions, same results.
-static __device__ __noinline__ float x_powf(float b, float x) { return powf(b, x); }
-static __device__ __noinline__ float x_logf(float x) { return logf(x); }
-static __device__ __noinline__ float x_expf(float x) { return expf(x); }
-static __device__ __noinline__ float x_log10f(float x) { return log10f(x); }
-template <bool OUT> __device__ __forceinline__ float m_powf(float b, float x) {
-  if constexpr (OUT) return x_powf(b, x); else return powf(b, x);
-}
-template <bool OUT> __device__ __forceinline__ float m_logf(float x) {
-  if constexpr (OUT) return x_logf(x); else return logf(x);
-}
-template <bool OUT> __device__ __forceinline__ float m_expf(float x) {
-  if constexpr (OUT) return x_expf(x); else return expf(x);
-}
-template <bool OUT> __device__ __forceinline__ float m_log10f(float x) {
-  if constexpr (OUT) return x_log10f(x); else return log10f(x);
-}
-
 // ------------------------------------------------------------------------------------------------ PHY helpers
 // PHY.bler_lookup (isaac_net/core/phy.py:271-285), CUDA torch semantics: division by a python scalar is a multiply
 // by the float32 reciprocal.
@@ -591,7 +571,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     float sum = 0.0f;
     for (int s = 0; s < S; ++s) sum = s == 0 ? REF(0) : fa(sum, REF(s));
     const float x = fm(fs(fm(sum, p.inv_S), p.phr_min), 0.1f);
-    const float nmp = fm((float)p.ref_prbs, m_powf<MC>(10.0f, x));
+    const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
     n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
   }
 
@@ -707,7 +687,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
       // the env's N+I in dB of this slot, the serving link's reference, power control and the PHR cap
-      for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, m_log10f<MC>(s_ni[gi][i / S][i % S]));
+      for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, log10f(s_ni[gi][i / S][i % S]));
       float pg_s = pg_c[0];
 #pragma unroll
       for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
@@ -716,7 +696,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (p.pc_on) pcv = fs(p.ue_tx, fa(p.pc_p0, fm(p.pc_alpha, fs(p.ue_tx, rx_s))));
       if (p.phr_cap) {
         const float x = fm(fs(fs(rx_s, p.sub_noise), p.phr_min), 0.1f);
-        const float nmp = fm((float)p.ref_prbs, m_powf<MC>(10.0f, x));
+        const float nmp = fm((float)p.ref_prbs, powf(10.0f, x));
         n_max = (int)clampf_t(floorf(x_fdv(nmp, s_w[0])), 1.0f, (float)S);
       }
       const bool ok = g >= ho_end;              // outside the handover interruption (mac.py:249-251)
@@ -916,14 +896,86 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    float split = fm(10.0f, m_log10f<MC>(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
     if constexpr (MC) split = fmaxf(split, pcv);   // at least the power-control backoff (mac_ul.py:176-180)
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
     float lnw = 0.0f;
     int mcs_new = 0;
     long long tbs_new = 0;
-    for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+    uint32_t la_serial = __ballot_sync(0xFFFFFFFFu, tx);   // robots served one at a time below
+    bool rest_only = false;                                // ... for the lane-per-MCS search only
+    if constexpr (MC) {
+      if (__popc(la_serial) >= 6) {
+        // Six or more robots of the warp transmit (the loaded multi-cell configs): each lane evaluates its own robot's
+        // grant, lnw and the top MCS, with the same expressions in the same order (the max order-free, the sums
+        // left to right over the won RBGs); only robots whose top MCS fails take the lane-per-MCS search below, with
+        // their -SINR_lin already in their column.
+        bool more = false;
+        if (tx) {
+          uint32_t kmx = 0u;
+          for (uint32_t bb = won; bb; bb &= bb - 1u) kmx = max(kmx, fkey(s_lw[__ffs(bb) - 1]));
+          const float lmx = fkey_inv(kmx);
+          const float lm0 = isinf(lmx) ? 0.0f : lmx;
+          float sw = 0.0f;
+          for (uint32_t bb = won; bb; bb &= bb - 1u) {
+            const float ev = expf(fs(s_lw[__ffs(bb) - 1], lm0));
+            sw = bb == won ? ev : fa(sw, ev);
+          }
+          lnw = fa(logf(sw), lm0);
+          if (tx_new) {
+            const float off_ = p.olla_on ? olla : 0.0f;
+            for (uint32_t bb = won; bb; bb &= bb - 1u) {
+              const int s_ = __ffs(bb) - 1;
+              const float est_tx = fa(fs(REF(s_), split), CSI_A(csi_src, er, serv, s_));
+              v_x[s_ * NP] = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+            }
+            const long long trow = (long long)(int)n_prb * p.MCS;
+            int mtop = -1, n_cand = 0;
+            for (int m = min(p.mcs_max, p.MCS - 1); m >= 0; --m) {
+              if (A.t.la_tbs[CK(trow + m, NLA, 9)] > 0) {
+                if (mtop < 0) mtop = m;
+                ++n_cand;
+                if (n_cand > 1) break;
+              }
+            }
+            int chosen = -1;
+            if (mtop >= 0) {
+              const float beta = s_beta[mtop];
+              uint32_t kx = 0u;
+              for (uint32_t bb = won; bb; bb &= bb - 1u) {
+                const int s_ = __ffs(bb) - 1;
+                const float x = fa(x_fdv(v_x[s_ * NP], beta), s_lw[s_]);
+                kx = max(kx, fkey(isnan(x) ? -INFINITY : x));
+              }
+              const float mx = fkey_inv(kx);
+              const float m0 = isinf(mx) ? 0.0f : mx;
+              float se = 0.0f;
+              for (uint32_t bb = won; bb; bb &= bb - 1u) {
+                const int s_ = __ffs(bb) - 1;
+                const float ev = expf(fs(fa(x_fdv(v_x[s_ * NP], beta), s_lw[s_]), m0));
+                se = bb == won ? ev : fa(se, ev);
+              }
+              const float lse = fa(logf(se), m0);
+              const float eff = fa(db_of(fm(-beta, fs(lse, lnw))), off_);
+              const float b = bler_lookup(bgrid, mtop, eff, A.t.la_i0[CK(trow + mtop, NLA, 9)],
+                                          A.t.la_wi[CK(trow + mtop, NLA, 9)]);
+              const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + mtop, NLA, 9)]));
+              if (tbler <= p.target) chosen = mtop;
+            }
+            if (chosen >= 0 || n_cand <= 1) {
+              mcs_new = chosen < 0 ? 0 : chosen;
+              tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
+            } else {
+              more = true;
+            }
+          }
+        }
+        la_serial = __ballot_sync(0xFFFFFFFFu, more);
+        rest_only = true;
+      }
+    }
+    for (uint32_t tm = la_serial; tm; tm &= tm - 1u) {
       const int a = __ffs(tm) - 1;
       const int ta = wbase + a;
       const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
@@ -931,10 +983,15 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       const bool in = lane < S && ((won_a >> lane) & 1u);
       const float lw_l = lane < S ? s_lw[lane] : 0.0f;
       // logsumexp of log(w) over the grant
-      const float lmx = warp_max(in ? lw_l : -INFINITY);
-      const float lm0 = isinf(lmx) ? 0.0f : lmx;
-      const float lnw_a = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
-      if (lane == a) lnw = lnw_a;
+      float lnw_a;
+      if (rest_only) {
+        lnw_a = __shfl_sync(0xFFFFFFFFu, lnw, a);
+      } else {
+        const float lmx = warp_max(in ? lw_l : -INFINITY);
+        const float lm0 = isinf(lmx) ? 0.0f : lmx;
+        lnw_a = fa(logf(ordered_sum(in ? expf(fs(lw_l, lm0)) : 0.0f, won_a)), lm0);
+        if (lane == a) lnw = lnw_a;
+      }
       if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
         // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
         // whose TB BLER at the EESM SINR (+ OLLA) meets the target, else 0; MCS scanned downward (the first that
@@ -946,12 +1003,12 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
         const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
         float ng = 0.0f;   // -10^(clamp(est, -30, 60) / 10) of this lane's RBG
-        if (in) {
+        if (in && !rest_only) {
           const int s = lane;
           const float refs = REF_A(s, ta, ref_a, serv_a);
           const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s) : A.gain[CK(g_csi + ra + s, GCAP, 13)];
           const float est_tx = fa(fs(refs, split_a), csi_s);
-          ng = -m_powf<MC>(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
+          ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
         const long long trow = (long long)(int)nprb_a * p.MCS;
         // candidates: MCS <= mcs_max with a TBS; the highest first (one lane per RBG), which is the usual outcome;
@@ -959,21 +1016,22 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const uint32_t cand = __ballot_sync(0xFFFFFFFFu, lane <= p.mcs_max && lane < p.MCS &&
                                                          A.t.la_tbs[CK(trow + (lane < p.MCS ? lane : 0), NLA, 9)] > 0);
         int chosen = -1;
-        if (cand) {
+        if (cand && !rest_only) {
           const int m = 31 - __clz(cand);
           const float beta = s_beta[m];
           const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
           const float mx = warp_max(x);
           const float m0 = isinf(mx) ? 0.0f : mx;
-          const float lse = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(x, m0)) : 0.0f, won_a)), m0);
+          const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
           const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-          const float tbler = fs(1.0f, m_powf<MC>(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+          const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
           if (tbler <= p.target) chosen = m;   // the same value on every lane
         }
         const uint32_t rest = chosen < 0 && cand ? cand & ~(1u << (31 - __clz(cand))) : 0u;
         if (rest) {
-          if (in) d_x[lane * NP + ta] = ng;     // the grant's -SINR_lin into robot a's column (its rates are done)
+          // the grant's -SINR_lin into robot a's column (its rates are done; already there in rest_only mode)
+          if (in && !rest_only) d_x[lane * NP + ta] = ng;
           __syncwarp();
           bool pass = false;
           if ((rest >> lane) & 1u) {
@@ -989,14 +1047,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             bool first = true;
             for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
-              const float e = m_expf<MC>(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
+              const float e = expf(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
               sum = first ? e : fa(sum, e);
               first = false;
             }
-            const float lse = fa(m_logf<MC>(sum), m0);
+            const float lse = fa(logf(sum), m0);
             const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
             const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
-            const float tbler = fs(1.0f, m_powf<MC>(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
+            const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
             pass = tbler <= p.target;
           }
           const uint32_t pm = __ballot_sync(0xFFFFFFFFu, pass);
@@ -1051,7 +1109,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           for (int cc = 0; cc < NC; ++cc) {
             if (cc >= C || cc == serv_a) continue;
             const float psd = fs(fs(fa(pga[cc], p.ue_tx), p.ref_db), split_a);
-            const float prx = m_powf<MC>(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er_a, cc, s), GCAP, 13)]), 0.1f));
+            const float prx = powf(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er_a, cc, s), GCAP, 13)]), 0.1f));
             atomicAdd(&s_if[gi_a][cc][s], prx);
           }
         }
@@ -1060,7 +1118,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       for (int i = r; i < C * S; i += GW) {
         const int cc = i / S, s = i % S;
         const float ni_now = fa(s_if[gi][cc][s], p.noise_mw);
-        s_nadb[gi][cc][s] = fm(10.0f, m_log10f<MC>(ni_now));
+        s_nadb[gi][cc][s] = fm(10.0f, log10f(ni_now));
         s_ni[gi][cc][s] = p.li_alpha == 1.0f ? ni_now : fa(fm(p.li_alpha, ni_now), fm(p.li_beta, s_ni[gi][cc][s]));
         s_if[gi][cc][s] = 0.0f;
       }
@@ -1109,27 +1167,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         } else {
           a_ = fa(fs(refs, split_a), A.gain[CK(g_gain + ra + s, GCAP, 13)]);
         }
-        const float negl = -m_powf<MC>(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+        const float negl = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
         x = fa(x_fdv(negl, beta), s_lw[s]);
       }
       const float mx = warp_max(x);
       const float m0 = isinf(mx) ? 0.0f : mx;
-      const float lse = fa(m_logf<MC>(ordered_sum(in ? m_expf<MC>(fs(x, m0)) : 0.0f, won_a)), m0);
+      const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
       const float eff = db_of(fm(-beta, fs(lse, lnw_a)));
       if (lane == a) eff_tx = eff;
     }
     if (tx) {
       const float eff = eff_tx;
-      const float lin = m_powf<MC>(10.0f, fm(eff, 0.1f));
+      const float lin = powf(10.0f, fm(eff, 0.1f));
       const float comb = p.comb_cc ? fa(comb0, lin) : lin;
-      const float eff_used = fm(10.0f, m_log10f<MC>(clamp_min_t(comb, 1e-9f)));
+      const float eff_used = fm(10.0f, log10f(clamp_min_t(comb, 1e-9f)));
       float cbs, ncb;
       segment(tbs, s_rate[mcs], cbs, ncb);
       int i0;
       float wi;
       cidx(p, cbs, i0, wi);
       const float b = bler_lookup(bgrid, mcs, eff_used, i0, wi);
-      const float p_err = fs(1.0f, m_powf<MC>(fs(1.0f, b), ncb));
+      const float p_err = fs(1.0f, powf(fs(1.0f, b), ncb));
       const float u = uniform_at(key_stream(kenv, (uint32_t)((SITE_BLER_UL << 16) | rel)), (uint32_t)r);
       ok = u >= p_err;
       fail = !ok;
@@ -1236,7 +1294,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll
       for (int cc = 1; cc < NC; ++cc) if (cc == serv) pg_s = pg_c[cc];
       for (int s = 0; s < S; ++s) sum = s == 0 ? s_ni[gi][serv][0] : fa(sum, s_ni[gi][serv][s]);
-      const float snr = fs(fs(fa(pg_s, p.ue_tx), p.ref_db), fm(10.0f, m_log10f<MC>(fm(sum, p.inv_S))));
+      const float snr = fs(fs(fa(pg_s, p.ue_tx), p.ref_db), fm(10.0f, log10f(fm(sum, p.inv_S))));
       out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = snr;
       out_ptr(o.serving_cell, ob)[CK(er, NER, 1)] = serv;
       if (o.pathgain) {
