@@ -286,7 +286,9 @@ def main():
     total_envs = E * world
     value = total_envs * a.steps / (t_ms / 1e3)
     e2e = total_envs * a.steps / (e2e_ms / 1e3)
-    launches = 4 + (1 if eng.dtraffic is not None else 0)   # per graph step: store2, [traffic], fading, MAC, finish
+    radio = bool(eng._args.rm.on)
+    # per graph step: store2, [traffic], [radio], fading, MAC, finish
+    launches = 4 + (1 if eng.dtraffic is not None else 0) + (1 if radio else 0)
     peak, peak_kind = peaks()
     per_launch = b_env(cfg, R) * E
     achieved = per_launch / (k_ms / 1e3) / 1e9
@@ -306,7 +308,8 @@ def main():
             "gpu_launches": a.steps * launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic, "peak_kind": peak_kind,
-                         "kernel": "traffic + fading + MAC + finish kernels of one step",
+                         "kernel": ("traffic + radio + fading + MAC + finish kernels of one step" if radio else
+                                    "traffic + fading + MAC + finish kernels of one step"),
                          "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
             "clocks": clk}
     if rank == 0 and world == 1 and not a.no_cpu:
