@@ -884,6 +884,10 @@ class NRB200Engine:
             "assoc.a3_cand": "a3_cand", "assoc.a3_cnt": "a3_cnt", "assoc.ho_end": "ho_end", "assoc.n_ho": "n_ho",
             "assoc.pending": "pending", "net.ni_ul": "ni_ul"}
 
+    # the radio field the kernel evaluates, under the reference's names (RadioMC.k / phi for log_distance,
+    # TR38901Channel.sf_los for tr38901 with the forced LOS state)
+    _FIELD_KEYS = {"log_distance": ("radio.k", "radio.phi"), "tr38901": ("radio.sf_los.k", "radio.sf_los.phi")}
+
     def reference_state(self):
         """Engine state under the reference's names (ul.*, q.*, net.*, rng.*, eng.*), device tensors (views)."""
         out = {k: self.st[v] for k, v in self._REF.items() if v in self.st}
@@ -897,6 +901,9 @@ class NRB200Engine:
             for n, v in self._blk.items():
                 out["radio.blk." + n] = v
             out["radio.blk.t"] = self._blk_t
+        if self._fields is not None and self.config.channel in self._FIELD_KEYS:
+            kk, pk = self._FIELD_KEYS[self.config.channel]
+            out[kk], out[pk] = self._fields
         return out
 
     def load_reference_state(self, snap):
@@ -904,11 +911,13 @@ class NRB200Engine:
         are a function of (seed, env id, episode): envs whose episode the snapshot changes get theirs redrawn, and
         the blockage clock and draws (radio.blk.*) are taken from the snapshot when it has them."""
         ep0 = self.episode.clone()
-        blk = {}
+        blk, fld = {}, {}
         for k, v in snap.items():
             t = torch.as_tensor(np.asarray(v) if not torch.is_tensor(v) else v)
             if k.startswith("radio.blk."):
                 blk[k[len("radio.blk."):]] = t
+            elif k in self._FIELD_KEYS.get(self.config.channel, ()):
+                fld[k] = t
             elif k in self._REF and self._REF[k] in self.st:
                 self.st[self._REF[k]].copy_(t.to(self.dev))
             elif k == "net.last_g":
@@ -929,11 +938,17 @@ class NRB200Engine:
             changed = self.episode != ep0
             if bool(changed.any()):
                 self._reset_radio(changed)
-        if blk and self.config.blockage:
+        if (blk and self.config.blockage) or fld:
             if not self._radio_ready:
                 self._make_radio()
+        if blk and self.config.blockage:
             for n, t in blk.items():
                 (self._blk_t if n == "t" else self._blk[n]).copy_(t.to(self.dev))
+        if fld and self._fields is not None:    # the shadowing field the kernel evaluates: wave vectors, phases
+            kk, pk = self._FIELD_KEYS[self.config.channel]
+            for key, buf in ((kk, self._fields[0]), (pk, self._fields[1])):
+                if key in fld:
+                    buf.copy_(fld[key].to(self.dev))
         if torch.any(self.epoch != 0):
             self._uniform_epoch = None
 
