@@ -82,7 +82,7 @@ typedef struct {
   float *queue_bytes, *sinr_db;                            /* [E,R] */
   float *pathgain;                                         /* [E,R,C] path gain of every link (dB) */
   uint8_t *det_env;                                        /* [E] */
-  int64_t *serving_cell;                                   /* [E,R] (NULL with one cell) */
+  int64_t *serving_cell;                                   /* [E,R] (0 with one cell; required with C > 1) */
   /* obstacle outputs of the serving link (NULL: not produced; only with blockage and poses through the radio) */
   uint8_t *blocked;                                        /* [E,R] a blockage region is on the direct path */
   uint8_t *los;                                            /* [E,R] LOS state (InbParams.los_const) */

@@ -1309,6 +1309,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       st.n_ho[CK(er, NER, 1)] = n_ho;
     } else {
       out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
+      if (o.serving_cell) out_ptr(o.serving_cell, ob)[CK(er, NER, 1)] = 0;
       if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
       if (o.blocked) out_ptr(o.blocked, ob)[CK(er, NER, 1)] = A.rm.blk[CK(er, NER, 1)] & 1;
     }

@@ -475,7 +475,7 @@ class NRB200Engine:
             self.T = 0
             self.epoch.zero_()
             self._uniform_epoch = 0
-            self._last_snr.zero_()
+            self._last_snr = torch.zeros_like(self._last_snr)   # the last step's output tensor stays the caller's
             self._last_hid.zero_()
             self.last_g = None
             self._reset_radio(torch.ones(self.E, dtype=torch.bool, device=self.dev))
@@ -487,7 +487,7 @@ class NRB200Engine:
         self._kernel_reset(m)
         self.epoch.index_fill_(0, ids, self.T)
         self._uniform_epoch = None
-        self._last_snr.index_fill_(0, ids, 0.0)
+        self._last_snr = self._last_snr.index_fill(0, ids, 0.0)
         self._last_hid.index_fill_(0, ids, 0)
         self._reset_radio(m)
 
@@ -608,8 +608,7 @@ class NRB200Engine:
                 ("gen_accepted", torch.long, (E, R)), ("gen_bytes", torch.long, (E, R)),
                 ("queue_bytes", torch.float32, (E, R)), ("sinr_db", torch.float32, (E, R)),
                 ("pathgain", torch.float32, (E, R, self.C) if self.C > 1 else (E, R)), ("det_env", torch.bool, (E,))]
-        if self.C > 1:
-            spec.append(("serving_cell", torch.long, (E, R)))
+        spec.append(("serving_cell", torch.long, (E, R)))      # 0 with one cell, written by the MAC kernel
         if self._obstacles:       # obstacle outputs of the serving link (engine.py:437-448)
             spec.append(("blocked", torch.bool, (E, R)))
             if self.config.channel == "tr38901":
@@ -636,10 +635,72 @@ class NRB200Engine:
         return out, o
 
     def step(self, t=None, x=None, cur_hid=None, *, snr_db=None, dl_snr_db=None, pathgain_db=None, vel=None,
-             triggers=None, blockers=None, _pathgain=None, _arrivals=None):
+             triggers=None, blockers=None, fetch=None, _pathgain=None, _arrivals=None):
         """Advance [t, t+1). x: poses [E,R,2|3] (through the engine's radio) or SNR [E,R] dB; snr_db= [E,R] or
         [E,R,S]; triggers= feeds event traffic models.  Returns the step dict (or (newest, det_env) in the legacy
-        form step(t, snr, cur_hid))."""
+        form step(t, snr, cur_hid)).
+
+        Host memory: poses x may live on the host (pinned, for an asynchronous copy); they are copied to the device on
+        the engine's input stream, which overlaps the copy with the kernels of the previous step.  fetch= {key: host
+        tensor} fills those host tensors with this step's outputs on the engine's output stream, overlapping the copy
+        with the kernels of the next step; the CUDA event `fetch_done` marks the copies complete (`sync_fetch()` waits
+        for it on the host)."""
+        staged = None
+        if x is not None and torch.is_tensor(x) and x.device.type == "cpu" and x.dim() == 3:
+            x, staged = self._stage_poses(x)
+        res = self._step(t, x, cur_hid, snr_db=snr_db, dl_snr_db=dl_snr_db, pathgain_db=pathgain_db, vel=vel,
+                         triggers=triggers, blockers=blockers, _pathgain=_pathgain, _arrivals=_arrivals)
+        if staged is not None:
+            staged.record(torch.cuda.current_stream(self.dev))     # the staging buffer has been read
+        if fetch:
+            if not isinstance(res, dict):
+                raise ValueError("fetch= needs the dict form of step (no cur_hid)")
+            self._fetch(res, fetch)
+        return res
+
+    # ------------------------------------------------------------------ host <-> device copies off the compute stream
+    def _stage_poses(self, x):
+        """Copy host poses into one of two device staging buffers on the input stream; the current stream waits for
+        the copy.  Returns the buffer and the event to record once the step has read it."""
+        if getattr(self, "_h2d", None) is None:
+            self._h2d = torch.cuda.Stream(self.dev)
+            self._stage = [torch.empty(self.E, self.R, 2, dtype=torch.float32, device=self.dev) for _ in range(2)]
+            self._stage_free = [None, None]
+            self._stage_i = 0
+        i = self._stage_i
+        self._stage_i ^= 1
+        buf = self._stage[i]
+        if self._stage_free[i] is not None:
+            self._h2d.wait_event(self._stage_free[i])          # the step two calls ago has read this buffer
+        with torch.cuda.stream(self._h2d):
+            buf.copy_(x[..., :2], non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(self._h2d)
+        torch.cuda.current_stream(self.dev).wait_event(ready)
+        self._stage_free[i] = torch.cuda.Event()
+        return buf, self._stage_free[i]
+
+    def _fetch(self, res, fetch):
+        if getattr(self, "_d2h", None) is None:
+            self._d2h = torch.cuda.Stream(self.dev)
+        done = torch.cuda.Event()
+        done.record(torch.cuda.current_stream(self.dev))
+        self._d2h.wait_event(done)
+        with torch.cuda.stream(self._d2h):
+            for k, dst in fetch.items():
+                src = res[k]
+                dst.copy_(src, non_blocking=True)
+                src.record_stream(self._d2h)
+            self.fetch_done = torch.cuda.Event()
+            self.fetch_done.record(self._d2h)
+
+    def sync_fetch(self):
+        """Block the host until the last step's fetch= copies are complete."""
+        ev = getattr(self, "fetch_done", None)
+        if ev is not None:
+            ev.synchronize()
+
+    def _step(self, t, x, cur_hid, *, snr_db, dl_snr_db, pathgain_db, vel, triggers, blockers, _pathgain, _arrivals):
         cfg = self.config
         if dl_snr_db is not None:
             raise B200Unsupported("dl_snr_db: the downlink is not built")
@@ -734,7 +795,7 @@ class NRB200Engine:
         self.T = T + 1
         sinr = out.pop("sinr_db") if snr_out is None else snr_out.clone()
         self.pathgain = out.pop("pathgain")
-        self._last_snr.copy_(sinr)
+        self._last_snr = sinr                   # this step's output tensor (never modified in place)
         if legacy:
             return out["newest"], out["det_env"]
         res = {k: out[k] for k in ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "delay",
@@ -743,9 +804,8 @@ class NRB200Engine:
             for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
                 res[k] = out[k]
         res["sinr_db"] = sinr
-        res["serving_cell"] = out["serving_cell"] if self.C > 1 else torch.zeros(E, R, dtype=torch.long,
-                                                                                device=self.dev)
-        res["t"] = (T - self.epoch).clone()
+        res["serving_cell"] = out["serving_cell"]
+        res["t"] = T - self.epoch
         if gen is not None:
             res["gen_accepted"] = out["gen_accepted"]
             res["gen_bytes"] = out["gen_bytes"]
@@ -820,16 +880,15 @@ class NRB200Engine:
         self.T = T + 1
         sinr = out.pop("sinr_db")
         self.pathgain = out.pop("pathgain")
-        self._last_snr.copy_(sinr)
+        self._last_snr = sinr                   # this step's output tensor (never modified in place)
         res = {k: out[k] for k in ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "delay",
                                    "queue_len", "queue_bytes")}
         if self._extras:
             for k in ("arrival", "arrival_slot", "tag", "priority", "bytes", "deadline_miss"):
                 res[k] = out[k]
         res["sinr_db"] = sinr
-        res["serving_cell"] = out["serving_cell"] if self.C > 1 else torch.zeros(E, R, dtype=torch.long,
-                                                                                device=self.dev)
-        res["t"] = (T - self.epoch).clone()
+        res["serving_cell"] = out["serving_cell"]
+        res["t"] = T - self.epoch
         if self.traffic is not None:
             res["gen_accepted"] = out["gen_accepted"]
             res["gen_bytes"] = out["gen_bytes"]
@@ -931,7 +990,7 @@ class NRB200Engine:
             elif k == "eng.epoch":
                 self.epoch.copy_(t.to(self.dev))
             elif k == "eng.last_snr":
-                self._last_snr.copy_(t.to(self.dev))
+                self._last_snr = t.to(self.dev, torch.float32).clone()
             elif k == "eng.last_hid":
                 self._last_hid.copy_(t.to(self.dev))
         if self._radio_ready:
