@@ -15,7 +15,9 @@ collective inside the step), so per-GPU work is fixed ("scaling": "weak").
   value   env-steps/s with the poses already resident in HBM, K steps between a barrier + synchronize pair, timed
           with CUDA events, max over ranks;
   e2e     the same through the public API from pinned host memory: every step copies its poses host -> device and
-          reads the per-robot observations (newest, queue_len, queue_bytes, sinr_db) back device -> host;
+          reads the per-robot observations (newest, queue_len, queue_bytes, sinr_db) back device -> host
+          (engine.step(None, host_poses, fetch=host_buffers): the engine runs both copies on its own streams,
+          overlapped with the kernels of the neighbouring steps; the timed region ends after the last copy);
   roofline  algorithmic bytes of one step (every per-robot state field read and written once at the reference's
           widths, the step-dict outputs and the pose input: 6680 B per robot for config 2) / the average duration of
           the step's four kernels (traffic, fading, MAC, finish: CUDA events around them on their stream, eager
@@ -209,7 +211,7 @@ def run_reference(a):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
     ap.add_argument("--workload", type=int, default=2)
