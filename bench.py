@@ -232,12 +232,14 @@ def main():
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
     eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
-    n_all = a.warmup + 2 * a.steps
-    host_pos = torch.empty(n_all, E, R, 2, dtype=torch.float32).pin_memory()
+    # a ring of NPOS consecutive pose frames of the random walk (at most 512 MB), cycled: the trajectory jumps back
+    # every NPOS steps
+    NPOS = max(4, min(128, (512 << 20) // (E * R * 2 * 4)))
+    host_pos = torch.empty(NPOS, E, R, 2, dtype=torch.float32).pin_memory()
     host_pos[0] = mot.current()
-    for i in range(1, n_all):
+    for i in range(1, NPOS):
         host_pos[i] = mot.advance()
-    dev_pos = host_pos[: a.warmup + a.steps].to(dev)
+    dev_ring = host_pos.to(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(a.steps)]
 
@@ -247,13 +249,13 @@ def main():
         torch.cuda.synchronize()
 
     for i in range(a.warmup):
-        eng.step(None, dev_pos[i])
+        eng.step(None, dev_ring[i % NPOS])
     clocks = Clocks(dev.index)
     barrier()
     clocks.start()
     ev0.record()
     for i in range(a.steps):
-        eng.step(None, dev_pos[a.warmup + i])
+        eng.step(None, dev_ring[(a.warmup + i) % NPOS])
     ev1.record()
     barrier()
     clk = clocks.stop()
@@ -268,7 +270,7 @@ def main():
     for i in range(a.steps):
         # the public API with host buffers: poses from pinned host memory in, observations to pinned host memory
         # out (the engine copies on its own input / output streams, overlapping the copies with the kernels)
-        eng.step(None, host_pos[a.warmup + a.steps + i], fetch=host_obs)
+        eng.step(None, host_pos[(a.warmup + a.steps + i) % NPOS], fetch=host_obs)
     torch.cuda.current_stream(dev).wait_event(eng.fetch_done)
     e1.record()
     barrier()
@@ -277,7 +279,7 @@ def main():
     nk = min(a.steps, 20)
     for i in range(nk):
         eng._kernel_events = kev[i]
-        eng.step(None, dev_pos[a.warmup + i])
+        eng.step(None, dev_ring[(a.warmup + i) % NPOS])
     eng._kernel_events = None
     barrier()
     k_ms = sum(s.elapsed_time(e) for s, e in kev[:nk]) / nk
