@@ -37,6 +37,7 @@ struct SmemGroup {
   int32_t rnsb[128];
   int32_t rserv[128];
   uint32_t rmask[4];              // per-warp ballot of the robots with a retransmission (GW > 32)
+  int32_t bc[2][INB_MAX_C];       // per-cell value broadcast by one lane (GW > 32), double-buffered
 };
 
 // float -> order-preserving u32 (non-NaN inputs)
@@ -161,6 +162,48 @@ struct Grp {
       mx = (uint32_t)(b >> 32);
       anyf = f != 0u;
       return 255 - (int)(b & 0xFFu);
+    }
+  }
+  // true on every lane of the warp (GW <= 32) or block (GW > 32) when any lane there has v; a block barrier for
+  // GW > 32 (which also orders shared-memory writes before it with reads after it)
+  __device__ static bool any_sync(bool v) {
+    if constexpr (GW > 32) {
+      return __syncthreads_or(v) != 0;
+    } else {
+      return __ballot_sync(0xFFFFFFFFu, v) != 0u;
+    }
+  }
+  // OR of v over the group's lanes of cell c (this lane's cell); a block barrier for GW > 32
+  template <int NC>
+  __device__ static uint32_t or_cell(uint32_t v, int c, int C, SmemGroup* sm, int& par) {
+    const int lane = threadIdx.x & 31;
+    if constexpr (GW <= 32) {
+      uint32_t res = 0u;
+#pragma unroll
+      for (int gq = 0; gq < 32 / GW; ++gq) {
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          if (cc >= C) continue;
+          const bool mine = lane / GW == gq && c == cc;
+          const uint32_t o = __reduce_or_sync(0xFFFFFFFFu, mine ? v : 0u);
+          if (mine) res = o;
+        }
+      }
+      return res;
+    } else {
+      const int wid = threadIdx.x >> 5;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        const uint32_t o = __reduce_or_sync(0xFFFFFFFFu, c == cc ? v : 0u);
+        if (lane == 0) sm->redf[par][cc][wid] = o;
+      }
+      __syncthreads();
+      uint32_t res = 0u;
+#pragma unroll
+      for (int w = 0; w < GW / 32; ++w) res |= sm->redf[par][c][w];
+      par ^= 1;
+      return res;
     }
   }
   // as two_or_more_uniform, counting the lanes of each cell (cell index c < C) separately
@@ -816,7 +859,99 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     // several cells: one scheduler per cell on the same RBGs (mac.py:335-345), the argmax over the cell's robots
     const bool contested = MC ? Grp<GW>::two_or_more_in_a_cell_uniform(act && want_cnt > 0, serv, C)
                               : Grp<GW>::two_or_more_uniform(act && want_cnt > 0);
-    if (contested) {
+    if (contested && p.sched == 2) {
+      // Round robin: a robot's metric (slots since its last transmission) is the same on every RBG, so the RBG by
+      // RBG argmax of the generic rounds below keeps picking one robot until it stops wanting, then the next: each
+      // round here finds a cell's winner once (the same key, the same candidates, the same lowest-index tie rule;
+      // with retransmission priority the retransmissions are the candidates while one of them wants) and the winner
+      // takes RBGs from the cell's cursor on while it still wants, exactly the RBGs the per-RBG rounds give it.
+      int cur = 0;   // next RBG of this lane's cell (the same on every lane of the cell)
+      bool live = true;
+#pragma unroll 1
+      for (;;) {
+        const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
+        float mkey = want ? fa(rr_metric, prio) : -1.0f;
+        if (lex) {
+          const bool wr = want && has_rx;
+          bool any_wr = false;
+          uint32_t mx_;
+          Grp<GW>::template argmax_cell<NC>(1u, wr, serv, C, mx_, any_wr, sm, par);
+          if (any_wr && !wr) mkey = -1.0f;
+        }
+        uint32_t mx;
+        bool unused;
+        const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), false, serv, C, mx, unused, sm, par);
+        const bool has = live && cur < S && fkey_inv(mx) >= 0.0f;
+        int ncur = cur;
+        if (has && w == r) {
+          int s = cur;
+          while (s < S && cnt < want_cnt && (has_rx || left > 0.0f)) {
+            won |= 1u << s;
+            cnt += 1;
+            if (!has_rx) left = fs(left, RATE(s));
+            ++s;
+          }
+          ncur = s;
+          if constexpr (GW > 32) sm->bc[par][serv] = ncur;
+        }
+        bool progress;
+        if constexpr (GW > 32) {
+          progress = Grp<GW>::any_sync(has);
+          if (has) cur = sm->bc[par][serv];
+          par ^= 1;
+        } else {
+          const int nc_w = __shfl_sync(0xFFFFFFFFu, ncur, (lane / GW) * GW + w);
+          progress = Grp<GW>::any_sync(has);
+          if (has) cur = nc_w;
+        }
+        live = has;
+        if (!progress) break;
+      }
+      if (!lex) {
+        // retransmissions that won fewer RBGs than their TB needs release them to the new-data robots of their
+        // cell, which take the released RBGs in RBG order by the same rule (mac.py:353-379)
+        const bool short_ = has_rx && (__popc(won) != rx_nsb);
+        const uint32_t rel_rs = short_ ? won : 0u;
+        if (short_) won = 0u;
+        cnt = __popc(won);
+        uint32_t rs = Grp<GW>::template or_cell<NC>(rel_rs, serv, C, sm, par);   // this cell's released RBGs
+        if (Grp<GW>::any_sync(rs != 0u)) {
+          bool live2 = true;
+#pragma unroll 1
+          for (;;) {
+            const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
+            const float mkey = want ? rr_metric : -1.0f;
+            uint32_t mx;
+            bool unused;
+            const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), false, serv, C, mx, unused, sm, par);
+            const bool has = live2 && rs != 0u && fkey_inv(mx) >= 0.0f;
+            uint32_t nrs = rs;
+            if (has && w == r) {
+              while (nrs != 0u && cnt < want_cnt && left > 0.0f) {
+                const int s = __ffs(nrs) - 1;
+                nrs &= nrs - 1u;
+                won |= 1u << s;
+                cnt += 1;
+                left = fs(left, RATE(s));
+              }
+              if constexpr (GW > 32) sm->bc[par][serv] = (int32_t)nrs;
+            }
+            bool progress;
+            if constexpr (GW > 32) {
+              progress = Grp<GW>::any_sync(has);
+              if (has) rs = (uint32_t)sm->bc[par][serv];
+              par ^= 1;
+            } else {
+              const uint32_t nrs_w = __shfl_sync(0xFFFFFFFFu, nrs, (lane / GW) * GW + w);
+              progress = Grp<GW>::any_sync(has);
+              if (has) rs = nrs_w;
+            }
+            live2 = has;
+            if (!progress) break;
+          }
+        }
+      }
+    } else if (contested) {
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);

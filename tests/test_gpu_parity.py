@@ -77,6 +77,44 @@ def test_kernel_equals_oracle_seq_bitwise(case):
     assert eng.counters()["ul"]["prb_avail"] == float(g.state(g.steps - 1)["ctr.prb_avail"])
 
 
+VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round robin without retransmission priority
+    # (the release of short retransmissions' RBGs), round robin on the PF configs, several cells
+    "1_rr_norp": (1, 8, 16, dict(retx_priority=False, ue_tx_dbm=-12.0, max_harq_tx=2)),
+    "2_rr": (2, 16, 32, dict(scheduler="rr", ue_tx_dbm=-8.0)),
+    "2_rr_norp": (2, 16, 32, dict(scheduler="rr", retx_priority=False, ue_tx_dbm=-8.0)),
+    "3_rr_norp": (3, 4, 64, dict(scheduler="rr", retx_priority=False, ue_tx_dbm=-6.0)),
+    "5_norp": (5, 6, 48, dict(retx_priority=False, ue_tx_dbm=-20.0)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(VARIANTS))
+def test_kernel_equals_oracle_seq_bitwise_variants(name):
+    """Free-running on seeded poses: the kernel against the oracle ("seq", same device) fed the kernel's own
+    arrivals and path gains, every output and state tensor bitwise, 12 steps with a partial reset."""
+    wl_i, E, R, over = VARIANTS[name]
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(wl_i)
+    cfg = wl.config(**over)
+    dev = torch.device("cuda:0")
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
+    orc = OracleEngine(cfg, E, R, dev, seed=wl.seed, reduce="seq")
+    mo = presets.Motion(wl_i, E, R, seed=4, step_ms=cfg.control_step_ms)
+    pos = mo.current()
+    for s in range(12):
+        if s == 7:
+            eng.reset([1])
+            orc.reset([1])
+        out = eng.step(None, pos.to(dev))
+        ref = orc.step(None, _arr_dict(eng.last_arrivals), pathgain=eng.pathgain.clone())
+        for k in ref:
+            assert _eq_t(out[k], ref[k]), f"step {s} output {k}"
+        st_o, st_k = orc.reference_state(), eng.reference_state()
+        for k, v in st_o.items():
+            assert _eq_t(st_k[k], v), f"step {s} state {k}"
+        pos = mo.advance()
+    assert eng.counters()["ul"]["tb_retx"] > 0
+
+
 @pytest.mark.parametrize("case", ("1", "2", "4", "3"))
 def test_kernel_radio_matches_oracle(case):
     g = Golden(case)
