@@ -859,6 +859,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     // several cells: one scheduler per cell on the same RBGs (mac.py:335-345), the argmax over the cell's robots
     const bool contested = MC ? Grp<GW>::two_or_more_in_a_cell_uniform(act && want_cnt > 0, serv, C)
                               : Grp<GW>::two_or_more_uniform(act && want_cnt > 0);
+    // the retransmission mask below can only act where a retransmission competes (uniform over the warp / block)
+    const bool lex_mask = lex && contested && Grp<GW>::any_sync(act && has_rx);
     if (contested && p.sched == 2) {
       // Round robin: a robot's metric (slots since its last transmission) is the same on every RBG, so the RBG by
       // RBG argmax of the generic rounds below keeps picking one robot until it stops wanting, then the next: each
@@ -871,7 +873,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       for (;;) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
         float mkey = want ? fa(rr_metric, prio) : -1.0f;
-        if (lex) {
+        if (lex_mask) {
           const bool wr = want && has_rx;
           bool any_wr = false;
           uint32_t mx_;
@@ -956,7 +958,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
         float mkey = want ? fa(METRIC(s), prio) : -1.0f;
-        if (lex) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
+        if (lex_mask) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
           const bool wr = want && has_rx;
           bool any_wr = false;
           if constexpr (MC) {
