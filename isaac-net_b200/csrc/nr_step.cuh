@@ -372,9 +372,11 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 }
 
 // ------------------------------------------------------------------------------------------------ the step kernel
+// RRK: the round-robin scheduler's instance (its allocation by runs; the other schedulers' per-RBG rounds are left
+// out of it, and it out of theirs, which keeps each instance's code smaller).
 // NCT: the number of cells; NCT > 1 (MC) adds the A3 association and handover, per-cell schedulers, UL power control
 // and interference
-template <int GW, int NCT>
+template <int GW, int NCT, bool RRK>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr bool MC = NCT > 1;   // several cells
   constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
@@ -861,9 +863,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
                               : Grp<GW>::two_or_more_uniform(act && want_cnt > 0);
     // the retransmission mask below can only act where a retransmission competes (uniform over the warp / block)
     const bool lex_mask = lex && contested && Grp<GW>::any_sync(act && has_rx);
-    if (contested && p.sched == 2) {
-      // Round robin: a robot's metric (slots since its last transmission) is the same on every RBG, so the RBG by
-      // RBG argmax of the generic rounds below keeps picking one robot until it stops wanting, then the next: each
+    if (contested && RRK) {
+      // Round robin (the RRK instance, p.sched == 2): a robot's metric (slots since its last transmission) is the
+      // same on every RBG, so the RBG by RBG argmax of the generic rounds (the other instances) keeps picking one
+      // robot until it stops wanting, then the next: each
       // round here finds a cell's winner once (the same key, the same candidates, the same lowest-index tie rule;
       // with retransmission priority the retransmissions are the candidates while one of them wants) and the winner
       // takes RBGs from the cell's cursor on while it still wants, exactly the RBGs the per-RBG rounds give it.
@@ -953,7 +956,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           }
         }
       }
-    } else if (contested) {
+    } else if (contested && !RRK) {
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
