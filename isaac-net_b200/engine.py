@@ -932,6 +932,119 @@ class NRB200Engine:
                 sch["los"] = ((E, R), "bool")
         return {k: {"shape": s, "dtype": d} for k, (s, d) in sch.items()}
 
+    # ------------------------------------------------------------------ checkpoints (core/checkpoint.py:1-60, 115-160)
+    _HOST = ("T", "_uniform_epoch", "last_g", "prb_avail", "env_offset", "_steps_done", "seed")
+    _DEV = ("env_id", "episode", "rng_ctr", "ctr", "status", "epoch", "_last_hid", "_last_snr")
+
+    def state_dict(self):
+        """Every piece of engine state as a flat dict {key: tensor clone | host value}: the per-robot MAC / HARQ /
+        queue / fading / association state, the counter-RNG rows, per-env clocks and counters, the radio's draws
+        (made at the first step with poses), the traffic models' state and generator positions, and the host
+        clocks.  load_state_dict on an engine of the same config and size continues exactly like this one (bitwise,
+        same device), as the reference's engine.state_dict() / load_state_dict() guarantee."""
+        sd = {"meta.level": "L2", "meta.backend": "b200", "meta.E": self.E, "meta.R": self.R,
+              "meta.config": repr(sorted(self.config.field_dict().items()))}
+        for n, t in self.st.items():
+            sd["st." + n] = t.clone()
+        for n in self._DEV:
+            sd["eng." + n] = getattr(self, n).clone()
+        for n in self._HOST:
+            sd["host." + n] = getattr(self, n)
+        if getattr(self, "pathgain", None) is not None:
+            sd["eng.pathgain"] = self.pathgain.clone()
+        if self._radio_ready:
+            sd["radio.ready"] = True
+            if self._fields is not None:
+                sd["radio.k"], sd["radio.phi"] = self._fields[0].clone(), self._fields[1].clone()
+            if self._blk is not None:
+                for n, t in self._blk.items():
+                    sd["radio.blk." + n] = t.clone()
+                sd["radio.blk.t"] = self._blk_t.clone()
+        if self.traffic is not None:
+            tg = self.traffic
+            sd["traffic.gen"], sd["traffic.rgen"] = tg.gen.get_state(), tg.rgen.get_state()
+            for i, src in enumerate(tg.sources):
+                for n in src.names:
+                    sd[f"traffic.src{i}.{n}"] = getattr(src, n).clone()
+                sd[f"traffic.src{i}.deferred"] = src.deferred.clone()
+            if self.dtraffic is not None:
+                sd["traffic.calls"] = self.dtraffic.calls.clone()
+        return sd
+
+    def load_state_dict(self, sd, strict=True):
+        """Restore a state_dict() in place: tensors are copied into the engine's own buffers (so captured CUDA graphs
+        keep reading the right memory), generator states and host values are set.  strict: raise on keys that do
+        not belong to this engine and on missing ones (else skip them); the size and config must match."""
+        if sd.get("meta.level") != "L2" or sd.get("meta.backend") != "b200":
+            raise ValueError("not a state_dict of the B200 L2 engine")
+        if (sd.get("meta.E"), sd.get("meta.R")) != (self.E, self.R):
+            raise ValueError(f"state_dict for E, R = {sd.get('meta.E')}, {sd.get('meta.R')}; this engine has "
+                             f"{self.E}, {self.R}")
+        if sd.get("meta.config") != repr(sorted(self.config.field_dict().items())):
+            raise ValueError("state_dict of an engine with another config")
+        mine = set(self.state_dict()) | {"radio.ready", "radio.k", "radio.phi", "radio.blk.k", "radio.blk.phi",
+                                         "radio.blk.xk", "radio.blk.yk", "radio.blk.vel", "radio.blk.t",
+                                         "eng.pathgain"}
+        extra = set(sd) - mine
+        missing = {k for k in self.state_dict() if not k.startswith(("radio.", "eng.pathgain"))} - set(sd)
+        if strict and (extra or missing):
+            raise KeyError(f"state_dict keys not placed: {sorted(extra)}; missing: {sorted(missing)}")
+        cp = lambda dst, key: dst.copy_(sd[key].to(dst.device)) if key in sd else None   # noqa: E731
+        for n, t in self.st.items():
+            cp(t, "st." + n)
+        for n in self._DEV:
+            key = "eng." + n
+            if key not in sd:
+                continue
+            if n == "_last_snr":
+                self._last_snr = sd[key].to(self.dev).clone()
+            else:
+                cp(getattr(self, n), key)
+        old_seed = self.seed
+        for n in self._HOST:
+            if "host." + n in sd:
+                setattr(self, n, sd["host." + n])
+        if self.seed != old_seed:            # the seed key is baked into captured steps
+            self.s0 = seed_key(self.seed)
+            self._args.p.s0 = self.s0
+            self._graphs.clear()
+        if "eng.pathgain" in sd:
+            self.pathgain = sd["eng.pathgain"].to(self.dev).clone()
+        if sd.get("radio.ready"):
+            if not self._radio_ready:
+                self._make_radio()
+            if self._fields is not None:
+                cp(self._fields[0], "radio.k")
+                cp(self._fields[1], "radio.phi")
+            if self._blk is not None:
+                for n, t in self._blk.items():
+                    cp(t, "radio.blk." + n)
+                cp(self._blk_t, "radio.blk.t")
+        elif self._radio_ready:              # the source had not made its radio yet: neither has this engine now
+            self._radio_ready = False
+            self._graphs.clear()
+        if self.traffic is not None:
+            tg = self.traffic
+            if "traffic.gen" in sd:
+                tg.gen.set_state(sd["traffic.gen"])
+                tg.rgen.set_state(sd["traffic.rgen"])
+            for i, src in enumerate(tg.sources):
+                for n in src.names:
+                    cp(getattr(src, n), f"traffic.src{i}.{n}")
+                cp(src.deferred, f"traffic.src{i}.deferred")
+            if self.dtraffic is not None:
+                cp(self.dtraffic.calls, "traffic.calls")
+
+    def save(self, path, extra=None):
+        """state_dict() (plus `extra`) to a file (torch.save), as checkpoint.save(net, path, extra=...)."""
+        torch.save({"format": 1, "state": self.state_dict(), "extra": extra}, path)
+
+    def load(self, path, strict=True):
+        """Restore a file written by save(); returns its `extra`."""
+        d = torch.load(path, map_location="cpu", weights_only=False)
+        self.load_state_dict(d["state"], strict=strict)
+        return d.get("extra")
+
     # ------------------------------------------------------------------ state exchange (reference names)
     _REF = {"ul.sent": "sent", "ul.floor": "floor_", "ul.olla": "olla", "ul.avg": "avg", "ul.bsr": "bsr",
             "ul.sr_t": "sr_t", "ul.last_tx": "last_tx", "ul.csi": "csi", "ul.h_state": "h_state",
