@@ -1,6 +1,7 @@
 """Benchmark of the B200 NR uplink engine: env-steps/s (envs x control steps per second).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 2]
+                    [--scaling weak|strong]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N ...
 
@@ -10,7 +11,8 @@ the MAC kernel (enqueue and arrival gate, radio, the K = 10 slots; nr_step.cuh) 
 (nr_finish.cu), which writes the step dict into a fresh output block.  The default
 workload is BASELINE config 2 (4096 envs x 32 robots, 100 MHz / 18 RBGs, PF, Rician K = 5 dB, mixed periodic +
 Poisson traffic) per GPU; with N GPUs every rank runs its own 4096-env shard (global env ids rank * 4096 + i, no
-collective inside the step), so per-GPU work is fixed ("scaling": "weak").
+collective inside the step), so per-GPU work is fixed ("scaling": "weak").  --scaling strong splits the workload's
+envs evenly over the GPUs instead (config 4: 65536 envs in all, 8192 per GPU in its weak runs).
 
   value   env-steps/s with the poses already resident in HBM, K steps between a barrier + synchronize pair, timed
           with CUDA events, max over ranks;
@@ -180,8 +182,9 @@ def max_over_ranks(vals, dist, dev):
     return t.tolist()
 
 
-def arm_config(wl, cfg, world):
-    return {"workload": wl.name, "envs_per_gpu": wl.E, "robots": wl.R, "slots_per_step": cfg.slots_per_step,
+def arm_config(wl, cfg, world, E=None):
+    return {"workload": wl.name, "envs_per_gpu": E or wl.envs_per_gpu, "robots": wl.R,
+            "slots_per_step": cfg.slots_per_step,
             "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
             "parallelism": f"env shards x{world}", "l2": "state > L2 (no flush needed)"}
 
@@ -218,6 +221,9 @@ def main():
     ap.add_argument("--cpu-envs", type=int, default=256)
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--scaling", default="weak", choices=("weak", "strong"),
+                    help="weak: every GPU runs the workload's per-GPU envs (config 4: 8192 of its 65536); strong: "
+                         "the workload's envs split evenly over the GPUs")
     a = ap.parse_args()
     if a.impl == "reference":
         return run_reference(a)
@@ -228,7 +234,13 @@ def main():
     presets = importlib.import_module("isaac-net_b200.presets")
     wl = presets.workload(a.workload)
     cfg = wl.config()
-    E, R = wl.E, wl.R
+    R = wl.R
+    if a.scaling == "strong":
+        if wl.E % world:
+            raise SystemExit(f"{wl.E} envs do not split evenly over {world} GPUs")
+        E = wl.E // world
+    else:
+        E = wl.envs_per_gpu
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
     eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
@@ -304,9 +316,9 @@ def main():
         except Exception:
             traffic = None
     line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": a.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
-            "config": arm_config(wl, cfg, world),
+            "config": arm_config(wl, cfg, world, E),
             "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": a.steps * launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -22,11 +22,16 @@ RADIO_MAP_CFG5 = os.path.join(_DATA, "radio_map_cfg5.npz")     # baked by data/m
 @dataclass(frozen=True)
 class Workload:
     name: str
-    E: int
+    E: int            # envs of the whole workload
     R: int
     steps: int
     seed: int
     fields: dict
+    E_gpu: int = 0    # envs per GPU of its weak-scaling runs (0: E)
+
+    @property
+    def envs_per_gpu(self):
+        return self.E_gpu or self.E
 
     def config(self, **overrides):
         return NRConfig(**{**self.fields, **overrides})
@@ -58,7 +63,7 @@ def workload(i: int) -> Workload:
         if i == 2:
             f.update(fading_rician=True, rician_k_db=5.0)
             return Workload("cfg2_4096x32_pf_rician", 4096, 32, 1000, 1, f)
-        return Workload("cfg4_65536x128_pf", 65536, 128, 500, 3, f)
+        return Workload("cfg4_65536x128_pf", 65536, 128, 500, 3, f, E_gpu=8192)
     if i == 3:
         f = _common(bandwidth_mhz=100, control_step_ms=10.0, n_cells=3, cell_layout="hex", cell_isd_m=200.0,
                     channel="log_distance", shadow_sigma_db=6.0, shadow_acf="exp", shadow_dcorr_m=20.0,
