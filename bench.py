@@ -298,6 +298,10 @@ def main():
     h2d = E * R * 2 * 4
     d2h = sum(host_obs[k].numel() * host_obs[k].element_size() for k in obs_keys)
     t_ms, e2e_ms, k_ms = max_over_ranks([t_ms, e2e_ms, k_ms], dist, dev)
+    # whole-batch MAC counters of the run: one all_reduce over the ranks (NCCL), after the timed regions
+    sharded = importlib.import_module("isaac-net_b200.sharded")
+    gc = sharded.global_counters(eng)["ul"]
+    stats = {k: gc[k] for k in ("tb_new", "tb_retx", "tb_ok", "tb_fail", "prb_used", "prb_avail")}
     total_envs = E * world
     value = total_envs * a.steps / (t_ms / 1e3)
     e2e = total_envs * a.steps / (e2e_ms / 1e3)
@@ -326,7 +330,7 @@ def main():
                          "kernel": ("traffic + radio + fading + MAC + finish kernels of one step" if radio else
                                     "traffic + fading + MAC + finish kernels of one step"),
                          "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
-            "clocks": clk}
+            "clocks": clk, "mac_counters": stats}
     if rank == 0 and world == 1 and not a.no_cpu:
         line["cpu_baseline"] = cpu_baseline(wl, cfg, a.cpu_envs, a.cpu_steps)
     if rank == 0:

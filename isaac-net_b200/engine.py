@@ -900,9 +900,13 @@ class NRB200Engine:
     # ------------------------------------------------------------------ observability
     def counters(self):
         """{"ul": counters} as NRNet.counters() (nr_engine.py:916-925), folded from the per-env device words."""
-        c = self.ctr.sum(0).cpu()
+        return self.fold_counters(self.ctr.sum(0), self.prb_avail)
+
+    def fold_counters(self, c, prb_avail):
+        """counters() from a summed counter vector c [INB_NCTR] and the PRBs offered (also for sums over shards)."""
+        c = c.cpu()
         res = {k: float(c[i]) for i, k in enumerate(nat.CTR_NAMES)}
-        res["prb_avail"] = self.prb_avail
+        res["prb_avail"] = float(prb_avail)
         H = self.config.max_harq_tx + 1
         res["ntx_hist"] = [float(v) for v in c[nat.CTR_NTX_HIST:nat.CTR_NTX_HIST + H]]
         res["rv_tx"] = [float(v) for v in c[nat.CTR_RV_TX:nat.CTR_RV_TX + H]]

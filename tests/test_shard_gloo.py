@@ -83,11 +83,30 @@ def _worker(rank, port, root, errq):
                     assert ok, f"step {t}: {k} of the gathered shards differs from the unsharded engine"
         mx = bench.max_over_ranks([float(rank), 10.0 - rank], dist, torch.device("cpu"))
         assert mx == [float(WORLD - 1), 10.0], mx
+        _check_stats(rank, cfg)
         dist.barrier()
         dist.destroy_process_group()
     except BaseException as ex:  # report to the parent; the other rank ends on the process-group timeout
         errq.put(f"rank {rank}: {type(ex).__name__}: {ex}")
         raise
+
+
+def _check_stats(rank, cfg):
+    """The shard statistics helpers: counters summed over ranks, per-env rows gathered in global env order."""
+    import importlib
+    import types
+    sharded = importlib.import_module("isaac-net_b200.sharded")
+    engine = importlib.import_module("isaac-net_b200.engine")
+    fake = types.SimpleNamespace(ctr=torch.arange(E_SHARD * 64, dtype=torch.long).view(E_SHARD, 64) * (rank + 1),
+                                 prb_avail=100.0 * (rank + 1), config=cfg)
+    fake.fold_counters = types.MethodType(engine.NRB200Engine.fold_counters, fake)
+    got = sharded.global_counters(fake)["ul"]
+    both = sum(torch.arange(E_SHARD * 64, dtype=torch.long).view(E_SHARD, 64) * (r + 1) for r in range(WORLD)).sum(0)
+    want = fake.fold_counters(both, 100.0 * sum(r + 1 for r in range(WORLD)))["ul"]
+    assert got == want, (got, want)
+    rows = torch.full((E_SHARD, 3), float(rank))
+    g = sharded.gather_env_rows(rows)
+    assert torch.equal(g, torch.cat([torch.full((E_SHARD, 3), float(r)) for r in range(WORLD)]))
 
 
 def _free_port():
