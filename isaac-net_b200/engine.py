@@ -683,16 +683,23 @@ class NRB200Engine:
     def _fetch(self, res, fetch):
         if getattr(self, "_d2h", None) is None:
             self._d2h = torch.cuda.Stream(self.dev)
+            self._fetch_hold = []
+        cur = torch.cuda.current_stream(self.dev)
         done = torch.cuda.Event()
-        done.record(torch.cuda.current_stream(self.dev))
+        done.record(cur)
         self._d2h.wait_event(done)
         with torch.cuda.stream(self._d2h):
             for k, dst in fetch.items():
-                src = res[k]
-                dst.copy_(src, non_blocking=True)
-                src.record_stream(self._d2h)
+                dst.copy_(res[k], non_blocking=True)
             self.fetch_done = torch.cuda.Event()
             self.fetch_done.record(self._d2h)
+        # The copied outputs stay referenced until a later step's fetch, and the compute stream waits for their
+        # copies before the reference is dropped, so their memory is reused only after the copies (cheaper on the
+        # host than per-tensor record_stream bookkeeping).
+        self._fetch_hold.append(([res[k] for k in fetch], self.fetch_done))
+        if len(self._fetch_hold) > 2:
+            _, ev = self._fetch_hold.pop(0)
+            cur.wait_event(ev)
 
     def sync_fetch(self):
         """Block the host until the last step's fetch= copies are complete."""
