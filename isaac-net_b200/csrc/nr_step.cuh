@@ -1177,17 +1177,21 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           if ((rest >> lane) & 1u) {
             const int m = lane;
             const float beta = s_beta[m];
+            // x_s of this lane's MCS kept in the warp's columns of the PF-metric rows (free once RBGs are allocated)
+            float* const xcol = d_m + wbase + lane;
             float mx = -INFINITY;
             for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
-              mx = fmaxf(mx, fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]));
+              const float x = fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]);
+              xcol[s * NP] = x;
+              mx = fmaxf(mx, x);
             }
             const float m0 = isinf(mx) ? 0.0f : mx;
             float sum = 0.0f;
             bool first = true;
             for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
-              const float e = expf(fs(fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]), m0));
+              const float e = expf(fs(xcol[s * NP], m0));
               sum = first ? e : fa(sum, e);
               first = false;
             }
