@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 5
+#define INB_ABI_VERSION 6
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -207,6 +207,8 @@ typedef struct {
   const int64_t *o_base;        /* if set, every pointer in `o` is a byte offset from the address stored here (so a
                                    captured CUDA graph can write each step's outputs into a new block) */
   InbRadio rm;                  /* radio launch (rm.on = 0: none) */
+  const int64_t *det_hid;       /* [E] hypothesis id that det_env checks this step, or NULL = last_hid (the legacy
+                                   step(t, snr, cur_hid) checks cur_hid without making it the enqueue's last_hid) */
 } InbStepArgs;
 
 /* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.

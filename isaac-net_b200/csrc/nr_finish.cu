@@ -83,7 +83,7 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
   const int seg = threadIdx.x / FW, l = threadIdx.x % FW;
   const int segs = blockDim.x / FW;
   const long long T = (A.T_dev != nullptr) ? *A.T_dev : p.T;
-  const long long epoch = A.epoch[e], last_hid = A.last_hid[e];
+  const long long epoch = A.epoch[e], last_hid = A.det_hid != nullptr ? A.det_hid[e] : A.last_hid[e];
   const double lim = da((double)(T + 1), 1e-9);
   bool det_hit = false;
   const int passes = (R + segs - 1) / segs;

@@ -721,8 +721,7 @@ class NRB200Engine:
             raise B200Unsupported("blockers= (screen blockage) is not built")
         T = self._now(t)
         legacy = cur_hid is not None
-        if legacy:
-            self._last_hid.copy_(cur_hid.to(self.dev, torch.long))
+        det_hid = cur_hid.to(self.dev, torch.long).contiguous() if legacy else None
         E, R, S, a, p = self.E, self.R, self.S, self._args, self._args.p
         if (self.graphs and self._steps_done > 0 and not legacy and _pathgain is None and _arrivals is None
                 and snr_db is None and x is not None and x.dim() == 3 and self._radio_ready
@@ -730,6 +729,10 @@ class NRB200Engine:
             return self._graph_step(T, x)
         self._steps_done += 1
         keep = []                                   # tensors whose pointers the launch reads
+        a.det_hid = None
+        if det_hid is not None:       # this step's det_env checks cur_hid; last_hid stays the submit's (engine.py:894)
+            keep.append(det_hid)
+            a.det_hid = det_hid.data_ptr()
         # inputs
         a.pos = a.pathgain_in = a.ul_ref_in = None
         snr_out = None
@@ -834,6 +837,7 @@ class NRB200Engine:
         p.T, p.s0 = 0, self.s0
         a.T_dev = self._ctl.data_ptr()
         a.pos, a.pathgain_in, a.ul_ref_in, a.trace = self._pos_buf.data_ptr(), None, None, None
+        a.det_hid = None
         # output pointers as offsets from the block address stored at _ctl[1] (never 0: a null pointer means "absent")
         if getattr(self, "_lay", None) is None:
             self._lay = self._out_layout(0)

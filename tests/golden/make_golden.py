@@ -16,6 +16,7 @@ from __future__ import annotations
 
 import argparse
 import importlib
+import math
 import os
 import sys
 
@@ -168,17 +169,89 @@ def run_case(i, E, R, steps, resets, every, over, speed=1.0):
     return rec
 
 
+# Policy-driven cases (no traffic models): each step the policy submits messages (engine.submit with per-message
+# tag / priority / deadline extras) and the step takes an SNR input instead of poses: [E,R] through x, or per RBG
+# [E,R,S] through snr_db=; one step (with an [E,R] SNR) uses the legacy form step(t, snr, cur_hid).
+# name: (workload id, E, R, steps, resets {step: env ids}, state every k steps, config overrides, legacy step)
+POLICY_CASES = {
+    "1p": (1, 6, 16, 30, {11: [2]}, 1, dict(traffic=None, msg_sizes=(1500.0, 4000.0), timeout_steps=6), 21),
+}
+
+
+def policy_inputs(E, R, S, steps, seed=17):
+    """The seeded policy and SNR inputs of a policy case (one dict per step, CPU tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for s in range(steps):
+        send = torch.where(torch.rand(E, R, generator=g) < 0.35, torch.randint(1, 3, (E, R), generator=g),
+                           torch.zeros(E, R, dtype=torch.long))
+        det = torch.rand(E, R, generator=g) < 0.3
+        hid = torch.randint(0, 5, (E,), generator=g)
+        tag = torch.randint(1, 5, (E, R), generator=g)
+        prio = torch.randint(0, 3, (E, R), generator=g)
+        dl = torch.where(torch.rand(E, R, generator=g) < 0.5, torch.full((E, R), math.inf),
+                         torch.where(torch.rand(E, R, generator=g) < 0.5, 15.0, 40.0)).double()
+        if s % 3 == 2:
+            snr = torch.randn(E, R, S, generator=g) * 6.0 + 8.0
+        else:
+            snr = torch.randn(E, R, generator=g) * 8.0 + 10.0
+        out.append({"send": send, "det": det, "hid": hid, "tag": tag, "prio": prio, "dline": dl, "snr": snr,
+                    "cur_hid": torch.randint(0, 5, (E,), generator=g)})
+    return out
+
+
+def run_policy_case(i, E, R, steps, resets, every, over, legacy_step):
+    from isaac_net import make_engine as ref_make
+    from isaac_net.core.proto.netsim import Requests as RefReq
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(i)
+    cfg = ref_config(wl, **over)
+    eng = ref_make("L2", E, R, "cpu", cfg, strict=None, seed=wl.seed)
+    rec = {"E": np.int64(E), "R": np.int64(R), "steps": np.int64(steps), "workload": np.int64(i),
+           "policy": np.int64(1), "legacy_step": np.int64(legacy_step)}
+    for k, v in ref_state(eng).items():
+        rec["init/" + k] = v
+    reset_rows = np.full((steps, E), False)
+    for s, inp in enumerate(policy_inputs(E, R, cfg.n_subbands, steps)):
+        if s in resets:
+            reset_rows[s, resets[s]] = True
+            eng.reset(torch.tensor(resets[s]))
+        acc = eng.submit(None, RefReq(inp["send"], inp["det"], inp["hid"]), tag=inp["tag"], priority=inp["prio"],
+                         deadline_ms=inp["dline"])
+        rec[f"s{s}/accepted"] = acc.numpy()
+        for k, v in inp.items():
+            rec[f"s{s}/in.{k}"] = v.numpy()
+        if s == legacy_step:
+            newest, det_env = eng.step(None, inp["snr"], inp["cur_hid"])
+            out = {"newest": newest, "det_env": det_env}
+        elif inp["snr"].dim() == 3:
+            out = eng.step(None, None, snr_db=inp["snr"])
+        else:
+            out = eng.step(None, inp["snr"])
+        for k, v in out.items():
+            rec[f"s{s}/out.{k}"] = v.detach().cpu().clone().numpy()
+        if s % every == 0 or s == steps - 1 or (s + 1) in resets:
+            for k, v in ref_state(eng).items():
+                rec[f"s{s}/st.{k}"] = v
+    rec["resets"] = reset_rows
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF", "/root/reference"))
-    ap.add_argument("--cases", default=",".join(str(k) for k in CASES))
+    ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES)))
     a = ap.parse_args()
     sys.path.insert(0, a.ref)
     sys.path.insert(0, ROOT)
     torch.set_num_threads(8)
     for c in a.cases.split(","):
-        rec = run_case(*CASES[c])
-        rec["overrides"] = np.array(repr(CASES[c][6]))
+        if c in POLICY_CASES:
+            rec = run_policy_case(*POLICY_CASES[c])
+            rec["overrides"] = np.array(repr(POLICY_CASES[c][6]))
+        else:
+            rec = run_case(*CASES[c])
+            rec["overrides"] = np.array(repr(CASES[c][6]))
         path = os.path.join(HERE, f"cfg{c}.npz")
         np.savez_compressed(path, **rec)
         print(path, os.path.getsize(path))

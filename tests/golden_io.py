@@ -7,6 +7,7 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t", "5", "5s", "1b")
+POLICY_CASES = ("1p",)   # policy submits + SNR input (tests/golden/make_golden.py POLICY_CASES)
 
 
 class Golden:
@@ -43,3 +44,12 @@ class Golden:
 
     def reset_ids(self, s):
         return np.nonzero(self.resets[s])[0].tolist()
+
+    @property
+    def legacy_step(self):
+        return int(self.d["legacy_step"]) if "legacy_step" in self.d.files else -1
+
+    def policy(self, s):
+        """The policy case's inputs of step s: send, det, hid, tag, prio, dline, snr, cur_hid (numpy)."""
+        pre = f"s{s}/in."
+        return {k[len(pre):]: self.d[k] for k in self.d.files if k.startswith(pre)}

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import CASES, Golden
+from golden_io import CASES, POLICY_CASES, Golden
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -132,3 +132,48 @@ def test_radio_map_is_the_fixture_map(case):
     with np.load(g.config().radio_map_path) as z:
         assert mk.gain_digest(z["gain_db"]) == str(g.d["radio_map_sha256"])
     assert str(g.d["radio_map_sha256"]) == mk.gain_digest(mk.bake()["gain_db"])
+
+
+def run_policy_step(eng, g, s, dev="cpu", oracle=True):
+    """Drive one step of a policy case: submit with extras, then the SNR step (or the legacy form); returns
+    (accepted, outputs).  eng is the oracle (oracle=True) or the B200 engine."""
+    inp = {k: torch.as_tensor(v).to(dev) for k, v in g.policy(s).items()}
+    if oracle:
+        acc = eng.submit(inp["send"], inp["det"], inp["hid"], tag=inp["tag"], priority=inp["prio"],
+                         deadline_ms=inp["dline"])
+        out = eng.step(snr=inp["snr"], cur_hid=inp["cur_hid"] if s == g.legacy_step else None)
+        if s == g.legacy_step:
+            out = {"newest": out["newest"], "det_env": out["det_env"]}
+        return acc, out
+    import importlib
+    tr = importlib.import_module("isaac-net_b200.traffic")
+    acc = eng.submit(None, tr.Requests(inp["send"], inp["det"], inp["hid"]), tag=inp["tag"], priority=inp["prio"],
+                     deadline_ms=inp["dline"])
+    if s == g.legacy_step:
+        newest, det_env = eng.step(None, inp["snr"], inp["cur_hid"])
+        return acc, {"newest": newest, "det_env": det_env}
+    if inp["snr"].dim() == 3:
+        return acc, eng.step(None, None, snr_db=inp["snr"])
+    return acc, eng.step(None, inp["snr"])
+
+
+@pytest.mark.parametrize("case", POLICY_CASES)
+def test_oracle_aten_bitwise_policy_case(case):
+    """Policy submits with tag / priority / deadline extras, SNR inputs ([E,R] and per RBG) and the legacy step form:
+    the oracle equals the reference bitwise, outputs and state, free-running."""
+    g = Golden(case)
+    o = OracleEngine(g.config(), g.E, g.R, "cpu", seed=g.workload().seed, reduce="aten")
+    assert not _state_diff(o, g.state(-1)), "initial state"
+    for s in range(g.steps):
+        ids = g.reset_ids(s)
+        if ids:
+            o.reset(ids)
+        acc, out = run_policy_step(o, g, s)
+        assert _eq(acc.numpy(), g.d[f"s{s}/accepted"]), f"step {s} accepted"
+        ref = g.outputs(s)
+        assert set(ref) == set(out), (s, set(ref) ^ set(out))
+        for k, v in ref.items():
+            assert _eq(out[k].cpu().numpy(), v), f"step {s} output {k}"
+        if g.has_state(s):
+            bad = _state_diff(o, g.state(s))
+            assert not bad, f"step {s} state {bad}"
