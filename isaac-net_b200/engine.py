@@ -24,6 +24,7 @@ import torch
 from . import _native as nat
 from .config import NRConfig
 from .phy import PhyTables
+from . import invariants as inv
 from .radio_map import cdf_table, load_radio_map
 from .traffic import DeviceTrafficGen, Requests, TrafficGen, generates
 
@@ -161,6 +162,8 @@ class NRB200Engine:
         self._T_dev = self._ctl[0]
         self._pos_buf = None
         self._steps_done = 0
+        # debug / test mode: check the state and the step's message conservation after every step (synchronizes)
+        self.debug_invariants = False
         self._args = nat.InbStepArgs()
         self._fill_static()
         self._setup_radio()
@@ -648,8 +651,16 @@ class NRB200Engine:
         staged = None
         if x is not None and torch.is_tensor(x) and x.device.type == "cpu" and x.dim() == 3:
             x, staged = self._stage_poses(x)
+        q_before = self.queued().clone() if self.debug_invariants else None
         res = self._step(t, x, cur_hid, snr_db=snr_db, dl_snr_db=dl_snr_db, pathgain_db=pathgain_db, vel=vel,
                          triggers=triggers, blockers=blockers, _pathgain=_pathgain, _arrivals=_arrivals)
+        if q_before is not None and isinstance(res, dict):
+            # submitted messages are queued already when the step starts; the step adds the traffic models' ones
+            acc = res["gen_accepted"] if "gen_accepted" in res else torch.zeros_like(q_before)
+            bad = inv.state_violations(self) + inv.step_violations(q_before, acc, res)
+            if bad or int(self.status.item()) != 0:
+                raise RuntimeError(f"engine invariants violated at T={self.T - 1}: {bad}, status "
+                                   f"{int(self.status.item()):#x}")
         if staged is not None:
             staged.record(torch.cuda.current_stream(self.dev))     # the staging buffer has been read
         if fetch:
