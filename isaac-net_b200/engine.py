@@ -164,6 +164,7 @@ class NRB200Engine:
         self._steps_done = 0
         # debug / test mode: check the state and the step's message conservation after every step (synchronizes)
         self.debug_invariants = False
+        self.nvtx = False          # an NVTX range around every step (for nsys / ncu timelines)
         self._args = nat.InbStepArgs()
         self._fill_static()
         self._setup_radio()
@@ -648,6 +649,8 @@ class NRB200Engine:
         tensor} fills those host tensors with this step's outputs on the engine's output stream, overlapping the copy
         with the kernels of the next step; the CUDA event `fetch_done` marks the copies complete (`sync_fetch()` waits
         for it on the host)."""
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(f"inb.step T={self.T}")
         staged = None
         if x is not None and torch.is_tensor(x) and x.device.type == "cpu" and x.dim() == 3:
             x, staged = self._stage_poses(x)
@@ -667,6 +670,8 @@ class NRB200Engine:
             if not isinstance(res, dict):
                 raise ValueError("fetch= needs the dict form of step (no cur_hid)")
             self._fetch(res, fetch)
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
         return res
 
     # ------------------------------------------------------------------ host <-> device copies off the compute stream
