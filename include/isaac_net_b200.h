@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 6
+#define INB_ABI_VERSION 7
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -209,6 +209,10 @@ typedef struct {
   InbRadio rm;                  /* radio launch (rm.on = 0: none) */
   const int64_t *det_hid;       /* [E] hypothesis id that det_env checks this step, or NULL = last_hid (the legacy
                                    step(t, snr, cur_hid) checks cur_hid without making it the enqueue's last_hid) */
+  int32_t phases;               /* 0: the whole step; else a bit mask of the launches of this call: 1 = radio,
+                                   2 = fading, 4 = MAC and finish.  Radio and fading need no arrivals and not each
+                                   other, so a caller may run them on two streams beside the step's traffic arrivals
+                                   and the MAC phase after all of them. */
 } InbStepArgs;
 
 /* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.

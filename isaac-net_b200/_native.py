@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 6
+ABI_VERSION = 7
 MAX_ROWS = 64
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -89,7 +89,7 @@ class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
                 ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
-                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P), ("rm", InbRadio), ("det_hid", P)]
+                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P), ("rm", InbRadio), ("det_hid", P), ("phases", i32)]
 
 
 class InbResetArgs(ctypes.Structure):

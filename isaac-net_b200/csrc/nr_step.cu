@@ -52,13 +52,20 @@ static int launch_all(const InbStepArgs& args, cudaStream_t s) {
   InbStepArgs a = args;
   const InbParams& p = a.p;
   cudaError_t err = cudaSuccess;
+  const bool all = a.phases == 0;
+  const bool radio = all || (a.phases & 1), fading = all || (a.phases & 2), mac = all || (a.phases & 4);
   if (a.rm.on && a.pathgain_in == nullptr) {   // path gains of this step's poses: the MAC reads them
-    err = launch_radio(a, s);
-    if (err != cudaSuccess) return -100 - (int)err;
+    if (radio) {
+      err = launch_radio(a, s);
+      if (err != cudaSuccess) return -100 - (int)err;
+    }
     a.pathgain_in = a.rm.pg;
   }
-  err = launch_fading(a, s);
-  if (err != cudaSuccess) return -100 - (int)err;
+  if (fading) {
+    err = launch_fading(a, s);
+    if (err != cudaSuccess) return -100 - (int)err;
+  }
+  if (!mac) return 0;
   if (p.R <= 16)
     err = launch_step_g16(a, s);
   else if (p.R <= 32)

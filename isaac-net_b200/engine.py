@@ -165,6 +165,7 @@ class NRB200Engine:
         # debug / test mode: check the state and the step's message conservation after every step (synchronizes)
         self.debug_invariants = False
         self.nvtx = False          # an NVTX range around every step (for nsys / ncu timelines)
+        self.concurrent_traffic = True   # graph steps run traffic and radio beside the fading launch
         self._args = nat.InbStepArgs()
         self._fill_static()
         self._setup_radio()
@@ -869,15 +870,41 @@ class NRB200Engine:
             g.register_generator_state(self.traffic.gen)
         arr = None
         with torch.cuda.graph(g, pool=self._pool):
-            if self.traffic is not None:
-                arr = self.dtraffic.step() if self.dtraffic is not None else self.traffic.step(self._T_dev - self.epoch,
-                                                                                               None)
-                for n in nat.ARR_FIELDS:
-                    setattr(a.a, n, getattr(arr, n).data_ptr())
-                p.M = arr.valid.shape[-1]
+            if self.dtraffic is not None and self.concurrent_traffic:
+                # the traffic kernel and the radio launch on a side stream, concurrent with the fading launch (none
+                # of them needs another's results); the MAC launch waits for all
+                main = torch.cuda.current_stream(self.dev)
+                if getattr(self, "_side", None) is None:
+                    self._side = torch.cuda.Stream(self.dev)
+                fork = torch.cuda.Event()
+                fork.record(main)
+                self._side.wait_event(fork)
+                with torch.cuda.stream(self._side):
+                    arr = self.dtraffic.step()
+                    for n in nat.ARR_FIELDS:
+                        setattr(a.a, n, getattr(arr, n).data_ptr())
+                    p.M = arr.valid.shape[-1]
+                    if a.rm.on:
+                        a.phases = 1
+                        nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+                    join = torch.cuda.Event()
+                    join.record(self._side)
+                a.phases = 2
+                nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+                main.wait_event(join)
+                a.phases = 4
+                nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+                a.phases = 0
             else:
-                p.M = 0
-            nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+                if self.traffic is not None:
+                    arr = self.dtraffic.step() if self.dtraffic is not None else \
+                        self.traffic.step(self._T_dev - self.epoch, None)
+                    for n in nat.ARR_FIELDS:
+                        setattr(a.a, n, getattr(arr, n).data_ptr())
+                    p.M = arr.valid.shape[-1]
+                else:
+                    p.M = 0
+                nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
         ent = {"graph": g, "args": a, "arr": arr}
         self._graphs[key] = ent
         return ent
