@@ -20,6 +20,11 @@ namespace inb {
 
 __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
   const InbParams& p = A.p;
+  // the stream salt of each row's FADING draws (the same for every thread): computed once per block
+  __shared__ uint32_t s_salt[INB_MAX_ROWS];
+  for (int k = threadIdx.x; k < p.K_rows; k += blockDim.x)
+    s_salt[k] = salt((uint32_t)((SITE_FADING << 16) | p.rows[k][0]));
+  __syncthreads();
   const long long NER = (long long)p.E * p.R;
   const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (robot, cell, RBG), RBGs fastest
   const int S = p.S;
@@ -58,7 +63,7 @@ __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
   for (int k = 0; k < p.K_rows; ++k) {
     const int rel = p.rows[k][0], uls = p.rows[k][1], fad = p.rows[k][3];
     if (p.fading && fad) {
-      const uint32_t base_f = key_stream(kenv, (uint32_t)((SITE_FADING << 16) | rel));
+      const uint32_t base_f = mix32(kenv ^ s_salt[k]);   // key_stream(kenv, (SITE_FADING << 16) | rel)
       const float rho = p.rowf[k][0], c1 = p.rowf[k][1];
       const float zr = normal_at(base_f, j, two_pi);
       const float zi = normal_at(base_f, j + 1u, two_pi);
