@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 7
+#define INB_ABI_VERSION 8
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -144,6 +144,10 @@ typedef struct {
   float pc_p0, pc_alpha;        /* fractional UL power control: backoff = ue_tx - (P0 + alpha (ue_tx - RSRP)) */
   float li_alpha, li_beta;      /* N+I filter: ni = alpha ni_now + beta ni (beta = float32(1 - alpha)) */
   int32_t los_const;            /* value of the `los` output (the forced tr38901 LOS state) */
+  int32_t pf_rbg;               /* pf_update = "rbg": the PF metric of RBG s uses the average moved by the bytes granted so
+                                   far in the slot, and the average update uses the new TBs' bytes (mac.py:326-330,
+                                   526-555) */
+  int32_t pf_freeze;            /* pf_avg_idle = "freeze": only robots with new data to schedule update their average */
   int32_t field_fma;            /* plane-wave phase k . x as fma(y, k_y, x k_x) (1) or x k_x + y k_y rounded twice (0):
                                    the rounding of the reference's CPU einsum, which takes its BLAS path (fused) when
                                    2 R C K >= 400 (C fields of K waves) and its plain loop (two roundings) below */

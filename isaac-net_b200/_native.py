@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 7
+ABI_VERSION = 8
 MAX_ROWS = 64
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -72,7 +72,7 @@ class InbParams(ctypes.Structure):
                 + [(n, i32) for n in ("C", "ttt", "ho_int", "has_floor", "ho_flush", "pc_on")]
                 + [(n, f32) for n in ("a3_off", "a3_hyst", "floor_rx", "noise_mw", "ue_tx_ref", "ref_db", "pc_p0",
                                       "pc_alpha", "li_alpha", "li_beta")]
-                + [("los_const", i32), ("field_fma", i32)])
+                + [("los_const", i32), ("pf_rbg", i32), ("pf_freeze", i32), ("field_fma", i32)])
 
 
 class InbRadio(ctypes.Structure):

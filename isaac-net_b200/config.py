@@ -327,8 +327,6 @@ class NRConfig:
                ("ul_grant_model", "the SR/BSR grant pipeline is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),
                ("ul_tpc", "closed-loop power control is not built"),
-               ("pf_update", "per-RBG PF updates are not built"),
-               ("pf_avg_idle", "frozen PF averages are not built"),
                ("ul_retx_sched", "TDMA retransmissions are not built"),
                ("ul_amc_alloc", "previous-allocation AMC is not built"),
                ("eff_sinr", "only EESM is built"),
@@ -351,6 +349,11 @@ class NRConfig:
         for name, why in chk:
             if getattr(self, name) != getattr(d, name):
                 out.append((f"{name}={getattr(self, name)!r}", why))
+        if self.pf_update not in ("slot", "rbg") or self.pf_avg_idle not in ("decay", "freeze"):
+            out.append((f"pf_update={self.pf_update!r} / pf_avg_idle={self.pf_avg_idle!r}", "unknown PF option"))
+        if self.pf_update == "rbg" and self.scheduler != "pf":
+            out.append((f"pf_update='rbg' with scheduler={self.scheduler!r}", "per-RBG PF updates need the pf "
+                                                                              "scheduler"))
         if self.scheduler not in ("pf", "rr", "maxci"):
             out.append((f"scheduler={self.scheduler!r}", "schedulers built: pf, rr, maxci"))
         if self.harq_combining not in ("cc", "none"):

@@ -808,6 +808,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
 #define RATE(s) v_x[(s) * NP]
 #define METRIC(s) (p.sched == 2 ? rr_metric : (p.sched == 1 ? RATE(s) : v_m[(s) * NP]))
+    // the allocation's metric of RBG s: with pf_update = "rbg" the PF rate over the average moved by the bytes this
+    // robot has been granted so far in the slot (MacLink._rbg_metric, mac.py:526-532), else the slot metric
+    const float pf_base = fm(p.pf_a, avg);
+    float got = 0.0f;
+#define AMET(s) (p.pf_rbg ? x_fdv(RATE(s), fmaxf(fa(pf_base, fm(p.pf_b, got)), 1e-9f)) : METRIC(s))
     // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit (mac.py:300-312)
     if (Grp<GW>::any_uniform(has_rx, sm, par)) {
       float rkey = -1.0f;
@@ -960,7 +965,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll 1
       for (int s = 0; s < S; ++s) {
         const bool want = act && (cnt < want_cnt) && (has_rx || left > 0.0f);
-        float mkey = want ? fa(METRIC(s), prio) : -1.0f;
+        float mkey = want ? fa(AMET(s), prio) : -1.0f;
         if (lex_mask) {   // while a retransmission wants RBG s, the new-data robots of the cell are masked out
           const bool wr = want && has_rx;
           bool any_wr = false;
@@ -986,6 +991,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         if (oh) {
           won |= 1u << s;
           cnt += 1;
+          if (p.pf_rbg) got = fa(got, RATE(s));
           if (!has_rx) left = fs(left, RATE(s));
         }
       }
@@ -998,7 +1004,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll 1
         for (int s = 0; s < S; ++s) {
           const bool want = act && (cnt < want_cnt) && new_el && (left > 0.0f);
-          const float mkey = want ? METRIC(s) : -1.0f;
+          const float mkey = want ? AMET(s) : -1.0f;
           uint32_t mx;
           bool av;
           const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), ((rel_rs >> s) & 1u) != 0u, serv, C, mx, av, sm,
@@ -1007,6 +1013,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           if (oh) {
             won |= 1u << s;
             cnt += 1;
+            if (p.pf_rbg) got = fa(got, RATE(s));
             left = fs(left, RATE(s));
           }
         }
@@ -1016,9 +1023,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 #pragma unroll 1
         for (int s = 0; s < S && cnt < want_cnt; ++s) {
           if (!(has_rx || left > 0.0f)) break;
-          if (fa(METRIC(s), prio) >= 0.0f) {
+          if (fa(AMET(s), prio) >= 0.0f) {
             won |= 1u << s;
             cnt += 1;
+            if (p.pf_rbg) got = fa(got, RATE(s));
             if (!has_rx) left = fs(left, RATE(s));
           }
         }
@@ -1026,6 +1034,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       // a short retransmission releases its RBGs; with no other candidate nobody takes them
       if (!lex && has_rx && (__popc(won) != rx_nsb)) won = 0u;
     }
+#undef AMET
 #undef METRIC
 #undef RATE
     const int n_sb = __popc(won);
@@ -1380,7 +1389,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     if (tx) bsr = enq - sent;
     if constexpr (MC) csi_src = u;   // the serving link's gain of this row is the CSI of the next decision
     ++u;
-    avg = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, (float)served)), 1e-9f);
+    if (!p.pf_rbg && !p.pf_freeze) {
+      avg = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, (float)served)), 1e-9f);
+    } else {   // MacLink._pf_update's other branch (mac.py:545-552)
+      const float upd = p.pf_rbg ? fm((float)(tbs_new / 8), tx_new ? 1.0f : 0.0f) : (float)served;
+      const float na = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, upd)), 1e-9f);
+      if (!p.pf_freeze || (need > 0 && !has_rx)) avg = na;
+    }
     if (p.sched == 2 && tx) last_tx = g;
     if (tx) {   // counters (only transmitting robots have any to add)
       if (tx_new) {

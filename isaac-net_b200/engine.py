@@ -237,6 +237,7 @@ class NRB200Engine:
         p.olla_dn = _f32(cfg.olla_up_db * (1 - cfg.bler_target) / cfg.bler_target)
         p.pf_a = _f32(1 - 1 / cfg.pf_window)
         p.pf_b = _f32(1 / cfg.pf_window)
+        p.pf_rbg, p.pf_freeze = int(cfg.pf_update == "rbg"), int(cfg.pf_avg_idle == "freeze")
         p.target = _f32(cfg.bler_target)
         p.inv_S = _f32(1.0 / self.S)
         p.s0_snr, p.c0_cbs = _f32(tab.s0), _f32(tab.c0)

@@ -53,6 +53,11 @@ CASES = {
     # terms active; a 3 m mast puts most links inside the regions' elevation window)
     "1b": (1, 4, 16, 24, {10: [2]}, 2, dict(blockage=True, blockage_model="stochastic", ue_tx_dbm=-10.0,
                                             gnb_height_m=3.0)),
+    # 5G-LENA PF switches: the average moves after every RBG (pf_update="rbg") and idle robots keep theirs
+    # (pf_avg_idle="freeze"); with retransmission priority off (released RBGs), and with three cells
+    "2r": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", retx_priority=False,
+                                           ue_tx_dbm=-6.0)),
+    "3r": (3, 2, 64, 16, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze")),
 }
 
 
