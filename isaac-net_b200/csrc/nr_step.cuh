@@ -372,14 +372,17 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 }
 
 // ------------------------------------------------------------------------------------------------ the step kernel
-// RRK: the round-robin scheduler's instance (its allocation by runs; the other schedulers' per-RBG rounds are left
-// out of it, and it out of theirs, which keeps each instance's code smaller).
+// SV: the scheduler variant.  1 is the round-robin scheduler's instance (its allocation by runs; the other
+// schedulers' per-RBG rounds are left out of it, and it out of theirs, which keeps each instance's code smaller); 2 is
+// the PF instance with pf_update = "rbg" (the per-RBG metric over the bytes granted so far); 0 is every other case.
 // NCT: the number of cells; NCT > 1 (MC) adds the A3 association and handover, per-cell schedulers, UL power control
 // and interference
-template <int GW, int NCT, bool RRK>
+template <int GW, int NCT, int SV>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr bool MC = NCT > 1;   // several cells
   constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
+  constexpr bool RRK = SV == 1;  // round-robin allocation by runs (p.sched == 2)
+  constexpr bool PFR = SV == 2;  // per-RBG PF metric and update (p.pf_rbg)
   constexpr int NT = GW > 32 ? GW : 128;
   constexpr int NP = NT + 1;   // row stride of the shared vectors: a warp reading one column across rows is
                                // conflict-free as well as a warp reading one row
@@ -812,7 +815,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     // robot has been granted so far in the slot (MacLink._rbg_metric, mac.py:526-532), else the slot metric
     const float pf_base = fm(p.pf_a, avg);
     float got = 0.0f;
-#define AMET(s) (p.pf_rbg ? x_fdv(RATE(s), fmaxf(fa(pf_base, fm(p.pf_b, got)), 1e-9f)) : METRIC(s))
+#define AMET(s) (PFR ? x_fdv(RATE(s), fmaxf(fa(pf_base, fm(p.pf_b, got)), 1e-9f)) : METRIC(s))
     // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit (mac.py:300-312)
     if (Grp<GW>::any_uniform(has_rx, sm, par)) {
       float rkey = -1.0f;
@@ -991,7 +994,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         if (oh) {
           won |= 1u << s;
           cnt += 1;
-          if (p.pf_rbg) got = fa(got, RATE(s));
+          if (PFR) got = fa(got, RATE(s));
           if (!has_rx) left = fs(left, RATE(s));
         }
       }
@@ -1013,7 +1016,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           if (oh) {
             won |= 1u << s;
             cnt += 1;
-            if (p.pf_rbg) got = fa(got, RATE(s));
+            if (PFR) got = fa(got, RATE(s));
             left = fs(left, RATE(s));
           }
         }
@@ -1026,7 +1029,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           if (fa(AMET(s), prio) >= 0.0f) {
             won |= 1u << s;
             cnt += 1;
-            if (p.pf_rbg) got = fa(got, RATE(s));
+            if (PFR) got = fa(got, RATE(s));
             if (!has_rx) left = fs(left, RATE(s));
           }
         }
@@ -1389,10 +1392,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     if (tx) bsr = enq - sent;
     if constexpr (MC) csi_src = u;   // the serving link's gain of this row is the CSI of the next decision
     ++u;
-    if (!p.pf_rbg && !p.pf_freeze) {
+    if (!PFR && !p.pf_freeze) {
       avg = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, (float)served)), 1e-9f);
     } else {   // MacLink._pf_update's other branch (mac.py:545-552)
-      const float upd = p.pf_rbg ? fm((float)(tbs_new / 8), tx_new ? 1.0f : 0.0f) : (float)served;
+      const float upd = PFR ? fm((float)(tbs_new / 8), tx_new ? 1.0f : 0.0f) : (float)served;
       const float na = fmaxf(fa(fm(p.pf_a, avg), fm(p.pf_b, upd)), 1e-9f);
       if (!p.pf_freeze || (need > 0 && !has_rx)) avg = na;
     }

@@ -84,6 +84,9 @@ VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round r
     "2_rr_norp": (2, 16, 32, dict(scheduler="rr", retx_priority=False, ue_tx_dbm=-8.0)),
     "3_rr_norp": (3, 4, 64, dict(scheduler="rr", retx_priority=False, ue_tx_dbm=-6.0)),
     "5_norp": (5, 6, 48, dict(retx_priority=False, ue_tx_dbm=-20.0)),
+    # the PF switches of 5G-LENA (the per-RBG metric and update, frozen idle averages) on one and three cells
+    "2_pf_rbg": (2, 16, 32, dict(pf_update="rbg", ue_tx_dbm=-8.0)),
+    "3_pf_rbg_freeze": (3, 4, 64, dict(pf_update="rbg", pf_avg_idle="freeze", ue_tx_dbm=-6.0)),
 }
 
 
