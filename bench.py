@@ -211,6 +211,37 @@ def run_reference(a):
     print(json.dumps(line))
 
 
+def net_obs_bytes(F, K, dim, R):
+    """Algorithmic bytes per robot of one observation-packing launch: the step-dict fields it reads (newest,
+    queue_len, serving 8 B each; queue_bytes, sinr 4 B; delivered F B, cap 8F B, delay 4F B), its state read and
+    written (last_cap 8 B, history 4K B), its outputs (last_cap 8 B, aoi 4 B, delay_s 4F B, rsrp 4 B, x 4 dim B,
+    three flags) and the per-env t / det_env / cur_tag (17 B per env, shared by the R robots)."""
+    return 8 * 3 + 4 * 2 + 13 * F + 2 * (8 + 4 * K) + 8 + 4 + 4 * F + 4 + 4 * dim + 3 + 17.0 / R
+
+
+def net_obs_timing(o, cfg, E, R, dev, n=50):
+    """Average device time of the observation packing (inb_net_obs, every feature selected, history 4) over n
+    launches on the bench engine's step dict `o`, CUDA events around them on their stream."""
+    nm = importlib.import_module("isaac-net_b200.net_module")
+    pk = nm.ObsPacker(nm.OBS_FEATURES, E, R, cfg.frame_buffer, cfg.n_cells, 4, cfg.control_step_ms / 1000.0,
+                      cfg.subband_noise_dbm, 50 * cfg.control_step_ms / 1000.0,
+                      cfg.frame_buffer * max(cfg.msg_sizes), dev)
+    cur = torch.zeros(E, dtype=torch.long, device=dev)
+    for _ in range(3):
+        pk.step(o, cur)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record()
+    for _ in range(n):
+        pk.step(o, cur)
+    b.record()
+    torch.cuda.synchronize()
+    us = a.elapsed_time(b) / n * 1e3
+    per = net_obs_bytes(cfg.frame_buffer, 4, pk.dim, R)
+    return {"kernel_us": us, "bytes_per_launch": per * E * R, "features": "all 12, history 4",
+            "launches_per_step": 1}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -291,13 +322,16 @@ def main():
     nk = min(a.steps, 20)
     for i in range(nk):
         eng._kernel_events = kev[i]
-        eng.step(None, dev_ring[(a.warmup + i) % NPOS])
+        last_o = eng.step(None, dev_ring[(a.warmup + i) % NPOS])
     eng._kernel_events = None
     barrier()
     k_ms = sum(s.elapsed_time(e) for s, e in kev[:nk]) / nk
     h2d = E * R * 2 * 4
     d2h = sum(host_obs[k].numel() * host_obs[k].element_size() for k in obs_keys)
-    t_ms, e2e_ms, k_ms = max_over_ranks([t_ms, e2e_ms, k_ms], dist, dev)
+    obs = net_obs_timing(last_o, cfg, E, R, dev)
+    t_ms, e2e_ms, k_ms, obs_us = max_over_ranks([t_ms, e2e_ms, k_ms, obs["kernel_us"]], dist, dev)
+    obs["kernel_us"] = obs_us
+    obs["achieved_gbs"] = obs["bytes_per_launch"] / (obs_us * 1e-6) / 1e9
     # whole-batch MAC counters of the run: one all_reduce over the ranks (NCCL), after the timed regions
     sharded = importlib.import_module("isaac-net_b200.sharded")
     gc = sharded.global_counters(eng)["ul"]
@@ -331,6 +365,8 @@ def main():
                                     "traffic + fading + MAC + finish kernels of one step"),
                          "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
             "clocks": clk, "mac_counters": stats}
+    obs["frac"] = obs["achieved_gbs"] / peak
+    line["net_obs"] = obs
     if rank == 0 and world == 1 and not a.no_cpu:
         line["cpu_baseline"] = cpu_baseline(wl, cfg, a.cpu_envs, a.cpu_steps)
     if rank == 0:

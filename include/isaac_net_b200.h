@@ -20,6 +20,8 @@
  *   inb_traffic_step   TrafficGen.step (isaac_net/core/traffic.py:408-430) with _Stream._step (traffic.py:301-365) for
  *                      periodic, video and bursty models: the step's arrivals [E,R,M] from the engine's
  *                      torch.Generator stream (CUDA Philox), reproduced draw for draw.
+ *   inb_net_obs        the Isaac-side consumer of the step dict: NetModule.step's post-processing
+ *                      (isaac_net/isaac/net_module.py:340-374) and NetObs.update (isaac_net/isaac/obs.py:48-87).
  * Status: 0 = launched; negative = invalid arguments (nothing launched).  Kernel-side faults are reported in the
  * int32 device status word `status` (0 = ok), which the host reads only when it asks for it.
  */
@@ -32,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 8
+#define INB_ABI_VERSION 9
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -302,6 +304,32 @@ int inb_traffic_step(const InbTrafficArgs *args, void *cuda_stream);
 /* Store two int64 values at dst[0], dst[1] in stream order (e.g. the control step and the output block address that
  * a captured step reads through T_dev / o_base). */
 int inb_store2(int64_t *dst, int64_t v0, int64_t v1, void *cuda_stream);
+
+/* Network observation packing of one control step: what isaac-net's Isaac-side module does with the engine's step
+ * dict on the engine's own radio.  Replaces NetModule.step's post-processing (isaac_net/isaac/net_module.py:340-374:
+ * last_cap = max(last_cap, newest), aoi_s = (t + 1 - last_cap).float() * step_dt, delay_s = delay * step_dt,
+ * rsrp_dbm = sinr_db + noise, blocked / los defaults, tag_delivered) and NetObs.update (isaac_net/isaac/obs.py:48-87:
+ * the delay history and the selected features, normalised, into x [E,R,dim]).  Inputs are the step dict's device
+ * tensors; last_cap [E,R] and hist [E,R,K] are the caller's persistent state, updated in place.  Outputs left NULL
+ * are not written.  The float inputs of the normalisation are the float32 values torch uses on a CUDA device:
+ * step_dt and noise_db rounded to float32, inv_* = 1.0f / float32(divisor).  -2: sizes out of range; -3: a required
+ * pointer is NULL; -4: a feature column beyond dim. */
+typedef struct {
+  int32_t E, R, F, G, K, dim;   /* envs, robots, frame slots, gNBs (one-hot width), delay-history length, x width */
+  int32_t off_mask, off_delay, off_aoi, off_qlen, off_qbytes, off_sinr, off_rsrp, off_serv, off_last, off_hist,
+          off_blocked, off_los;   /* first column of each feature in x (isaac/config.py OBS_FEATURES), -1 = off */
+  float step_dt, inv_ts, inv_F, inv_qbytes, inv_db, noise_db;
+  const int64_t *newest, *t, *queue_len, *serving;   /* [E,R], [E], [E,R], [E,R] */
+  const float *queue_bytes, *sinr_db, *delay;        /* [E,R], [E,R], [E,R,F] (control steps, NaN = none) */
+  const uint8_t *delivered, *blocked, *los, *det_env; /* [E,R,F]; [E,R] or NULL (defaults); [E,R] or NULL; [E] */
+  const int64_t *cap, *cur_tag;                      /* [E,R,F]; [E] or NULL (no tag_delivered) */
+  int64_t *last_cap;            /* [E,R] state: newest capture step delivered this episode */
+  float *hist;                  /* [E,R,K] state: delay history, newest first */
+  int64_t *last_cap_out;        /* [E,R] */
+  float *aoi_s, *delay_s, *rsrp_dbm, *x;             /* [E,R], [E,R,F], [E,R], [E,R,dim] */
+  uint8_t *delivered_any, *blocked_out, *los_out, *tag_delivered;   /* [E,R], [E,R], [E,R], [E] */
+} InbObsArgs;
+int inb_net_obs(const InbObsArgs *args, void *cuda_stream);
 
 /* ABI version of the loaded library (INB_ABI_VERSION). */
 int inb_abi_version(void);

@@ -6,6 +6,7 @@ The package directory is named ``isaac-net_b200``; it registers itself as ``isaa
 Public API (a drop-in for ``isaac_net.make_engine("L2", ...)`` on the uplink path):
     make_engine(level, E, R, device, config, backend="b200", *, seed=None) -> NRB200Engine
     NRConfig, TrafficModel, Requests
+    NetModule, IsaacNetCfg, TrafficRequest  (the Isaac-side module on the engine's radio, net_module.py)
 """
 import importlib as _importlib
 import importlib.abc as _abc
@@ -44,4 +45,11 @@ def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, size
     return _make(level, E, R, device, config, backend, sizes=sizes, seed=seed, strict=strict)
 
 
-__all__ = ["make_engine", "NRConfig", "TrafficModel", "Requests"]
+def __getattr__(name):
+    """The Isaac-side module (net_module.py) on first use: NetModule, IsaacNetCfg, TrafficRequest."""
+    if name in ("NetModule", "IsaacNetCfg", "TrafficRequest"):
+        return getattr(_importlib.import_module(__name__ + ".net_module"), name)
+    raise AttributeError(name)
+
+
+__all__ = ["make_engine", "NRConfig", "TrafficModel", "Requests", "NetModule", "IsaacNetCfg", "TrafficRequest"]

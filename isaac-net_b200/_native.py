@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 8
+ABI_VERSION = 9
 MAX_ROWS = 64
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -119,8 +119,22 @@ class InbTrafficArgs(ctypes.Structure):
                 + [("calls", P), ("src", InbTrafficSource * MAX_SRC)] + [(n, P) for n in TRAFFIC_OUT])
 
 
+OBS_OFFS = ("off_mask", "off_delay", "off_aoi", "off_qlen", "off_qbytes", "off_sinr", "off_rsrp", "off_serv",
+            "off_last", "off_hist", "off_blocked", "off_los")   # in the order of isaac/config.py OBS_FEATURES
+OBS_IN = ("newest", "t", "queue_len", "serving", "queue_bytes", "sinr_db", "delay", "delivered", "blocked", "los",
+          "det_env", "cap", "cur_tag")
+OBS_OUT = ("last_cap", "hist", "last_cap_out", "aoi_s", "delay_s", "rsrp_dbm", "x", "delivered_any", "blocked_out",
+           "los_out", "tag_delivered")
+
+
+class InbObsArgs(ctypes.Structure):
+    _fields_ = ([(n, i32) for n in ("E", "R", "F", "G", "K", "dim")] + [(n, i32) for n in OBS_OFFS]
+                + [(n, f32) for n in ("step_dt", "inv_ts", "inv_F", "inv_qbytes", "inv_db", "noise_db")]
+                + [(n, P) for n in OBS_IN + OBS_OUT])
+
+
 EXPORTS = ("inb_nr_step", "inb_nr_step_noalloc", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step",
-           "inb_store2", "inb_abi_version")
+           "inb_store2", "inb_net_obs", "inb_abi_version")
 NOALLOC_GAIN_MAX = 1 << 25
 _lib = None
 
@@ -150,6 +164,8 @@ def lib():
     L.inb_store2.argtypes = [P, i64, i64, P]
     L.inb_traffic_step.restype = ctypes.c_int
     L.inb_traffic_step.argtypes = [ctypes.POINTER(InbTrafficArgs), P]
+    L.inb_net_obs.restype = ctypes.c_int
+    L.inb_net_obs.argtypes = [ctypes.POINTER(InbObsArgs), P]
     _lib = L
     return L
 
@@ -160,4 +176,4 @@ def check(rc, what):
 
 
 __all__ = ["lib", "check", "InbStepArgs", "InbResetArgs", "InbParams", "InbState", "InbOutputs", "InbArrivals",
-           "InbTables", "InbRadio", "InbTrafficArgs", "InbTrafficSource", "EXPORTS", "LIB_PATH"]
+           "InbTables", "InbRadio", "InbTrafficArgs", "InbTrafficSource", "InbObsArgs", "EXPORTS", "LIB_PATH"]

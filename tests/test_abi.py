@@ -32,7 +32,7 @@ def test_library_loads_and_exports_every_symbol():
 STRUCTS = {"InbState": nat.InbState, "InbOutputs": nat.InbOutputs, "InbArrivals": nat.InbArrivals,
            "InbTables": nat.InbTables, "InbParams": nat.InbParams, "InbStepArgs": nat.InbStepArgs,
            "InbResetArgs": nat.InbResetArgs, "InbTrafficSource": nat.InbTrafficSource,
-           "InbTrafficArgs": nat.InbTrafficArgs, "InbRadio": nat.InbRadio}
+           "InbTrafficArgs": nat.InbTrafficArgs, "InbRadio": nat.InbRadio, "InbObsArgs": nat.InbObsArgs}
 
 
 def _c_layout(tmp_path):
