@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 9
+#define INB_ABI_VERSION 10
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -51,6 +51,7 @@ extern "C" {
 enum {
   INB_CTR_TB_NEW = 0, INB_CTR_TB_RETX, INB_CTR_TB_OK, INB_CTR_TB_FAIL, INB_CTR_EXHAUST, INB_CTR_BYTES_OK,
   INB_CTR_BYTES_NEW, INB_CTR_NEW_WHILE_PENDING, INB_CTR_PRB_USED, INB_CTR_LOST_FRAMES,
+  INB_CTR_TB_BYTES = 10, INB_CTR_TB_EMPTY, INB_CTR_RETX_BLOCK,   /* with InbParams.lena_ctr (mac.py:492-493, 299) */
   INB_CTR_NTX_HIST = 16, INB_CTR_RV_TX = 32, INB_CTR_RV_FAIL = 48
 };
 
@@ -72,6 +73,7 @@ typedef struct {
   int64_t *serv, *a3_cand, *a3_cnt, *ho_end, *n_ho;        /* [E,R] */
   uint8_t *pending;                                        /* [E] */
   float *ni_ul;                                            /* [E,C,S] */
+  float *last_nprb;             /* [E,R] PRBs of the robot's last PUSCH (ul_amc_alloc = "previous"; NULL otherwise) */
 } InbState;
 
 /* Step outputs (the step dict of NREngine.step), [E,R,F] unless noted. */
@@ -153,6 +155,12 @@ typedef struct {
   int32_t field_fma;            /* plane-wave phase k . x as fma(y, k_y, x k_x) (1) or x k_x + y k_y rounded twice (0):
                                    the rounding of the reference's CPU einsum, which takes its BLAS path (fused) when
                                    2 R C K >= 400 (C fields of K waves) and its plain loop (two roundings) below */
+  int32_t tdma;                 /* ul_retx_sched = "tdma": one retransmission per slot and cell, the oldest NACK first
+                                   (lowest robot on ties), and no new data in a cell that has one (mac.py:279-299) */
+  int32_t amc_prev;             /* ul_amc_alloc = "previous": the new TB's MCS is chosen for the PRB count of the
+                                   robot's last PUSCH (s.last_nprb, this grant's when 0), its TBS for this grant
+                                   (mac.py:393-400, 484) */
+  int32_t lena_ctr;             /* 5G-LENA MAC switches on: also count tb_bytes, tb_empty, retx_block (mac.py:119-121) */
 } InbParams;
 
 /* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes

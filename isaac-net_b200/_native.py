@@ -12,13 +12,14 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 9
+ABI_VERSION = 10
 MAX_ROWS = 64
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
 CDF_STRIDE = 64        # INB_CDF_STRIDE
 CTR_NAMES = ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "new_while_pending",
              "prb_used", "lost_frames")
+LENA_CTR_NAMES = ("tb_bytes", "tb_empty", "retx_block")   # words 10-12 with InbParams.lena_ctr
 CTR_NTX_HIST, CTR_RV_TX, CTR_RV_FAIL = 16, 32, 48
 
 P = ctypes.c_void_p
@@ -27,7 +28,7 @@ i32, i64, u32, f32, f64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctype
 STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg", "csi", "h", "spec", "k_lin",
                 "h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb", "cap", "start",
                 "end_", "cls", "hid", "tag", "prio", "lost", "det", "fin", "off", "dline", "serv", "a3_cand", "a3_cnt",
-                "ho_end", "n_ho", "pending", "ni_ul")
+                "ho_end", "n_ho", "pending", "ni_ul", "last_nprb")
 OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
               "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
               "sinr_db", "pathgain", "det_env", "serving_cell", "blocked", "los")
@@ -72,7 +73,8 @@ class InbParams(ctypes.Structure):
                 + [(n, i32) for n in ("C", "ttt", "ho_int", "has_floor", "ho_flush", "pc_on")]
                 + [(n, f32) for n in ("a3_off", "a3_hyst", "floor_rx", "noise_mw", "ue_tx_ref", "ref_db", "pc_p0",
                                       "pc_alpha", "li_alpha", "li_beta")]
-                + [("los_const", i32), ("pf_rbg", i32), ("pf_freeze", i32), ("field_fma", i32)])
+                + [("los_const", i32), ("pf_rbg", i32), ("pf_freeze", i32), ("field_fma", i32), ("tdma", i32),
+                   ("amc_prev", i32), ("lena_ctr", i32)])
 
 
 class InbRadio(ctypes.Structure):

@@ -313,6 +313,12 @@ class NRConfig:
         """Period (in slots) after which the schedule of a control step repeats."""
         return math.lcm(len(self.tdd_pattern), self.sr_period_slots, self.cqi_period_slots)
 
+    def lena_mac_switches(self):
+        """The 5G-LENA MAC switches set away from their defaults, {field: value} (config.py:1092-1094)."""
+        d = {"pf_update": "slot", "pf_avg_idle": "decay", "ul_retx_sched": "ofdma", "ul_amc_alloc": "current",
+             "ul_grant_model": "lumped"}
+        return {k: getattr(self, k) for k, v in d.items() if getattr(self, k) != v}
+
     def field_dict(self):
         """{field: value} of every field (the plain form the reference's NRConfig(**...) takes, traffic aside)."""
         return {f.name: getattr(self, f.name) for f in fields(self)}
@@ -327,8 +333,6 @@ class NRConfig:
                ("ul_grant_model", "the SR/BSR grant pipeline is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),
                ("ul_tpc", "closed-loop power control is not built"),
-               ("ul_retx_sched", "TDMA retransmissions are not built"),
-               ("ul_amc_alloc", "previous-allocation AMC is not built"),
                ("eff_sinr", "only EESM is built"),
                ("bler_source", "only the shipped Sionna PDSCH tables are built"),
                ("tbs_mode", "only the exact 38.214 TBS is built"),
@@ -349,6 +353,9 @@ class NRConfig:
         for name, why in chk:
             if getattr(self, name) != getattr(d, name):
                 out.append((f"{name}={getattr(self, name)!r}", why))
+        if self.ul_retx_sched not in ("ofdma", "tdma") or self.ul_amc_alloc not in ("current", "previous"):
+            out.append((f"ul_retx_sched={self.ul_retx_sched!r} / ul_amc_alloc={self.ul_amc_alloc!r}",
+                        "unknown 5G-LENA MAC option"))
         if self.pf_update not in ("slot", "rbg") or self.pf_avg_idle not in ("decay", "freeze"):
             out.append((f"pf_update={self.pf_update!r} / pf_avg_idle={self.pf_avg_idle!r}", "unknown PF option"))
         if self.pf_update == "rbg" and self.scheduler != "pf":

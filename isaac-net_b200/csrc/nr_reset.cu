@@ -28,6 +28,7 @@ __global__ void nr_reset_kernel(const InbResetArgs A) {
   const uint32_t kenv = key_env(A.s0, A.env_id[e], ep, CH_RESET, 0);
   st.sent[er] = 0; st.floor_[er] = 0; st.bsr[er] = 0; st.sr_t[er] = -1; st.last_tx[er] = -1; st.enq[er] = 0;
   st.olla[er] = 0.0f; st.avg[er] = 100.0f;
+  if (st.last_nprb != nullptr) st.last_nprb[er] = 0.0f;
   const uint32_t base_h = key_stream(kenv, (uint32_t)(SITE_H0 << 16));
   const int C = A.C > 1 ? A.C : 1;
   for (int s = 0; s < S; ++s) st.csi[er * S + s] = 0.0f;

@@ -467,6 +467,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     sent = st.sent[CK(er, NER, 1)]; floor_ = st.floor_[CK(er, NER, 1)]; bsr = st.bsr[CK(er, NER, 1)]; sr_t = st.sr_t[CK(er, NER, 1)]; last_tx = st.last_tx[CK(er, NER, 1)];
     enq = st.enq[CK(er, NER, 1)]; olla = st.olla[CK(er, NER, 1)]; avg = st.avg[CK(er, NER, 1)];
   }
+  float last_nprb = 0.0f;   // PRBs of the last PUSCH (ul_amc_alloc = "previous")
+  if (act && p.amc_prev) last_nprb = st.last_nprb[CK(er, NER, 1)];
   // HARQ process states as bit masks (state 1: holds a TB awaiting its retransmission or ACK; state 0: free)
   uint32_t pend = 0u, freem = 0u;
   if (act) {
@@ -816,8 +818,22 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const float pf_base = fm(p.pf_a, avg);
     float got = 0.0f;
 #define AMET(s) (PFR ? x_fdv(RATE(s), fmaxf(fa(pf_base, fm(p.pf_b, got)), 1e-9f)) : METRIC(s))
-    // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit (mac.py:300-312)
-    if (Grp<GW>::any_uniform(has_rx, sm, par)) {
+    if (p.tdma) {
+      // 5G-LENA UL HARQ (ul_retx_sched = "tdma", mac.py:279-299): one retransmission per slot and cell, the oldest
+      // NACK (earliest ready slot of its process; lowest robot on ties, torch.argmin) first, and no new data in a
+      // cell that has one.  Key: 1 + the slots since it became ready, so the arg-max is the arg-min of ready.
+      const long long age = g - best_ready;
+      const uint32_t key = has_rx ? (uint32_t)(age < 0xFFFFFFFELL ? age : 0xFFFFFFFELL) + 1u : 0u;
+      uint32_t mx = 0u;
+      bool anyrx = false;
+      const int wl = Grp<GW>::template argmax_cell<NC>(key, has_rx, serv, C, mx, anyrx, sm, par);
+      const bool adm = has_rx && wl == r;
+      if (anyrx) new_el = false;
+      if (adm && p.lena_ctr && rx_nsb < S) atomicAdd(sc + INB_CTR_RETX_BLOCK, 1ull);
+      has_rx = adm;
+    } else if (Grp<GW>::any_uniform(has_rx, sm, par)) {
+      // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit
+      // (mac.py:300-312)
       float rkey = -1.0f;
       if (has_rx) {
         float sum = 0.0f;
@@ -1082,7 +1098,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
               const float est_tx = fa(fs(REF(s_), split), CSI_A(csi_src, er, serv, s_));
               v_x[s_ * NP] = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
             }
-            const long long trow = (long long)(int)n_prb * p.MCS;
+            // the TBS row of this grant, and the row the MCS is chosen on (the last PUSCH's PRBs under
+            // ul_amc_alloc = "previous", mac.py:393-400)
+            const long long trow_g = (long long)(int)n_prb * p.MCS;
+            const long long trow = (p.amc_prev && last_nprb > 0.0f) ? (long long)(int)last_nprb * p.MCS : trow_g;
             int mtop = -1, n_cand = 0;
             for (int m = min(p.mcs_max, p.MCS - 1); m >= 0; --m) {
               if (A.t.la_tbs[CK(trow + m, NLA, 9)] > 0) {
@@ -1117,7 +1136,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             }
             if (chosen >= 0 || n_cand <= 1) {
               mcs_new = chosen < 0 ? 0 : chosen;
-              tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
+              tbs_new = A.t.la_tbs[CK(trow_g + mcs_new, NLA, 9)];
             } else {
               more = true;
             }
@@ -1152,6 +1171,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
         const float off_a = __shfl_sync(0xFFFFFFFFu, p.olla_on ? olla : 0.0f, a);
         const float nprb_a = __shfl_sync(0xFFFFFFFFu, n_prb, a);
+        const float lnp_a = __shfl_sync(0xFFFFFFFFu, last_nprb, a);
         const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
         const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
         float ng = 0.0f;   // -10^(clamp(est, -30, 60) / 10) of this lane's RBG
@@ -1162,7 +1182,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float est_tx = fa(fs(refs, split_a), csi_s);
           ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
-        const long long trow = (long long)(int)nprb_a * p.MCS;
+        const long long trow_g = (long long)(int)nprb_a * p.MCS;   // this grant's TBS row
+        const long long trow = (p.amc_prev && lnp_a > 0.0f) ? (long long)(int)lnp_a * p.MCS : trow_g;   // MCS row
         // candidates: MCS <= mcs_max with a TBS; the highest first (one lane per RBG), which is the usual outcome;
         // if it fails, every other candidate at once (one lane per MCS) and the highest that passes
         const uint32_t cand = __ballot_sync(0xFFFFFFFFu, lane <= p.mcs_max && lane < p.MCS &&
@@ -1219,7 +1240,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         }
         if (lane == a) {
           mcs_new = chosen < 0 ? 0 : chosen;
-          tbs_new = A.t.la_tbs[CK(trow + mcs_new, NLA, 9)];
+          tbs_new = A.t.la_tbs[CK(trow_g + mcs_new, NLA, 9)];
         }
       }
     }
@@ -1400,7 +1421,12 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (!p.pf_freeze || (need > 0 && !has_rx)) avg = na;
     }
     if (p.sched == 2 && tx) last_tx = g;
+    if (p.amc_prev && tx) last_nprb = n_prb;   // mac.py:484
     if (tx) {   // counters (only transmitting robots have any to add)
+      if (tx_new && p.lena_ctr) {   // grant accounting of the 5G-LENA switches (mac.py:492-493)
+        atomicAdd(sc + INB_CTR_TB_BYTES, (unsigned long long)(tbs_new / 8));
+        if (byt_new == 0) atomicAdd(sc + INB_CTR_TB_EMPTY, 1ull);
+      }
       if (tx_new) {
         atomicAdd(sc + INB_CTR_TB_NEW, 1ull);
         atomicAdd(sc + INB_CTR_BYTES_NEW, (unsigned long long)byt_new);
@@ -1480,6 +1506,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
+    if (p.amc_prev) st.last_nprb[CK(er, NER, 1)] = last_nprb;
   }
 #undef REF
   if constexpr (MC) {   // the env's N+I back to memory; the initial association is done

@@ -202,6 +202,8 @@ class NRB200Engine:
         st["fin"] = full((E, R, F), torch.float64, math.inf)
         st["off"] = full((E, R, F), torch.float64, 0.0)
         st["dline"] = full((E, R, F), torch.float64, math.inf)
+        if self.config.ul_amc_alloc == "previous":   # AMC_STATE (mac_ul.py:51)
+            st["last_nprb"] = full((E, R), f32, 0.0)
         self.st = st
 
     def _state_struct(self):
@@ -238,6 +240,8 @@ class NRB200Engine:
         p.pf_a = _f32(1 - 1 / cfg.pf_window)
         p.pf_b = _f32(1 / cfg.pf_window)
         p.pf_rbg, p.pf_freeze = int(cfg.pf_update == "rbg"), int(cfg.pf_avg_idle == "freeze")
+        p.tdma, p.amc_prev = int(cfg.ul_retx_sched == "tdma"), int(cfg.ul_amc_alloc == "previous")
+        p.lena_ctr = int(bool(cfg.lena_mac_switches()))
         p.target = _f32(cfg.bler_target)
         p.inv_S = _f32(1.0 / self.S)
         p.s0_snr, p.c0_cbs = _f32(tab.s0), _f32(tab.c0)
@@ -961,6 +965,9 @@ class NRB200Engine:
         """counters() from a summed counter vector c [INB_NCTR] and the PRBs offered (also for sums over shards)."""
         c = c.cpu()
         res = {k: float(c[i]) for i, k in enumerate(nat.CTR_NAMES)}
+        if self.config.lena_mac_switches():      # grant accounting of the 5G-LENA switches (mac.py:119-121)
+            for i, k in enumerate(nat.LENA_CTR_NAMES):
+                res[k] = float(c[len(nat.CTR_NAMES) + i])
         res["prb_avail"] = float(prb_avail)
         H = self.config.max_harq_tx + 1
         res["ntx_hist"] = [float(v) for v in c[nat.CTR_NTX_HIST:nat.CTR_NTX_HIST + H]]
@@ -1113,7 +1120,7 @@ class NRB200Engine:
             "q.cls": "cls", "q.det": "det", "q.hid": "hid", "q.off": "off", "q.tag": "tag", "q.prio": "prio",
             "q.dline": "dline", "net.h": "h", "net.spec": "spec", "net.k_lin": "k_lin", "assoc.serv": "serv",
             "assoc.a3_cand": "a3_cand", "assoc.a3_cnt": "a3_cnt", "assoc.ho_end": "ho_end", "assoc.n_ho": "n_ho",
-            "assoc.pending": "pending", "net.ni_ul": "ni_ul"}
+            "assoc.pending": "pending", "net.ni_ul": "ni_ul", "ul.last_nprb": "last_nprb"}
 
     # the radio field the kernel evaluates, under the reference's names (RadioMC.k / phi for log_distance,
     # TR38901Channel.sf_los for tr38901 with the forced LOS state)

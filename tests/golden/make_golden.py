@@ -58,6 +58,15 @@ CASES = {
     "2r": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", retx_priority=False,
                                            ue_tx_dbm=-6.0)),
     "3r": (3, 2, 64, 16, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze")),
+    # the validated 5G-LENA MAC of ul_v2l (lena_validation_v2 without the BSR pipeline): TDMA retransmissions (one per
+    # slot and cell, oldest first, no new data beside it) and the MCS chosen for the previous PUSCH's PRB count, on
+    # weak links so that retransmissions compete; with PF on one and three cells, and with round robin
+    "2v": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
+                                           ul_amc_alloc="previous", ue_tx_dbm=-6.0)),
+    "3v": (3, 2, 64, 16, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
+                                           ul_amc_alloc="previous", ue_tx_dbm=-4.0)),
+    "1v": (1, 4, 16, 24, {10: [2]}, 2, dict(ul_retx_sched="tdma", ul_amc_alloc="previous", ue_tx_dbm=-12.0,
+                                            max_harq_tx=3)),
 }
 
 
@@ -91,6 +100,8 @@ def ref_state(eng):
     for n in ("off", "tag", "prio", "dline"):
         if hasattr(q, n):
             st["q." + n] = getattr(q, n)
+    if hasattr(ul, "last_nprb"):
+        st["ul.last_nprb"] = ul.last_nprb
     st["net.h"] = net.h
     if net.rician:
         st["net.spec"] = net.spec
