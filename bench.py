@@ -219,27 +219,39 @@ def net_obs_bytes(F, K, dim, R):
     return 8 * 3 + 4 * 2 + 13 * F + 2 * (8 + 4 * K) + 8 + 4 + 4 * F + 4 + 4 * dim + 3 + 17.0 / R
 
 
-def net_obs_timing(o, cfg, E, R, dev, n=50):
-    """Average device time of the observation packing (inb_net_obs, every feature selected, history 4) over n
-    launches on the bench engine's step dict `o`, CUDA events around them on their stream."""
+def net_obs_timing(o, cfg, E, R, dev, n=20, reps=5):
+    """Average device time of the observation packing (inb_net_obs, every feature selected, history 4) on the bench
+    engine's step dict `o`: n launches captured in a CUDA graph (the python launch path costs more host time than
+    the kernel takes, so eager back-to-back launches would time the host), the graph replayed reps times between
+    CUDA events on the replay stream."""
     nm = importlib.import_module("isaac-net_b200.net_module")
     pk = nm.ObsPacker(nm.OBS_FEATURES, E, R, cfg.frame_buffer, cfg.n_cells, 4, cfg.control_step_ms / 1000.0,
                       cfg.subband_noise_dbm, 50 * cfg.control_step_ms / 1000.0,
                       cfg.frame_buffer * max(cfg.msg_sizes), dev)
     cur = torch.zeros(E, dtype=torch.long, device=dev)
-    for _ in range(3):
-        pk.step(o, cur)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            pk.step(o, cur)
     torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(n):
+            pk.step(o, cur)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(n):
-        pk.step(o, cur)
+    for _ in range(reps):
+        g.replay()
     b.record()
     torch.cuda.synchronize()
-    us = a.elapsed_time(b) / n * 1e3
+    us = a.elapsed_time(b) / (n * reps) * 1e3
+    del g
     per = net_obs_bytes(cfg.frame_buffer, 4, pk.dim, R)
     return {"kernel_us": us, "bytes_per_launch": per * E * R, "features": "all 12, history 4",
-            "launches_per_step": 1}
+            "launches_per_step": 1, "timing": f"CUDA graph of {n} launches, replayed {reps} times"}
 
 
 def main():

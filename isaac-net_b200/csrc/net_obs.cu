@@ -49,57 +49,73 @@ __global__ void __launch_bounds__(OBS_THREADS) net_obs_kernel(const InbObsArgs A
   constexpr int RPW = 32 / FW;                      // robots per warp and pass
   const unsigned seg = FW >= 32 ? 0xFFFFFFFFu : (((1u << FW) - 1u) << (lane / FW * FW));
   const int l = lane % FW;
-  // ---- (1) frame stage
-  for (int base = warp * RPW; base < nrb; base += (OBS_THREADS / 32) * RPW) {   // warp-uniform trip count
-    const int rl = base + lane / FW;
-    const bool live = rl < nrb;
-    const long long fb = (rb0 + (live ? rl : 0)) * F;
-    long long best = LLONG_MIN;
-    int best_f = 0x7FFFFFFF;
-    bool any = false;
-    float dd[2] = {0.0f, 0.0f};
-    bool dl[2] = {false, false};
+  // ---- (1) frame stage: each warp takes NPASS groups of RPW robots at a time, all their loads issued before the
+  // first reduction (the loads of a group are independent of the others': latency overlaps instead of adding up)
+  constexpr int NPASS = 4, STRIDE = (OBS_THREADS / 32) * RPW;
+  for (int base = warp * RPW; base < nrb; base += STRIDE * NPASS) {   // warp-uniform trip count
+    bool dl[NPASS][2];
+    float dd[NPASS][2];
+    long long ck[NPASS][2];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int f = l + j * FW;
-      if (!live || f >= F) continue;
-      const bool d = A.delivered[fb + f] != 0;
-      const float ds = obs_fm(A.delay[fb + f], A.step_dt);
-      if (A.delay_s) A.delay_s[fb + f] = ds;
-      dd[j] = obs_nan0(ds);
-      dl[j] = d;
-      any = any || d;
-      const long long key = d ? A.cap[fb + f] : -(1LL << 62);
-      if (key > best || (key == best && f < best_f)) {
-        best = key;
-        best_f = f;
+    for (int q = 0; q < NPASS; ++q) {
+      const int rl = base + q * STRIDE + lane / FW;
+      const long long fb = (rb0 + (rl < nrb ? rl : 0)) * F;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int f = l + j * FW;
+        const bool in = rl < nrb && f < F;
+        dl[q][j] = in && A.delivered[fb + f] != 0;
+        dd[q][j] = in ? obs_fm(A.delay[fb + f], A.step_dt) : 0.0f;
+        ck[q][j] = in ? A.cap[fb + f] : 0;
       }
     }
 #pragma unroll
-    for (int o = FW / 2; o > 0; o >>= 1) {   // segmented arg-max: largest key, lowest slot on ties
-      const long long ob = __shfl_xor_sync(0xFFFFFFFFu, best, o, FW);
-      const int of = __shfl_xor_sync(0xFFFFFFFFu, best_f, o, FW);
-      if (ob > best || (ob == best && of < best_f)) {
-        best = ob;
-        best_f = of;
-      }
-    }
-    any = (__ballot_sync(0xFFFFFFFFu, any) & seg) != 0u;
-    const int owner = best_f % FW, jw = best_f / FW;   // the delay of the winning slot, from its lane
-    const float mine = jw == 0 ? dd[0] : dd[1];
-    const float dwin = __shfl_sync(0xFFFFFFFFu, mine, owner, FW);
-    if (!live) continue;
-    if (l == 0) {
-      s_dwin[rl] = dwin;
-      s_any[rl] = any ? 1 : 0;
-    }
-    float* const row = tile + (size_t)rl * dim;
+    for (int q = 0; q < NPASS; ++q) {
+      const int rl = base + q * STRIDE + lane / FW;
+      const bool live = rl < nrb;
+      const long long fb = (rb0 + (live ? rl : 0)) * F;
+      long long best = LLONG_MIN;
+      int best_f = 0x7FFFFFFF;
+      bool any = false;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int f = l + j * FW;
-      if (f >= F) continue;
-      if (A.off_mask >= 0) row[A.off_mask + f] = dl[j] ? 1.0f : 0.0f;
-      if (A.off_delay >= 0) row[A.off_delay + f] = dl[j] ? obs_clamp01(obs_fm(dd[j], A.inv_ts)) : 0.0f;
+      for (int j = 0; j < 2; ++j) {
+        const int f = l + j * FW;
+        if (!live || f >= F) continue;
+        if (A.delay_s) A.delay_s[fb + f] = dd[q][j];
+        dd[q][j] = obs_nan0(dd[q][j]);
+        any = any || dl[q][j];
+        const long long key = dl[q][j] ? ck[q][j] : -(1LL << 62);
+        if (key > best || (key == best && f < best_f)) {
+          best = key;
+          best_f = f;
+        }
+      }
+#pragma unroll
+      for (int o = FW / 2; o > 0; o >>= 1) {   // segmented arg-max: largest key, lowest slot on ties
+        const long long ob = __shfl_xor_sync(0xFFFFFFFFu, best, o, FW);
+        const int of = __shfl_xor_sync(0xFFFFFFFFu, best_f, o, FW);
+        if (ob > best || (ob == best && of < best_f)) {
+          best = ob;
+          best_f = of;
+        }
+      }
+      any = (__ballot_sync(0xFFFFFFFFu, any) & seg) != 0u;
+      const int owner = best_f % FW, jw = best_f / FW;   // the delay of the winning slot, from its lane
+      const float mine = jw == 0 ? dd[q][0] : dd[q][1];
+      const float dwin = __shfl_sync(0xFFFFFFFFu, mine, owner, FW);
+      if (!live) continue;
+      if (l == 0) {
+        s_dwin[rl] = dwin;
+        s_any[rl] = any ? 1 : 0;
+      }
+      float* const row = tile + (size_t)rl * dim;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int f = l + j * FW;
+        if (f >= F) continue;
+        if (A.off_mask >= 0) row[A.off_mask + f] = dl[q][j] ? 1.0f : 0.0f;
+        if (A.off_delay >= 0) row[A.off_delay + f] = dl[q][j] ? obs_clamp01(obs_fm(dd[q][j], A.inv_ts)) : 0.0f;
+      }
     }
   }
   __syncthreads();
