@@ -195,6 +195,18 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
+    if a.workload == "ul":
+        ib = importlib.import_module("isaac-net_b200")
+        cfg = ib.NRConfig(msg_sizes=(4000.0, 30000.0))
+        res = ul_cpu_baseline(cfg, 4, UL_R, 1)
+        v = res["value"]
+        print(json.dumps({"metric": "env-steps/sec", "value": v, "unit": "env-steps/s", "n_gpus": a.gpus, "steps": 1,
+                          "warmup": 1, "ms_per_step": 4 / v * 1e3, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+                          "config": {"workload": "ul_4096x100_nrconfig_default"}, "cpu_baseline": res,
+                          "e2e": {"value": v, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
+                                  "d2h_bytes_per_step": 0}}))
+        return
     presets = importlib.import_module("isaac-net_b200.presets")
     wl = presets.workload(a.workload)
     cfg = wl.config()
@@ -254,13 +266,145 @@ def net_obs_timing(o, cfg, E, R, dev, n=20, reps=5):
             "launches_per_step": 1, "timing": f"CUDA graph of {n} launches, replayed {reps} times"}
 
 
+# The reference's own published NR benchmark (benchmarks/uncontended/bench_net.py --case L2 --cfg ul --E 4096 --R 100;
+# docs/performance.md:201): NRConfig() defaults with messages of 4 kB / 30 kB, seed 1, every control step
+# submit(send, det, hid) + step(None, snr[E,R]); 67.8 ms per step with its triton backend on an RTX 4090.
+UL_PUBLISHED_MS = 67.8
+UL_E, UL_R = 4096, 100
+
+
+class UlInputs:
+    """Pool of 16 input sets on the device, drawn as the reference's benchmark draws them (bench_net.py:152-171):
+    every robot sends w.p. 0.3 (a third of those the 30 kB class), detection flags w.p. 0.1, an SNR [E,R] drifting
+    around a U(0, 25) dB draw (+ N(0, 0.5^2) per step, clamped to [-5, 30])."""
+
+    def __init__(self, E, R, dev, seed=0):
+        g = torch.Generator(device=dev).manual_seed(seed)
+        self.sends, self.dets, self.snrs = [], [], []
+        snr = 25 * torch.rand(E, R, device=dev, generator=g)
+        for _ in range(16):
+            u = torch.rand(E, R, device=dev, generator=g)
+            self.sends.append((u < 0.3).long() * (1 + (u < 0.1).long()))
+            self.dets.append(torch.rand(E, R, device=dev, generator=g) < 0.1)
+            snr = (snr + 0.5 * torch.randn(E, R, device=dev, generator=g)).clamp(-5, 30)
+            self.snrs.append(snr.clone())
+        self.hid = torch.zeros(E, dtype=torch.long, device=dev)
+
+
+def ul_cpu_baseline(cfg, E, R, steps):
+    """The oracle port (torch on the host cores, the reference's op sequence) on E envs of the ul workload."""
+    from oracle.nr_oracle import OracleEngine
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    o = OracleEngine(cfg, E, R, "cpu", seed=1, reduce="aten")
+    inp = UlInputs(E, R, "cpu")
+    for k in range(1 + steps):
+        if k == 1:
+            t0 = time.perf_counter()
+        o.submit(inp.sends[k % 16], inp.dets[k % 16], inp.hid)
+        o.step(snr=inp.snrs[k % 16])
+    dt = time.perf_counter() - t0
+    return {"value": E * steps / dt, "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "sample": f"oracle port (torch CPU, reference op order) on {E} of {UL_E} envs x {R} robots, {steps} "
+                      f"control steps after 1 warm-up"}
+
+
+def run_ul(a, rank, world, dist, dev):
+    """--workload ul: the reference's published network-only NR case (see UL_PUBLISHED_MS), E = 4096 envs x 100
+    robots per GPU, through the public API (submit + step with an SNR input, the eager launch path of that input)."""
+    ib = importlib.import_module("isaac-net_b200")
+    cfg = ib.NRConfig(msg_sizes=(4000.0, 30000.0))
+    E, R = UL_E, UL_R
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=1)
+    eng.set_env_offset(rank * E)
+    inp = UlInputs(E, R, dev, seed=rank)
+    Rq = ib.Requests
+
+    def one(k, fetch=None):
+        eng.submit(None, Rq(inp.sends[k % 16], inp.dets[k % 16], inp.hid))
+        return eng.step(None, inp.snrs[k % 16])
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for k in range(a.warmup):
+        one(k)
+    clocks = Clocks(dev.index)
+    barrier()
+    clocks.start()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for k in range(a.steps):
+        one(a.warmup + k)
+    e1.record()
+    barrier()
+    clk = clocks.stop()
+    t_ms = e0.elapsed_time(e1)
+    # e2e: sends and SNR from pinned host memory every step, the newest / queue_len outputs back to pinned memory
+    hs = [x.cpu().pin_memory() for x in inp.sends]
+    hr = [x.cpu().pin_memory() for x in inp.snrs]
+    ho = {k: torch.empty(E, R, dtype=torch.long).pin_memory() for k in ("newest", "queue_len")}
+    barrier()
+    e0.record()
+    for k in range(a.steps):
+        send = hs[k % 16].to(dev, non_blocking=True)
+        snr = hr[k % 16].to(dev, non_blocking=True)
+        eng.submit(None, Rq(send, inp.dets[k % 16], inp.hid))
+        out = eng.step(None, snr)
+        for n, buf in ho.items():
+            buf.copy_(out[n], non_blocking=True)
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+    kev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(10)]
+    for i in range(10):
+        eng._kernel_events = kev[i]
+        one(i)
+    eng._kernel_events = None
+    barrier()
+    k_ms = sum(x.elapsed_time(y) for x, y in kev) / 10
+    t_ms, e2e_ms, k_ms = max_over_ranks([t_ms, e2e_ms, k_ms], dist, dev)
+    value = E * world * a.steps / (t_ms / 1e3)
+    peak, peak_kind = peaks()
+    per_launch = b_env(cfg, R) * E
+    achieved = per_launch / (k_ms / 1e3) / 1e9
+    published = UL_E / (UL_PUBLISHED_MS / 1e3)
+    line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": value / world / published, "dtype": "f32",
+            "data": "synthetic (the reference benchmark's send / SNR distributions, seeded)",
+            "config": {"workload": "ul_4096x100_nrconfig_default", "envs_per_gpu": E, "robots": R,
+                       "slots_per_step": cfg.slots_per_step, "rbgs": cfg.n_subbands, "harq": cfg.n_harq,
+                       "frames": cfg.frame_buffer, "parallelism": f"env shards x{world}",
+                       "l2": "state > L2 (no flush needed)"},
+            "baseline": {"ms_per_step": UL_PUBLISHED_MS, "value_per_gpu": published,
+                         "source": "isaac-net triton backend on an RTX 4090, docs/performance.md:201"},
+            "e2e": {"value": E * world * a.steps / (e2e_ms / 1e3), "unit": "env-steps/s",
+                    "h2d_bytes_per_step": E * R * (8 + 4), "d2h_bytes_per_step": E * R * 16},
+            "gpu_launches": a.steps * 3,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "traffic": None, "peak_kind": peak_kind, "kernel": "fading + MAC + finish kernels of one step",
+                         "kernel_ms": k_ms, "algorithmic_bytes_per_launch": per_launch},
+            "clocks": clk}
+    if rank == 0 and world == 1 and not a.no_cpu:
+        line["cpu_baseline"] = ul_cpu_baseline(cfg, 4, R, 1)
+    if rank == 0:
+        print(json.dumps(line))
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
-    ap.add_argument("--workload", type=int, default=2)
+    ap.add_argument("--workload", default="2", help="BASELINE config 1-5, or 'ul': the reference's published NR "
+                                                     "benchmark case (NRConfig() defaults, 4096 x 100 per GPU)")
     ap.add_argument("--cpu-envs", type=int, default=256)
     ap.add_argument("--cpu-steps", type=int, default=5)
     ap.add_argument("--no-cpu", action="store_true")
@@ -268,11 +412,15 @@ def main():
                     help="weak: every GPU runs the workload's per-GPU envs (config 4: 8192 of its 65536); strong: "
                          "the workload's envs split evenly over the GPUs")
     a = ap.parse_args()
+    if a.workload != "ul":
+        a.workload = int(a.workload)
     if a.impl == "reference":
         return run_reference(a)
     a.warmup = max(3, a.warmup)
     rank, world, dist = dist_setup(a.gpus)
     dev = torch.device("cuda", torch.cuda.current_device())
+    if a.workload == "ul":
+        return run_ul(a, rank, world, dist, dev)
     ib = importlib.import_module("isaac-net_b200")
     presets = importlib.import_module("isaac-net_b200.presets")
     wl = presets.workload(a.workload)

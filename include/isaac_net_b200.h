@@ -34,14 +34,14 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 10
+#define INB_ABI_VERSION 11
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
 #define INB_MAX_F 64      /* frame slots per robot */
 #define INB_MAX_M 64      /* traffic arrivals per robot per step */
 #define INB_MAX_MCS 32
-#define INB_MAX_ROWS 64   /* scheduled slots per control step */
+#define INB_MAX_ROWS 128  /* scheduled slots per control step */
 #define INB_MAX_KF 32     /* plane waves per shadowing field */
 #define INB_BLK_REGIONS 4 /* blockage model A regions per env (TR 38.901 Sec. 7.6.4.1: K = 4) */
 #define INB_CDF_STRIDE 64 /* blockage CDF table: entries per coarse bucket of the two-level search */

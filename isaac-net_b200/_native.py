@@ -12,8 +12,8 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 10
-MAX_ROWS = 64
+ABI_VERSION = 11
+MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
 CDF_STRIDE = 64        # INB_CDF_STRIDE
