@@ -763,9 +763,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const float rr_metric = (float)(g - last_tx);
     {
       const uint32_t wm0 = __ballot_sync(0xFFFFFFFFu, has_rx || new_el);
-      if (MC && __popc(wm0) * 4 > S * 3) {
-        // most robots of the warp want RBGs (the loaded multi-cell configs): each lane evaluates its own robot, RBG
-        // by RBG (the same expressions); the single-cell kernel keeps one path, which its i-cache prefers
+      if (__popc(wm0) * 4 > S * 3) {
+        // most robots of the warp want RBGs (loaded cells: the multi-cell configs, a saturated uplink): each lane
+        // evaluates its own robot, RBG by RBG (the same expressions), instead of one robot at a time
         if (has_rx || new_el) {
           for (int s = 0; s < S; ++s) {
             float est;

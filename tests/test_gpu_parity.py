@@ -77,6 +77,12 @@ def test_kernel_equals_oracle_seq_bitwise(case):
     assert eng.counters()["ul"]["prb_avail"] == float(g.state(g.steps - 1)["ctr.prb_avail"])
 
 
+def _bursty(size, rate_hz):
+    """Always-on Poisson arrivals of one message size (TrafficModel.bursty with on_off = (1, 0))."""
+    tm = importlib.import_module("isaac-net_b200.traffic").TrafficModel
+    return tm.bursty(size, rate_hz=rate_hz, burst_size=1, on_off=(1.0, 0.0))
+
+
 VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round robin without retransmission priority
     # (the release of short retransmissions' RBGs), round robin on the PF configs, several cells
     "1_rr_norp": (1, 8, 16, dict(retx_priority=False, ue_tx_dbm=-12.0, max_harq_tx=2)),
@@ -87,6 +93,10 @@ VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round r
     # the PF switches of 5G-LENA (the per-RBG metric and update, frozen idle averages) on one and three cells
     "2_pf_rbg": (2, 16, 32, dict(pf_update="rbg", ue_tx_dbm=-8.0)),
     "3_pf_rbg_freeze": (3, 4, 64, dict(pf_update="rbg", pf_avg_idle="freeze", ue_tx_dbm=-6.0)),
+    # saturated single-cell uplinks (most robots of a warp want RBGs every slot: the lane-per-robot rate path) on
+    # groups of 16 and 128 lanes
+    "1_saturated": (1, 8, 16, dict(traffic=(_bursty(1500, 2000),), ue_tx_dbm=-6.0)),
+    "4_saturated": (4, 2, 128, dict(traffic=(_bursty(8192, 400),), msg_sizes=(8192.0,), ue_tx_dbm=-8.0)),
 }
 
 
