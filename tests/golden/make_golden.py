@@ -255,10 +255,12 @@ def run_policy_case(i, E, R, steps, resets, every, over, legacy_step):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF"),
+                    help="source tree of the reference (isaac-net); default $ISAAC_NET_REF, else it must be importable")
     ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES)))
     a = ap.parse_args()
-    sys.path.insert(0, a.ref)
+    if a.ref:
+        sys.path.insert(0, a.ref)
     sys.path.insert(0, ROOT)
     torch.set_num_threads(8)
     for c in a.cases.split(","):
