@@ -195,3 +195,22 @@ def test_netmodule_end_to_end(wl_i, E, R, feats):
             assert torch.equal(a, b), (s, k)
         assert torch.equal(net.obs(), x), s
         pos = mot.advance()
+
+
+def test_packer_arguments_on_cpu():
+    """The launch arguments ObsPacker builds (no launch): every selected feature's first column of x in the order
+    given, -1 for the others, and the float32 constants torch uses on a CUDA device (python scalars rounded to
+    float32, divisions as float32 reciprocals)."""
+    feats = ("sinr", "delay_history", "serving_cell", "msg_delay", "aoi")
+    pk = nm.ObsPacker(feats, 2, 3, 16, 3, 5, 0.005, -96.99, 0.25, 16 * 30000.0, "cpu")
+    a = pk.args
+    assert (a.E, a.R, a.F, a.G, a.K, a.dim) == (2, 3, 16, 3, 5, 1 + 5 + 3 + 16 + 1)
+    assert (a.off_sinr, a.off_hist, a.off_serv, a.off_delay, a.off_aoi) == (0, 1, 6, 9, 25)
+    for n in ("off_mask", "off_qlen", "off_qbytes", "off_rsrp", "off_last", "off_blocked", "off_los"):
+        assert getattr(a, n) == -1, n
+    f32 = lambda x: float(np.float32(x))
+    assert a.step_dt == f32(0.005) and a.noise_db == f32(-96.99)
+    assert a.inv_ts == float(np.float32(1) / np.float32(0.25)) and a.inv_db == float(np.float32(1) / np.float32(40))
+    assert a.inv_F == float(np.float32(1) / np.float32(16))
+    assert a.inv_qbytes == float(np.float32(1) / np.float32(16 * 30000.0))
+    assert pk.last_cap.shape == (2, 3) and pk.hist.shape == (2, 3, 5)
