@@ -86,6 +86,14 @@ class NRConfig:
     ul_retx_sched: str = "ofdma"
     ul_amc_alloc: str = "current"
     ul_grant_model: str = "lumped"
+    # ul_grant_model = "bsr": the 5G-LENA SR / BSR pipeline (isaac_net/core/config.py:588-594)
+    sr_boot_slots: int = 6
+    sr_boot_bytes: int = 17
+    bsr_delay_slots: int = 10
+    bsr_hdr_bytes: int = 8
+    bsr_est_hdr_bytes: int = 5
+    rlc_tail_bytes: int = 16
+    rlc_tail_timer_ms: float = 10.0
     # radio model inside the engine
     snr_ref_prbs: int = 10
     ul_power: str = "allocated"
@@ -313,6 +321,11 @@ class NRConfig:
         """Period (in slots) after which the schedule of a control step repeats."""
         return math.lcm(len(self.tdd_pattern), self.sr_period_slots, self.cqi_period_slots)
 
+    @property
+    def rlc_tail_timer_slots(self):
+        """ul_grant_model="bsr": the RLC buffer-status timer in slots, at least one (config.py:1088-1090)."""
+        return max(1, int(round(self.rlc_tail_timer_ms / self.slot_ms)))
+
     def lena_mac_switches(self):
         """The 5G-LENA MAC switches set away from their defaults, {field: value} (config.py:1092-1094)."""
         d = {"pf_update": "slot", "pf_avg_idle": "decay", "ul_retx_sched": "ofdma", "ul_amc_alloc": "current",
@@ -329,6 +342,13 @@ class NRConfig:
         out = []
         d = NRConfig()
         chk = [("dl", "the downlink MAC is not built (uplink control-step path only)"),
+               ("sr_boot_slots", "the SR/BSR grant pipeline is not built"),
+               ("sr_boot_bytes", "the SR/BSR grant pipeline is not built"),
+               ("bsr_delay_slots", "the SR/BSR grant pipeline is not built"),
+               ("bsr_hdr_bytes", "the SR/BSR grant pipeline is not built"),
+               ("bsr_est_hdr_bytes", "the SR/BSR grant pipeline is not built"),
+               ("rlc_tail_bytes", "the SR/BSR grant pipeline is not built"),
+               ("rlc_tail_timer_ms", "the SR/BSR grant pipeline is not built"),
                ("ul_mini_slot_symbols", "mini-slot occasions are not built"),
                ("ul_grant_model", "the SR/BSR grant pipeline is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),

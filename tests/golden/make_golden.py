@@ -67,6 +67,11 @@ CASES = {
                                            ul_amc_alloc="previous", ue_tx_dbm=-4.0)),
     "1v": (1, 4, 16, 24, {10: [2]}, 2, dict(ul_retx_sched="tdma", ul_amc_alloc="previous", ue_tx_dbm=-12.0,
                                             max_harq_tx=3)),
+    # the 5G-LENA SR / BSR grant pipeline (ul_grant_model="bsr"): bootstrap grants, quantized reports in flight, the
+    # RLC tail residue; on one cell, and on three cells with frequent handovers (the target learns the buffer)
+    "2g": (2, 3, 32, 24, {9: [1]}, 2, dict(ul_grant_model="bsr", ue_tx_dbm=-6.0)),
+    "3g": (3, 2, 64, 16, {9: [1]}, 1, dict(ul_grant_model="bsr", a3_ttt_ms=2.0, a3_hyst_db=0.5,
+                                           ho_interruption_ms=1.5), 2000.0),
 }
 
 
@@ -102,6 +107,9 @@ def ref_state(eng):
             st["q." + n] = getattr(q, n)
     if hasattr(ul, "last_nprb"):
         st["ul.last_nprb"] = ul.last_nprb
+    if hasattr(ul, "rep_v"):                # BSR_STATE (mac_ul.py:45-50)
+        for n in ("est", "boot", "rep_v", "rep_g", "hid", "hid_until", "enq_seen", "armed"):
+            st["ul." + n] = getattr(ul, n)
     st["net.h"] = net.h
     if net.rician:
         st["net.spec"] = net.spec

@@ -7,6 +7,7 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t", "5", "5s", "1b", "2r", "3r", "2v", "3v", "1v")
+ORACLE_ONLY_CASES = ("2g", "3g")   # the SR / BSR grant pipeline: the oracle is pinned, the kernel refuses it
 POLICY_CASES = ("1p",)   # policy submits + SNR input (tests/golden/make_golden.py POLICY_CASES)
 
 

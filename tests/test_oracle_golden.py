@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import CASES, POLICY_CASES, Golden
+from golden_io import CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -40,7 +40,7 @@ def _state_diff(o, ref):
     return bad
 
 
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES)
 def test_oracle_aten_bitwise_free_running(case):
     g = Golden(case)
     wl = g.workload()
