@@ -21,9 +21,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF"),
+                    help="source tree of the reference (isaac-net); default $ISAAC_NET_REF, else it must be importable")
     a = ap.parse_args()
-    sys.path.insert(0, a.ref)
+    if a.ref:
+        sys.path.insert(0, a.ref)
     from isaac_net.core.phy import PHY
     out = {}
     for t in (1, 2):
