@@ -93,7 +93,7 @@ def _seq_flips(case, ties):
     return flips, robot_steps
 
 
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES)
 def test_oracle_seq_teacher_forced(case):
     """The kernels' summation order (seq) against the reference, with the reference's own tie order in the
     retransmission ranking: at most 1 in 1000 robot-steps may differ (ulp-level threshold moves)."""
@@ -177,3 +177,14 @@ def test_oracle_aten_bitwise_policy_case(case):
         if g.has_state(s):
             bad = _state_diff(o, g.state(s))
             assert not bad, f"step {s} state {bad}"
+
+
+def test_bsr_fixtures_have_activity():
+    """The SR / BSR pipeline fixtures exercise padded grants (tb_empty), the RLC tail residue and, on three cells,
+    handovers."""
+    for case in ORACLE_ONLY_CASES:
+        g = Golden(case)
+        last = g.state(g.steps - 1)
+        assert last["ctr.tb_empty"] > 0 and last["ctr.tb_new"] > 100, case
+        assert any(int(g.state(s)["ul.hid"].sum()) > 0 for s in range(g.steps) if g.has_state(s)), case
+    assert int(Golden("3g").state(Golden("3g").steps - 1)["assoc.n_ho"].sum()) > 50
