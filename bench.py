@@ -1,18 +1,18 @@
 """Benchmark of the B200 NR uplink engine: env-steps/s (envs x control steps per second).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 2]
-                    [--scaling weak|strong]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference] [--workload 4]
+                    [--scaling strong|weak]
     python -m torch.distributed.run --nnodes=1 --nproc-per-node N --master-addr 127.0.0.1 --master-port P \
         bench.py --gpus N ...
 
 One step = one control step of the engine over its whole batch, through the public API (engine.step), replayed as a
 CUDA graph of 5 launches: the control words (inb_store2), traffic arrivals (traffic.cu), AR(1) fading (nr_fading.cu),
 the MAC kernel (enqueue and arrival gate, radio, the K = 10 slots; nr_step.cuh) and the frame-parallel finish
-(nr_finish.cu), which writes the step dict into a fresh output block.  The default
-workload is BASELINE config 2 (4096 envs x 32 robots, 100 MHz / 18 RBGs, PF, Rician K = 5 dB, mixed periodic +
-Poisson traffic) per GPU; with N GPUs every rank runs its own 4096-env shard (global env ids rank * 4096 + i, no
-collective inside the step), so per-GPU work is fixed ("scaling": "weak").  --scaling strong splits the workload's
-envs evenly over the GPUs instead (config 4: 65536 envs in all, 8192 per GPU in its weak runs).
+(nr_finish.cu), which writes the step dict into a fresh output block.  The default workload is BASELINE config 4, the
+largest (65536 envs x 128 robots, 100 MHz / 18 RBGs, 16 HARQ processes, PF, mixed periodic + Poisson traffic), split
+evenly over the N GPUs ("scaling": "strong": 65536 envs on one GPU, 8192 per GPU at N = 8); every rank steps its own
+contiguous env shard (global env ids rank * E + i, no collective inside the step).  --scaling weak runs the
+workload's per-GPU batch on every rank instead (config 4: 8192 envs per GPU); --workload 1-5 picks another config.
 
   value   env-steps/s with the poses already resident in HBM, K steps between a barrier + synchronize pair, timed
           with CUDA events, max over ranks;
@@ -21,13 +21,15 @@ envs evenly over the GPUs instead (config 4: 65536 envs in all, 8192 per GPU in 
           (engine.step(None, host_poses, fetch=host_buffers): the engine runs both copies on its own streams,
           overlapped with the kernels of the neighbouring steps; the timed region ends after the last copy);
   roofline  algorithmic bytes of one step (every per-robot state field read and written once at the reference's
-          widths, the step-dict outputs and the pose input: 6680 B per robot for config 2) / the average duration of
+          widths, the step-dict outputs and the pose input: 6680 B per robot for config 4) / the average duration of
           the step's four kernels (traffic, fading, MAC, finish: CUDA events around them on their stream, eager
           launches), against the measured HBM copy bandwidth; traffic = DRAM bytes of those four kernels per step
           from an ncu capture (profiles/nr_step_traffic.json);
   cpu_baseline  the oracle port (oracle/nr_oracle.py, torch on the host cores, the reference's own op sequence) on a
-          bounded sample of the same workload.
-The state of one step is ~0.9 GB for config 2, larger than the 126 MB L2, so no L2 flush is needed between steps.
+          bounded sample of the same workload: the median of 3 windows, at the workload's full E where the oracle
+          steps it in seconds (configs 1, 2), else on a stated reduced E (256 envs).
+The state of one step is several GB (config 4: ~2.8 KB per robot), larger than the 126 MB L2, so no L2 flush is
+needed between steps.
 """
 from __future__ import annotations
 
@@ -39,6 +41,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 import torch
@@ -76,15 +79,25 @@ class Clocks:
         self.index, self.proc, self.path = index, None, None
 
     def start(self):
+        """Start sampling every 50 ms into a temporary file and wait (up to 3 s) for the first sample, so that even a
+        short timed region is covered."""
         try:
-            os.makedirs(os.path.join(ROOT, "gpurun_out"), exist_ok=True)
-            self.path = os.path.join(ROOT, "gpurun_out", f"clocks_{os.getpid()}.csv")
-            self.f = open(self.path, "w")
+            fd, self.path = tempfile.mkstemp(prefix="inb_clocks_", suffix=".csv")
+            self.f = os.fdopen(fd, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"], stdout=self.f,
+                                          "--format=csv,noheader,nounits", "-lms", "50"], stdout=self.f,
                                          stderr=subprocess.DEVNULL)
         except Exception:
             self.proc = None
+            return
+        t0 = time.time()
+        while time.time() - t0 < 3.0:
+            try:
+                if os.path.getsize(self.path) > 0:
+                    break
+            except OSError:
+                break
+            time.sleep(0.02)
 
     def stop(self):
         if self.proc is None:
@@ -109,6 +122,10 @@ class Clocks:
             for n, v in zip(names, c[5:9]):
                 if v.lower() == "active":
                     reasons.add(n)
+        try:
+            os.remove(self.path)
+        except OSError:
+            pass
         if not sm:
             return None
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
@@ -127,8 +144,9 @@ def dist_setup(n):
     return rank, dist.get_world_size(), dist
 
 
-def cpu_baseline(wl, cfg, E_sample, steps, warm=1):
-    """The oracle port (reference op sequence, torch on the host cores) on E_sample envs of the workload."""
+def cpu_baseline(wl, cfg, E_sample, steps, warm=1, windows=3):
+    """The oracle port (reference op sequence, torch on the host cores) on E_sample envs of the workload: `warm`
+    untimed steps, then `windows` windows of `steps` steps each; the value is the median window's env-steps/s."""
     from oracle.nr_oracle import OracleEngine
     tr = importlib.import_module("isaac-net_b200.traffic")
     presets = importlib.import_module("isaac-net_b200.presets")
@@ -152,13 +170,17 @@ def cpu_baseline(wl, cfg, E_sample, steps, warm=1):
         pos = mot.advance()
     for _ in range(warm):
         one()
-    t0 = time.perf_counter()
-    for _ in range(steps):
-        one()
-    dt = time.perf_counter() - t0
-    return {"value": E * steps / dt, "unit": "env-steps/s", "cores": threads, "kind": "port",
-            "sample": f"oracle port (torch CPU, reference op order) on {E} of {wl.E} envs x {R} robots, {steps} "
-                      f"control steps after {warm} warm-up"}
+    rates = []
+    for _ in range(windows):
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            one()
+        rates.append(E * steps / (time.perf_counter() - t0))
+    reduced = "" if E == wl.E else f" (reduced E: {E} of the workload's {wl.E} envs)"
+    return {"value": statistics.median(rates), "unit": "env-steps/s", "cores": threads, "kind": "port",
+            "windows": rates,
+            "sample": f"oracle port (torch CPU, reference op order) on {E} envs x {R} robots{reduced}, "
+                      f"{warm} warm-up step(s), then the median of {windows} windows of {steps} control steps"}
 
 
 def wl_id(wl):
@@ -182,11 +204,30 @@ def max_over_ranks(vals, dist, dev):
     return t.tolist()
 
 
+def shard_envs(wl, world, scaling):
+    """Envs per GPU: the workload's envs split evenly over `world` GPUs (strong), or its per-GPU batch (weak)."""
+    if scaling == "strong":
+        if wl.E % world:
+            raise SystemExit(f"{wl.E} envs do not split evenly over {world} GPUs")
+        return wl.E // world
+    return wl.envs_per_gpu
+
+
 def arm_config(wl, cfg, world, E=None):
-    return {"workload": wl.name, "envs_per_gpu": E or wl.envs_per_gpu, "robots": wl.R,
+    E = E or wl.envs_per_gpu
+    return {"workload": wl.name, "envs": E * world, "envs_per_gpu": E, "robots": wl.R,
             "slots_per_step": cfg.slots_per_step,
             "rbgs": cfg.n_subbands, "harq": cfg.n_harq, "frames": cfg.frame_buffer,
             "parallelism": f"env shards x{world}", "l2": "state > L2 (no flush needed)"}
+
+
+def cpu_envs(a, wl):
+    """Envs of the CPU sample: --cpu-envs, else the workload's whole per-GPU batch when the oracle steps it in a
+    few seconds (configs 1 and 2: 64 x 16 and 4096 x 32 robots), else 256 envs (a labelled reduced E: the oracle
+    needs ~1 s per step for 256 x 128 robots on 16 cores)."""
+    if a.cpu_envs:
+        return a.cpu_envs
+    return wl.E if wl.E * wl.R <= 4096 * 32 else 256
 
 
 def run_reference(a):
@@ -210,14 +251,14 @@ def run_reference(a):
     presets = importlib.import_module("isaac-net_b200.presets")
     wl = presets.workload(a.workload)
     cfg = wl.config()
-    steps = max(1, a.steps)
-    envs = max(16, min(a.cpu_envs, (a.cpu_envs * 200 // steps) // 16 * 16))
-    res = cpu_baseline(wl, cfg, envs, steps, warm=max(1, min(a.warmup, 2)))
+    steps = max(3, a.steps)
+    envs = cpu_envs(a, wl)
+    res = cpu_baseline(wl, cfg, envs, max(1, steps // 3), warm=max(1, min(a.warmup, 2)))
     v = res["value"]
     line = {"metric": "env-steps/sec", "value": v, "unit": "env-steps/s", "n_gpus": a.gpus, "steps": steps,
-            "warmup": a.warmup, "ms_per_step": envs / v * 1e3, "higher_is_better": True, "scaling": "weak",
+            "warmup": a.warmup, "ms_per_step": envs / v * 1e3, "higher_is_better": True, "scaling": a.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
-            "impl": "reference", "config": arm_config(wl, cfg, a.gpus),
+            "impl": "reference", "config": arm_config(wl, cfg, a.gpus, shard_envs(wl, a.gpus, a.scaling)),
             "cpu_baseline": res, "e2e": {"value": v, "unit": "env-steps/s", "h2d_bytes_per_step": 0,
                                           "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -403,14 +444,15 @@ def main():
     ap.add_argument("--steps", type=int, default=1000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="b200", choices=("b200", "reference"))
-    ap.add_argument("--workload", default="2", help="BASELINE config 1-5, or 'ul': the reference's published NR "
-                                                     "benchmark case (NRConfig() defaults, 4096 x 100 per GPU)")
-    ap.add_argument("--cpu-envs", type=int, default=256)
-    ap.add_argument("--cpu-steps", type=int, default=5)
+    ap.add_argument("--workload", default="4", help="BASELINE config 1-5 (default 4: 65536 envs x 128 robots), or "
+                                                     "'ul': the reference's published NR benchmark case (NRConfig() "
+                                                     "defaults, 4096 x 100 per GPU)")
+    ap.add_argument("--cpu-envs", type=int, default=0, help="envs of the CPU sample (0: see cpu_envs)")
+    ap.add_argument("--cpu-steps", type=int, default=2, help="steps per window of the CPU sample (3 windows)")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--scaling", default="weak", choices=("weak", "strong"),
-                    help="weak: every GPU runs the workload's per-GPU envs (config 4: 8192 of its 65536); strong: "
-                         "the workload's envs split evenly over the GPUs")
+    ap.add_argument("--scaling", default="strong", choices=("weak", "strong"),
+                    help="strong (default): the workload's envs split evenly over the GPUs (config 4: 65536 in all, "
+                         "8192 per GPU at N = 8); weak: every GPU runs the workload's per-GPU envs (config 4: 8192)")
     a = ap.parse_args()
     if a.workload != "ul":
         a.workload = int(a.workload)
@@ -426,12 +468,7 @@ def main():
     wl = presets.workload(a.workload)
     cfg = wl.config()
     R = wl.R
-    if a.scaling == "strong":
-        if wl.E % world:
-            raise SystemExit(f"{wl.E} envs do not split evenly over {world} GPUs")
-        E = wl.E // world
-    else:
-        E = wl.envs_per_gpu
+    E = shard_envs(wl, world, a.scaling)
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
     eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
@@ -461,7 +498,6 @@ def main():
         eng.step(None, dev_ring[(a.warmup + i) % NPOS])
     ev1.record()
     barrier()
-    clk = clocks.stop()
     t_ms = ev0.elapsed_time(ev1)
     # e2e: poses from pinned host memory each step, observations read back each step
     obs_keys = ("newest", "queue_len", "queue_bytes", "sinr_db")
@@ -477,6 +513,7 @@ def main():
     torch.cuda.current_stream(dev).wait_event(eng.fetch_done)
     e1.record()
     barrier()
+    clk = clocks.stop()     # sampled over the device-resident and the end-to-end timed regions
     e2e_ms = e0.elapsed_time(e1)
     # duration of the step's kernels alone: CUDA events around them on their stream (eager launches, same kernels)
     nk = min(a.steps, 20)
@@ -528,7 +565,7 @@ def main():
     obs["frac"] = obs["achieved_gbs"] / peak
     line["net_obs"] = obs
     if rank == 0 and world == 1 and not a.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(wl, cfg, a.cpu_envs, a.cpu_steps)
+        line["cpu_baseline"] = cpu_baseline(wl, cfg, cpu_envs(a, wl), a.cpu_steps)
     if rank == 0:
         print(json.dumps(line))
     if dist is not None:

@@ -237,7 +237,11 @@ int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array
  * inside the library (INB_NOALLOC_GAIN_MAX float32 elements per device), so `gain` / `gain_cap` are ignored and
  * nothing is allocated at call time.  No counterpart in the reference (its torch backends allocate per call).
- *   -10: the step's gain rows exceed INB_NOALLOC_GAIN_MAX (use inb_nr_step with a caller buffer);
+ * The array is 128 MiB of device memory on each device where this entry point has been called, held until exit; it
+ * sits in a module of its own, so processes that never call this entry point do not load it.
+ *   -10: the step's gain rows exceed INB_NOALLOC_GAIN_MAX: (UL rows + 1) x S x E x R with one cell, UL rows x C x S x
+ *        E x R with C > 1 cells (use inb_nr_step with a caller buffer); checked only when the call's phases run
+ *        the fading or the MAC launch;
  *   -8 / -9: no current CUDA device / the array's device address could not be resolved.
  * The array's address is resolved on the first call on each device: make that call before capturing a CUDA graph.
  * The array needs no initial value (each step writes every row it reads), but all calls on one device share it, so

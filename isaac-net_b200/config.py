@@ -341,14 +341,9 @@ class NRConfig:
         """[(feature, why)] of settings the B200 engine does not implement (empty: it runs)."""
         out = []
         d = NRConfig()
+        # the SR/BSR pipeline fields (sr_boot_*, bsr_*, rlc_tail_*) are read only under ul_grant_model="bsr"
+        # (reference config.py:119, 307), so a lumped config keeps whatever values they hold
         chk = [("dl", "the downlink MAC is not built (uplink control-step path only)"),
-               ("sr_boot_slots", "the SR/BSR grant pipeline is not built"),
-               ("sr_boot_bytes", "the SR/BSR grant pipeline is not built"),
-               ("bsr_delay_slots", "the SR/BSR grant pipeline is not built"),
-               ("bsr_hdr_bytes", "the SR/BSR grant pipeline is not built"),
-               ("bsr_est_hdr_bytes", "the SR/BSR grant pipeline is not built"),
-               ("rlc_tail_bytes", "the SR/BSR grant pipeline is not built"),
-               ("rlc_tail_timer_ms", "the SR/BSR grant pipeline is not built"),
                ("ul_mini_slot_symbols", "mini-slot occasions are not built"),
                ("ul_grant_model", "the SR/BSR grant pipeline is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),

@@ -2,9 +2,7 @@
 // map / blockage, nr_radio.cu; only with InbStepArgs.rm.on), the fading (nr_fading.cu), the MAC kernel variant of the
 // group width (nr_step_g16.cu ... nr_step_g128.cu; the kernel is in nr_step.cuh) and the end-of-step finish
 // (nr_finish.cu).
-#include <mutex>
-
-#include "nr_common.cuh"
+#include "nr_step_entry.cuh"
 namespace inb {
 cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
@@ -14,8 +12,7 @@ cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_radio(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
 
-// argument checks shared by both entry points; *gain_need = float32 elements of the step's gain rows
-static int check_args(const InbStepArgs& a, long long* gain_need) {
+int check_args(const InbStepArgs& a, long long* gain_need) {
   const InbParams& p = a.p;
   if (p.R < 1 || p.R > 128 || p.S < 1 || p.S > INB_MAX_S || p.P < 1 || p.P > INB_MAX_P || p.F < 1 ||
       p.F > INB_MAX_F || p.M < 0 || p.M > INB_MAX_M || p.MCS < 1 || p.MCS > INB_MAX_MCS || p.K_rows < 0 ||
@@ -48,7 +45,7 @@ static int check_args(const InbStepArgs& a, long long* gain_need) {
   return 0;
 }
 
-static int launch_all(const InbStepArgs& args, cudaStream_t s) {
+int launch_all(const InbStepArgs& args, cudaStream_t s) {
   InbStepArgs a = args;
   const InbParams& p = a.p;
   cudaError_t err = cudaSuccess;
@@ -78,26 +75,6 @@ static int launch_all(const InbStepArgs& args, cudaStream_t s) {
   return err == cudaSuccess ? 0 : -100 - (int)err;
 }
 
-// Gain-row scratch of inb_nr_step_noalloc: a fixed array in the library's device image (one per device the library
-// runs on), resolved to a device address once per device.  Its contents need no initial value: the fading launch of
-// a step writes every row the MAC launch of that step reads.
-__device__ __align__(256) float g_gain_scratch[INB_NOALLOC_GAIN_MAX];
-constexpr int kMaxDevices = 64;
-static float* g_scratch_addr[kMaxDevices];
-static std::mutex g_scratch_mu;
-
-static int scratch_of_current_device(float** out) {
-  int dev = -1;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return -8;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  if (g_scratch_addr[dev] == nullptr) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_gain_scratch) != cudaSuccess || p == nullptr) return -9;
-    g_scratch_addr[dev] = static_cast<float*>(p);
-  }
-  *out = g_scratch_addr[dev];
-  return 0;
-}
 }  // namespace inb
 
 extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
@@ -108,22 +85,6 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
   const int rc = inb::check_args(a, &need);
   if (rc != 0) return rc;
   if (a.gain == nullptr || a.gain_cap < need) return -6;
-  return inb::launch_all(a, (cudaStream_t)cuda_stream);
-}
-
-extern "C" int inb_nr_step_noalloc(const InbStepArgs* args, void* cuda_stream) {
-  if (args == nullptr) return -1;
-  if (args->p.E <= 0) return 0;
-  long long need = 0;
-  const int rc = inb::check_args(*args, &need);
-  if (rc != 0) return rc;
-  if (need > (long long)INB_NOALLOC_GAIN_MAX) return -10;
-  float* scratch = nullptr;
-  const int sr = inb::scratch_of_current_device(&scratch);
-  if (sr != 0) return sr;
-  InbStepArgs a = *args;
-  a.gain = scratch;
-  a.gain_cap = INB_NOALLOC_GAIN_MAX;
   return inb::launch_all(a, (cudaStream_t)cuda_stream);
 }
 

@@ -1,7 +1,8 @@
-// Fused NR uplink control step (sm_100a): traffic enqueue and arrival gate, large-scale radio, the K scheduled slots
-// (AR(1) fading, SR, candidate selection, retransmission admission, RBG-by-RBG PF / RR allocation, EESM link
-// adaptation, HARQ decode and update, OLLA, PF averages, RLC in-order delivery) and the end-of-step finish (delivery /
-// timeout / drop masks, outputs, FIFO compaction) in ONE launch.
+// Fused NR uplink MAC of one control step (sm_100a): traffic enqueue and arrival gate, large-scale radio, and the K
+// scheduled slots (SR, candidate selection, retransmission admission, RBG-by-RBG PF / RR allocation, EESM link
+// adaptation, HARQ decode and update, OLLA, PF averages, RLC in-order delivery).  The AR(1) fading of the step runs
+// before it (nr_fading.cu) and the end-of-step finish (delivery / timeout / drop masks, outputs, FIFO compaction)
+// after it (nr_finish.cu), as separate launches on the same stream.
 //
 // Thread mapping: one thread per robot; the R robots of an env form a group of GW lanes (GW = next power of two >= R,
 // at least 16).  GW <= 32: 128 / GW envs per 128-thread block, group collectives are segmented warp shuffles.

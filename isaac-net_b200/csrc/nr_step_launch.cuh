@@ -1,4 +1,5 @@
 #pragma once
+#include <atomic>
 // Launch of the fused step kernel for one group width GW (robots per env rounded up to a power of two).
 #include "nr_step.cuh"
 namespace inb {
@@ -8,11 +9,21 @@ cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
   const int gpb = GW > 32 ? 1 : 128 / GW;
   const int vecs = a.ul_ref_in != nullptr ? 3 : 2;
   const size_t smem = (size_t)vecs * a.p.S * (NT + 1) * sizeof(float);
-  static size_t configured = 0;   // dynamic shared memory above 48 KB needs an opt-in, once per size
-  if (smem > 48 * 1024 && smem > configured) {
-    cudaError_t e = cudaFuncSetAttribute(nr_step_kernel<GW, NCT, SV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // dynamic shared memory above 48 KB needs an opt-in, which holds per device: remembered per device and size
+  static std::atomic<size_t> configured[64];
+  if (smem > 48 * 1024) {
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    configured = smem;
+    if (dev < 0 || dev >= 64 || smem > configured[dev].load(std::memory_order_acquire)) {
+      e = cudaFuncSetAttribute(nr_step_kernel<GW, NCT, SV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return e;
+      if (dev >= 0 && dev < 64) {   // raise the remembered size (several threads may race here; the max wins)
+        size_t cur = configured[dev].load(std::memory_order_relaxed);
+        while (smem > cur && !configured[dev].compare_exchange_weak(cur, smem, std::memory_order_acq_rel)) {
+        }
+      }
+    }
   }
   dim3 grid((a.p.E + gpb - 1) / gpb), block(NT);
   nr_step_kernel<GW, NCT, SV><<<grid, block, smem, stream>>>(a);

@@ -2,7 +2,9 @@
 
 Two engines with the same seed step the same poses, one through each entry point; every output and every state
 tensor must be bitwise equal after each of two consecutive steps (the second step reuses the array the first one
-wrote).  The size check refuses a step whose gain rows exceed the array, before anything is launched.
+wrote); the three-cell case uses the multi-cell row layout (one row per UL slot holding every link's gain).  The
+size check refuses a step whose gain rows exceed the array, before anything is launched, and only for calls that run
+the fading or MAC launch.
 This file is collected last and needs nothing from the other test files.
 """
 import ctypes
@@ -37,7 +39,7 @@ def _same(a, b):
     return torch.equal(a, b)
 
 
-@pytest.mark.parametrize("wl_i,E,R", [(1, 64, 16), (2, 256, 32)])
+@pytest.mark.parametrize("wl_i,E,R", [(1, 64, 16), (2, 256, 32), (3, 32, 64)])
 def test_noalloc_step_equals_step_on_two_consecutive_calls(wl_i, E, R):
     presets = importlib.import_module("isaac-net_b200.presets")
     wl = presets.workload(wl_i)
@@ -74,4 +76,23 @@ def test_noalloc_refuses_oversize_gain_rows():
     a.p.rows[0][1] = 12                           # one UL row
     a.p.E = nat.NOALLOC_GAIN_MAX // (2 * a.p.S * a.p.R) + 1
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert eng.L.inb_nr_step_noalloc(ctypes.byref(a), stream) == -10
+
+
+def test_noalloc_size_check_only_for_the_gain_phases():
+    """A call whose phases launch neither the fading nor the MAC kernel (phases = 1 with no radio launch configured:
+    nothing runs) is not refused by the gain-row limit."""
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(1)
+    eng = ib.make_engine("L2", 8, 16, "cuda:0", wl.config(), seed=1)
+    a = nat.InbStepArgs.from_buffer_copy(eng._args)
+    a.pathgain_in = eng.st["olla"].data_ptr()
+    a.p.K_rows = 1
+    a.p.rows[0][1] = 12
+    a.p.E = nat.NOALLOC_GAIN_MAX // (2 * a.p.S * a.p.R) + 1
+    a.rm.on = 0
+    a.phases = 1
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    assert eng.L.inb_nr_step_noalloc(ctypes.byref(a), stream) == 0
+    a.phases = 2
     assert eng.L.inb_nr_step_noalloc(ctypes.byref(a), stream) == -10
