@@ -450,6 +450,8 @@ def main():
     ap.add_argument("--cpu-envs", type=int, default=0, help="envs of the CPU sample (0: see cpu_envs)")
     ap.add_argument("--cpu-steps", type=int, default=2, help="steps per window of the CPU sample (3 windows)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--envs", type=int, default=0, help="envs per GPU (0: set by --scaling); a smaller batch of the "
+                                                       "same workload, for profiling captures")
     ap.add_argument("--scaling", default="strong", choices=("weak", "strong"),
                     help="strong (default): the workload's envs split evenly over the GPUs (config 4: 65536 in all, "
                          "8192 per GPU at N = 8); weak: every GPU runs the workload's per-GPU envs (config 4: 8192)")
@@ -468,7 +470,7 @@ def main():
     wl = presets.workload(a.workload)
     cfg = wl.config()
     R = wl.R
-    E = shard_envs(wl, world, a.scaling)
+    E = a.envs or shard_envs(wl, world, a.scaling)
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
     eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)

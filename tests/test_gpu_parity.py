@@ -8,8 +8,9 @@
 3. kernel vs the reference's own outputs (CPU goldens) teacher-forced: the engine is loaded with the reference state
    before each step and fed the reference's arrivals and path gains (the radio evaluated on the CPU exactly as the
    reference does; torch itself moves them by up to 1.3e-3 dB between CPU and CUDA on config 3, which shifts SINRs
-   and so delivery slots); at most 1 robot-step in 1000 may differ in any output (CUDA vs CPU transcendentals and
-   reduction order move threshold decisions by an ulp), float outputs within 1e-5 relative / 1e-3 absolute.
+   and so delivery slots).  No robot-step may differ in any integer output, and float outputs must be within 1e-5
+   relative / 1e-3 absolute (CUDA's and the CPU's transcendentals differ by ulps; measured on a B200: 0 robot-steps
+   differ in every case).  The handover stress case is the one exception, bounded by the reference's tie order.
 """
 import importlib
 import math
@@ -261,25 +262,25 @@ def _teacher_forced_flips(case):
 @pytest.mark.parametrize("case", [c for c in CASES if c != "3s"])
 def test_kernel_vs_reference_goldens_teacher_forced(case):
     flips, total = _teacher_forced_flips(case)
-    assert flips * 1000 <= total, (flips, total)
+    assert flips == 0, (flips, total)
 
 
 def test_kernel_vs_reference_handover_stress_teacher_forced():
     """The handover stress case: PF averages restart at every handover, so equal retransmission ranking keys are
     common and the reference's CPU argsort orders them its own way, while the kernel ranks ties by robot index.  The
     kernel may differ from the reference in no more robot-steps than the oracle with the kernel's tie rule does
-    (CPU, teacher-forced), plus the usual 1 in 1000."""
+    (CPU, teacher-forced; measured on a B200: 82 of 4224 robot-steps, every one a tie of the ranking)."""
     from test_oracle_golden import _seq_flips
     flips, total = _teacher_forced_flips("3s")
     ties, n = _seq_flips("3s", ties="stable")
-    assert flips <= ties + max(1, total // 1000), (flips, ties, total)
+    assert flips <= ties, (flips, ties, total)
 
 
 @pytest.mark.parametrize("case", POLICY_CASES)
 def test_kernel_policy_case(case):
     """Policy submits with extras, SNR inputs ([E,R] and per RBG) and the legacy step form, on the engine: every output
-    and state bitwise equal to the oracle ("seq", same device); against the reference's own outputs (CPU fixture) at
-    most 1 robot-step in 1000 may differ (CPU vs CUDA transcendentals), float outputs within 1e-5 / 1e-3."""
+    and state bitwise equal to the oracle ("seq", same device); against the reference's own outputs (CPU fixture) no
+    robot-step may differ, float outputs within 1e-5 / 1e-3 (CPU vs CUDA transcendentals)."""
     from test_oracle_golden import run_policy_step
     g = Golden(case)
     cfg, wl = g.config(), g.workload()
@@ -312,4 +313,4 @@ def test_kernel_policy_case(case):
             rows &= eq[:, None] if eq.ndim == 1 else eq.reshape(g.E, g.R, -1).all(-1)
         flips += int((~rows).sum())
         total += g.E * g.R
-    assert flips * 1000 <= total, (flips, total)
+    assert flips == 0, (flips, total)
