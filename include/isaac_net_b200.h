@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 11
+#define INB_ABI_VERSION 12
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -46,6 +46,7 @@ extern "C" {
 #define INB_BLK_REGIONS 4 /* blockage model A regions per env (TR 38.901 Sec. 7.6.4.1: K = 4) */
 #define INB_CDF_STRIDE 64 /* blockage CDF table: entries per coarse bucket of the two-level search */
 #define INB_NCTR 64       /* per-env counter words (int64) */
+#define INB_BSR_DEPTH 4   /* buffer-status reports in flight per robot (ul_grant_model = "bsr") */
 
 /* counter words of InbStepArgs.ctr (per env, int64), MacLink.ctr / ntx_hist / rv_tx / rv_fail (mac.py:116-126) */
 enum {
@@ -74,6 +75,14 @@ typedef struct {
   uint8_t *pending;                                        /* [E] */
   float *ni_ul;                                            /* [E,C,S] */
   float *last_nprb;             /* [E,R] PRBs of the robot's last PUSCH (ul_amc_alloc = "previous"; NULL otherwise) */
+  /* ul_grant_model = "bsr" (NULL otherwise), UlMac's BSR_STATE (isaac_net/core/mac_ul.py:45-50): the gNB's buffer
+   * estimate, the bootstrap grant owed after an SR, the reports in flight (value, slot sent; -2^62 = empty), the RLC
+   * header residue hidden from the reports and the slot its timer reports it, the queue size last seen, and whether
+   * new data arrived since the last buffer-draining TB */
+  int64_t *bsr_est;                                        /* [E,R] */
+  int64_t *bsr_rep_v, *bsr_rep_g;                          /* [E,R,INB_BSR_DEPTH] */
+  int64_t *bsr_hid, *bsr_hid_until, *bsr_enq_seen;         /* [E,R] */
+  uint8_t *bsr_boot, *bsr_armed;                           /* [E,R] */
 } InbState;
 
 /* Step outputs (the step dict of NREngine.step), [E,R,F] unless noted. */
@@ -161,6 +170,10 @@ typedef struct {
                                    robot's last PUSCH (s.last_nprb, this grant's when 0), its TBS for this grant
                                    (mac.py:393-400, 484) */
   int32_t lena_ctr;             /* 5G-LENA MAC switches on: also count tb_bytes, tb_empty, retx_block (mac.py:119-121) */
+  /* ul_grant_model = "bsr": the SR / BSR grant pipeline (mac_ul.py:262-329) replaces the lumped SR grant; slots after
+   * an SR until the bootstrap grant, its bytes, the report delay, the RLC timer; header bytes of a report, of the
+   * gNB's estimate, and the RLC residue a buffer-draining TB leaves behind */
+  int32_t bsr_on, sr_boot_slots, sr_boot_bytes, bsr_delay, rlc_tail_slots, bsr_hdr, bsr_est_hdr, rlc_tail_bytes;
 } InbParams;
 
 /* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes
@@ -231,7 +244,8 @@ typedef struct {
 
 /* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.
  * With rm.on and pathgain_in NULL the radio launch evaluates the poses and the MAC reads rm.pg; a pathgain_in
- * skips it.  -11: a radio pointer or size is missing or out of range, or o.blocked is set without the launch. */
+ * skips it.  -11: a radio pointer or size is missing or out of range, or o.blocked is set without the launch.
+ * -12: p.bsr_on without the InbState.bsr_* buffers (or a negative pipeline delay). */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array

@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 11
+ABI_VERSION = 12
 MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -28,7 +28,9 @@ i32, i64, u32, f32, f64 = ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32, ctype
 STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg", "csi", "h", "spec", "k_lin",
                 "h_state", "h_lo", "h_hi", "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb", "cap", "start",
                 "end_", "cls", "hid", "tag", "prio", "lost", "det", "fin", "off", "dline", "serv", "a3_cand", "a3_cnt",
-                "ho_end", "n_ho", "pending", "ni_ul", "last_nprb")
+                "ho_end", "n_ho", "pending", "ni_ul", "last_nprb", "bsr_est", "bsr_rep_v", "bsr_rep_g", "bsr_hid",
+                "bsr_hid_until", "bsr_enq_seen", "bsr_boot", "bsr_armed")
+BSR_DEPTH = 4          # INB_BSR_DEPTH
 OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
               "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
               "sinr_db", "pathgain", "det_env", "serving_cell", "blocked", "los")
@@ -74,7 +76,9 @@ class InbParams(ctypes.Structure):
                 + [(n, f32) for n in ("a3_off", "a3_hyst", "floor_rx", "noise_mw", "ue_tx_ref", "ref_db", "pc_p0",
                                       "pc_alpha", "li_alpha", "li_beta")]
                 + [("los_const", i32), ("pf_rbg", i32), ("pf_freeze", i32), ("field_fma", i32), ("tdma", i32),
-                   ("amc_prev", i32), ("lena_ctr", i32)])
+                   ("amc_prev", i32), ("lena_ctr", i32)]
+                + [(n, i32) for n in ("bsr_on", "sr_boot_slots", "sr_boot_bytes", "bsr_delay", "rlc_tail_slots",
+                                      "bsr_hdr", "bsr_est_hdr", "rlc_tail_bytes")])
 
 
 class InbRadio(ctypes.Structure):

@@ -345,7 +345,6 @@ class NRConfig:
         # (reference config.py:119, 307), so a lumped config keeps whatever values they hold
         chk = [("dl", "the downlink MAC is not built (uplink control-step path only)"),
                ("ul_mini_slot_symbols", "mini-slot occasions are not built"),
-               ("ul_grant_model", "the SR/BSR grant pipeline is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),
                ("ul_tpc", "closed-loop power control is not built"),
                ("eff_sinr", "only EESM is built"),

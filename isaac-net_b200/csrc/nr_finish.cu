@@ -216,6 +216,10 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
       pend = false;
     }
     bsr = bsr < enq - sent ? bsr : enq - sent;
+    if (p.bsr_on && act && l == 0) {   // UlMac.compact (mac_ul.py:255-260): the residue never exceeds the unsent bytes
+      const long long h = st.bsr_hid[er];
+      st.bsr_hid[er] = h < enq - sent ? h : enq - sent;
+    }
     const long long qb = enq - ack_of(pend, floor_, sent);
     if (act && l == 0) {
       o.newest[er] = newest >= 0 ? newest - epoch : -1;

@@ -29,6 +29,14 @@ __global__ void nr_reset_kernel(const InbResetArgs A) {
   st.sent[er] = 0; st.floor_[er] = 0; st.bsr[er] = 0; st.sr_t[er] = -1; st.last_tx[er] = -1; st.enq[er] = 0;
   st.olla[er] = 0.0f; st.avg[er] = 100.0f;
   if (st.last_nprb != nullptr) st.last_nprb[er] = 0.0f;
+  if (st.bsr_est != nullptr) {   // BSR_STATE initial values (mac_ul.py:45-50)
+    st.bsr_est[er] = 0; st.bsr_hid[er] = 0; st.bsr_hid_until[er] = -1; st.bsr_enq_seen[er] = 0;
+    st.bsr_boot[er] = 0; st.bsr_armed[er] = 0;
+    for (int j = 0; j < INB_BSR_DEPTH; ++j) {
+      st.bsr_rep_v[er * INB_BSR_DEPTH + j] = 0;
+      st.bsr_rep_g[er * INB_BSR_DEPTH + j] = -BIGI;
+    }
+  }
   const uint32_t base_h = key_stream(kenv, (uint32_t)(SITE_H0 << 16));
   const int C = A.C > 1 ? A.C : 1;
   for (int s = 0; s < S; ++s) st.csi[er * S + s] = 0.0f;

@@ -23,6 +23,11 @@ int check_args(const InbStepArgs& a, long long* gain_need) {
                   a.s.ho_end == nullptr || a.s.n_ho == nullptr || a.s.pending == nullptr || a.s.ni_ul == nullptr ||
                   a.o.serving_cell == nullptr))
     return -7;
+  if (p.bsr_on && (a.s.bsr_est == nullptr || a.s.bsr_rep_v == nullptr || a.s.bsr_rep_g == nullptr ||
+                   a.s.bsr_hid == nullptr || a.s.bsr_hid_until == nullptr || a.s.bsr_enq_seen == nullptr ||
+                   a.s.bsr_boot == nullptr || a.s.bsr_armed == nullptr || p.sr_boot_slots < 0 || p.bsr_delay < 0 ||
+                   p.rlc_tail_slots < 1))
+    return -12;   // the BSR pipeline's state (InbState.bsr_*) or its timing is missing
   if (a.pos == nullptr && a.pathgain_in == nullptr) return -4;
   const InbRadio& rm = a.rm;
   const bool radio = rm.on && a.pathgain_in == nullptr;   // the radio launch runs (poses through the radio)

@@ -26,6 +26,7 @@
 #include <cmath>
 #include <cstdint>
 
+#include "nr_bsr.cuh"
 #include "nr_common.cuh"
 
 namespace inb {
@@ -683,6 +684,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     csi_src = -2;
     sr_t = -1;
     bsr = enq - sent;
+    if (p.bsr_on) bsr_handover(st, p, er, enq, sent);
   };
 
 
@@ -705,16 +707,22 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       }
       enq = vis > base ? vis : base;
     }
-    // ---- SR (UlMac.sr_step, mac_ul.py:66-71)
-    if (srf && (enq - sent > 0) && bsr <= 0 && sr_t < 0) sr_t = g;
+    // ---- SR (UlMac.sr_step, mac_ul.py:66-71; the BSR pipeline's, mac_ul.py:280-287)
+    if (srf && act) {
+      if (p.bsr_on) bsr_sr_step(st, er, enq, sent, g, sr_t);
+      else if ((enq - sent > 0) && bsr <= 0 && sr_t < 0) sr_t = g;
+    }
     if (!uls) continue;
 
     // =================================================================== UL data slot (MacLink.slot, mac.py:228-508)
     const long long unsent = enq - sent;
     // the CSI of this decision is gain row u (the gain of the previous UL row), this row's fading gain is row u + 1
     const long long g_csi = (long long)u * plane, g_gain = g_csi + plane;
-    // lumped SR grant (mac_ul.py:140-147)
-    if (sr_t >= 0 && g - sr_t >= p.sr_delay) {
+    // lumped SR grant (mac_ul.py:140-147), or the BSR pipeline's bootstrap grant and matured reports
+    long long need_bsr = 0;
+    if (p.bsr_on) {
+      if (act) need_bsr = bsr_pre_slot(st, p, er, enq, g, sr_t);
+    } else if (sr_t >= 0 && g - sr_t >= p.sr_delay) {
       bsr = bsr < 1 ? 1 : bsr;
       sr_t = -1;
     }
@@ -733,7 +741,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     const bool any_free = p_new >= 0;
     if (p_new < 0) p_new = 0;
-    const long long need = bsr < unsent ? bsr : unsent;
+    const long long need = p.bsr_on ? need_bsr : (bsr < unsent ? bsr : unsent);
     bool new_el = act && any_free && need > 0 && !has_rx;
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
@@ -1247,7 +1255,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     long long cap_b = tbs_new / 8 - p.tb_oh;
     cap_b = cap_b < 1 ? 1 : cap_b;
-    const long long byt_new = cap_b < unsent ? cap_b : unsent;
+    const long long byt_new = (p.bsr_on && tx_new) ? bsr_tb_payload(st, p, er, enq, sent, cap_b, g)
+                                                   : (cap_b < unsent ? cap_b : unsent);
     // ---- bind the TB to its HARQ process (mac.py:406-423)
     const int p_tx = tx_rx ? rx_p : p_new;
     const long long hp = eP + p_tx;
@@ -1411,7 +1420,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       const float up = fm(p.olla_up, ok ? 1.0f : 0.0f), dn = fm(p.olla_dn, fail ? 1.0f : 0.0f);
       olla = clampf_t(fs(fa(olla, up), dn), -10.0f, 10.0f);
     }
-    if (tx) bsr = enq - sent;
+    if (p.bsr_on) {
+      if (act) bsr_post_slot(st, p, er, enq, sent, g, tx, tx_new, tbs_new);
+    } else if (tx) {
+      bsr = enq - sent;
+    }
     if constexpr (MC) csi_src = u;   // the serving link's gain of this row is the CSI of the next decision
     ++u;
     if (!PFR && !p.pf_freeze) {

@@ -204,6 +204,13 @@ class NRB200Engine:
         st["dline"] = full((E, R, F), torch.float64, math.inf)
         if self.config.ul_amc_alloc == "previous":   # AMC_STATE (mac_ul.py:51)
             st["last_nprb"] = full((E, R), f32, 0.0)
+        if self.config.ul_grant_model == "bsr":      # BSR_STATE (mac_ul.py:45-50)
+            st["bsr_est"] = full((E, R), L, 0)
+            st["bsr_rep_v"] = full((E, R, nat.BSR_DEPTH), L, 0)
+            st["bsr_rep_g"] = full((E, R, nat.BSR_DEPTH), L, -(2 ** 62))
+            st["bsr_hid"], st["bsr_hid_until"] = full((E, R), L, 0), full((E, R), L, -1)
+            st["bsr_enq_seen"] = full((E, R), L, 0)
+            st["bsr_boot"], st["bsr_armed"] = full((E, R), b, False), full((E, R), b, False)
         self.st = st
 
     def _state_struct(self):
@@ -242,6 +249,12 @@ class NRB200Engine:
         p.pf_rbg, p.pf_freeze = int(cfg.pf_update == "rbg"), int(cfg.pf_avg_idle == "freeze")
         p.tdma, p.amc_prev = int(cfg.ul_retx_sched == "tdma"), int(cfg.ul_amc_alloc == "previous")
         p.lena_ctr = int(bool(cfg.lena_mac_switches()))
+        p.bsr_on = int(cfg.ul_grant_model == "bsr")
+        if p.bsr_on:   # the SR / BSR pipeline's timing and header sizes (config.py:588-594, 1088-1090)
+            p.sr_boot_slots, p.sr_boot_bytes = int(cfg.sr_boot_slots), int(cfg.sr_boot_bytes)
+            p.bsr_delay, p.rlc_tail_slots = int(cfg.bsr_delay_slots), int(cfg.rlc_tail_timer_slots)
+            p.bsr_hdr, p.bsr_est_hdr = int(cfg.bsr_hdr_bytes), int(cfg.bsr_est_hdr_bytes)
+            p.rlc_tail_bytes = int(cfg.rlc_tail_bytes)
         p.target = _f32(cfg.bler_target)
         p.inv_S = _f32(1.0 / self.S)
         p.s0_snr, p.c0_cbs = _f32(tab.s0), _f32(tab.c0)
@@ -1120,7 +1133,10 @@ class NRB200Engine:
             "q.cls": "cls", "q.det": "det", "q.hid": "hid", "q.off": "off", "q.tag": "tag", "q.prio": "prio",
             "q.dline": "dline", "net.h": "h", "net.spec": "spec", "net.k_lin": "k_lin", "assoc.serv": "serv",
             "assoc.a3_cand": "a3_cand", "assoc.a3_cnt": "a3_cnt", "assoc.ho_end": "ho_end", "assoc.n_ho": "n_ho",
-            "assoc.pending": "pending", "net.ni_ul": "ni_ul", "ul.last_nprb": "last_nprb"}
+            "assoc.pending": "pending", "net.ni_ul": "ni_ul", "ul.last_nprb": "last_nprb",
+            "ul.est": "bsr_est", "ul.boot": "bsr_boot", "ul.rep_v": "bsr_rep_v", "ul.rep_g": "bsr_rep_g",
+            "ul.hid": "bsr_hid", "ul.hid_until": "bsr_hid_until", "ul.enq_seen": "bsr_enq_seen",
+            "ul.armed": "bsr_armed"}
 
     # the radio field the kernel evaluates, under the reference's names (RadioMC.k / phi for log_distance,
     # TR38901Channel.sf_los for tr38901 with the forced LOS state)

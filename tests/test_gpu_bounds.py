@@ -1,7 +1,7 @@
 """The bounds-checked build (INB_CHECK: every global index of the MAC kernel checked against its array, an
 out-of-range one recorded in the device status word and redirected to element 0) runs the configs' step sequences
-with a partial reset, graph and eager steps, radio map and blockage, several cells, policy submits and SNR input, and
-ends with status 0.  It runs in a child process because the library variant is chosen when the package loads."""
+with a partial reset, graph and eager steps, radio map and blockage, several cells, the SR / BSR grant pipeline,
+policy submits and SNR input, and ends with status 0.  It runs in a child process because the library variant is chosen when the package loads."""
 import os
 import subprocess
 import sys
@@ -21,7 +21,8 @@ dev = torch.device("cuda:0")
 bad = []
 for wl_i, E, R, over in ((1, 8, 16, {}), (2, 16, 32, {}), (2, 8, 32, dict(scheduler="rr", retx_priority=False)),
                          (3, 4, 64, {}), (5, 4, 48, {}), (1, 4, 16, dict(blockage=True, blockage_model="stochastic")),
-                         (4, 2, 128, {})):
+                         (4, 2, 128, {}), (2, 8, 32, dict(ul_grant_model="bsr")),
+                         (3, 4, 64, dict(ul_grant_model="bsr", a3_ttt_ms=2.0, a3_hyst_db=0.5))):
     wl = presets.workload(wl_i)
     cfg = wl.config(**over)
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)

@@ -98,6 +98,9 @@ VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round r
     # groups of 16 and 128 lanes
     "1_saturated": (1, 8, 16, dict(traffic=(_bursty(1500, 2000),), ue_tx_dbm=-6.0)),
     "4_saturated": (4, 2, 128, dict(traffic=(_bursty(8192, 400),), msg_sizes=(8192.0,), ue_tx_dbm=-8.0)),
+    # the SR / BSR grant pipeline with the round-robin instance and on groups of 128 lanes
+    "1_bsr": (1, 8, 16, dict(ul_grant_model="bsr", ue_tx_dbm=-12.0, max_harq_tx=2)),
+    "4_bsr": (4, 2, 128, dict(ul_grant_model="bsr", ue_tx_dbm=-8.0)),
 }
 
 

@@ -74,3 +74,14 @@ def test_config_carrier_quantities():
     assert (c1.nprb, c1.rbg, c1.n_subbands, c1.subband_prbs[-1]) == (51, 4, 13, 3)
     assert (c0.nprb, c0.rbg) == (106, 8) and (c2.nprb, c2.rbg, c2.n_subbands) == (135, 8, 17)
     assert (c3.nprb, c3.rbg, c3.n_subbands) == (273, 16, 18)
+
+
+def test_bsr_level_table_matches_the_oracle():
+    """The MAC kernel's short-BSR level table (csrc/nr_bsr.cuh, TS 38.321 Table 6.1.3.1-1) equals the oracle's, which
+    the BSR fixtures pin to the reference (isaac_net/core/mac_ul.py:38-42)."""
+    import os
+    import re
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "isaac-net_b200", "csrc",
+                            "nr_bsr.cuh")).read()
+    body = re.search(r"kBsrLevels\[64\] = \{([^}]*)\}", src).group(1)
+    assert [int(x) for x in body.replace("\n", " ").split(",")] == list(O.BSR_LEVELS)

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
+from golden_io import BSR_CASES, CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -182,7 +182,7 @@ def test_oracle_aten_bitwise_policy_case(case):
 def test_bsr_fixtures_have_activity():
     """The SR / BSR pipeline fixtures exercise padded grants (tb_empty), the RLC tail residue and, on three cells,
     handovers."""
-    for case in ORACLE_ONLY_CASES:
+    for case in BSR_CASES:
         g = Golden(case)
         last = g.state(g.steps - 1)
         assert last["ctr.tb_empty"] > 0 and last["ctr.tb_new"] > 100, case
