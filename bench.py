@@ -187,10 +187,11 @@ def wl_id(wl):
     return int(wl.name[3])
 
 
-def shard_seed(seed, rank, cfg):
+def shard_seed(seed, rank, cfg, traffic_rng="generator"):
     """Seed of shard `rank` (isaac_net/core/sharded.py:95-103): the common seed when every draw is keyed by global env
-    id, else (seed + rank * 0x9E3779B97F4A7C15) mod 2^62 (the traffic models draw from one generator per engine)."""
-    if cfg.traffic:
+    id (no traffic models, or the counter-keyed traffic stream), else (seed + rank * 0x9E3779B97F4A7C15) mod 2^62 (the
+    traffic models draw from one generator per engine)."""
+    if cfg.traffic and traffic_rng == "generator":
         return (int(seed) + rank * 0x9E3779B97F4A7C15) % 2 ** 62
     return int(seed)
 
@@ -450,6 +451,9 @@ def main():
     ap.add_argument("--cpu-envs", type=int, default=0, help="envs of the CPU sample (0: see cpu_envs)")
     ap.add_argument("--cpu-steps", type=int, default=2, help="steps per window of the CPU sample (3 windows)")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--traffic-rng", default="generator", choices=("generator", "counter"),
+                    help="the traffic models' stream: the reference's torch.Generator (default) or the opt-in "
+                         "counter-keyed one, whose arrivals do not depend on the split over GPUs")
     ap.add_argument("--envs", type=int, default=0, help="envs per GPU (0: set by --scaling); a smaller batch of the "
                                                        "same workload, for profiling captures")
     ap.add_argument("--scaling", default="strong", choices=("weak", "strong"),
@@ -471,7 +475,8 @@ def main():
     cfg = wl.config()
     R = wl.R
     E = a.envs or shard_envs(wl, world, a.scaling)
-    eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg))
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=shard_seed(wl.seed, rank, cfg, a.traffic_rng),
+                         traffic_rng=a.traffic_rng)
     eng.set_env_offset(rank * E)              # global env ids, initial reset redone under them
     mot = presets.Motion(a.workload, E, R, seed=wl.seed + 7919 * rank, step_ms=cfg.control_step_ms)
     # a ring of NPOS consecutive pose frames of the random walk (at most 512 MB), cycled: the trajectory jumps back
@@ -555,7 +560,7 @@ def main():
     line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": t_ms / a.steps, "higher_is_better": True, "scaling": a.scaling,
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded poses and the engine's traffic models)",
-            "config": arm_config(wl, cfg, world, E),
+            "config": {**arm_config(wl, cfg, world, E), "traffic_rng": a.traffic_rng},
             "e2e": {"value": e2e, "unit": "env-steps/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": a.steps * launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",

@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 12
+#define INB_ABI_VERSION 13
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -324,6 +324,13 @@ typedef struct {
   float *nbytes;
   int64_t *slot, *tag, *prio;
   double *dline;
+  /* counter = 1: the opt-in counter-keyed stream instead of the torch.Generator one (no counterpart in the
+   * reference, whose arrivals depend on how the envs are split over engines): uniform d of a robot's step is
+   * ((h0 >> 5) 2^26 + (h1 >> 6)) 2^-53 with h0, h1 the counter-RNG element hashes 2r, 2r + 1 of stream d under the
+   * key (s0, env_id[e], episode[e], channel 0x54, calls[e,r]), so it depends on the global env id, not on the shard */
+  int32_t counter;
+  uint32_t s0;
+  const int64_t *env_id, *episode;   /* [E] */
 } InbTrafficArgs;
 int inb_traffic_step(const InbTrafficArgs *args, void *cuda_stream);
 

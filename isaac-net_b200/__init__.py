@@ -39,10 +39,13 @@ from .config import NRConfig  # noqa: E402
 from .traffic import Requests, TrafficModel  # noqa: E402
 
 
-def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, sizes=None, seed=None, strict=False):
-    """Build the B200 NR engine (level "L2") for E envs x R robots (isaac_net/core/engine.py:232-293 signature)."""
+def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, sizes=None, seed=None, strict=False,
+                traffic_rng="generator"):
+    """Build the B200 NR engine (level "L2") for E envs x R robots (isaac_net/core/engine.py:232-293 signature).
+    traffic_rng="counter" opts into the shard-invariant counter-keyed traffic stream (see NRB200Engine)."""
     from .engine import make_engine as _make
-    return _make(level, E, R, device, config, backend, sizes=sizes, seed=seed, strict=strict)
+    return _make(level, E, R, device, config, backend, sizes=sizes, seed=seed, strict=strict,
+                 traffic_rng=traffic_rng)
 
 
 def __getattr__(name):

@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 12
+ABI_VERSION = 13
 MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -122,7 +122,8 @@ TRAFFIC_OUT = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
 class InbTrafficArgs(ctypes.Structure):
     _fields_ = ([(n, i32) for n in ("E", "R", "M", "N", "n_src")] + [("seed", u64), ("off0", u64)]
                 + [(n, i64) for n in ("stride", "inc", "ndraws")] + [("step_ms", f64), ("inv_slot_ms", f64)]
-                + [("calls", P), ("src", InbTrafficSource * MAX_SRC)] + [(n, P) for n in TRAFFIC_OUT])
+                + [("calls", P), ("src", InbTrafficSource * MAX_SRC)] + [(n, P) for n in TRAFFIC_OUT]
+                + [("counter", i32), ("s0", u32), ("env_id", P), ("episode", P)])
 
 
 OBS_OFFS = ("off_mask", "off_delay", "off_aoi", "off_qlen", "off_qbytes", "off_sinr", "off_rsrp", "off_serv",

@@ -13,13 +13,20 @@
 //
 // Float64 arithmetic follows the reference op by op with round-to-nearest intrinsics: exponential draws are
 // (-log1p(-u)) * mean, slots are floor(max(t, 0) * (1 / slot_ms)) (torch's CUDA division by a python scalar).
+//
+// With InbTrafficArgs.counter the uniforms come instead from the opt-in counter-keyed stream (CounterU below): the
+// same models and the same draw indices d, each uniform a function of (seed key, global env id, episode, the robot's
+// step count, d, robot), so the arrivals of an env do not depend on which engine (shard) steps it.
 #include <cmath>
 #include <cstdint>
 #include <curand_kernel.h>
 
 #include "isaac_net_b200.h"
+#include "nr_common.cuh"
 
 namespace inb {
+
+constexpr uint32_t CH_TRAFFIC = 0x54u;   // counter-RNG channel of the counter-keyed traffic stream's step draws
 
 struct Philox {
   unsigned long long seed, base;  // base: offset of draw 0 of this step
@@ -37,8 +44,41 @@ struct Philox {
   }
   // _Source._expo: -log1p(-u) * mean_ms
   __device__ double expo(long long d, double mean) const { return __dmul_rn(-log1p(-u(d)), mean); }
+
+  // the draws of element li (robot r) in its n-th step
+  __device__ static Philox make(const InbTrafficArgs& A, long long li, long long n, int r) {
+    Philox p;
+    p.seed = A.seed;
+    p.base = A.off0 + (unsigned long long)(n * A.ndraws * A.inc);
+    p.inc = A.inc;
+    p.sub = (unsigned long long)(li % A.stride);
+    const long long q = li / A.stride;
+    p.call_off = (unsigned long long)(q >> 1) * 4ull;
+    p.comp = (int)(q & 1);
+    return p;
+  }
 };
 
+// The counter-keyed stream: uniform d = 53 bits from the element hashes 2r, 2r + 1 of stream d under the key
+// (s0, env id, episode, CH_TRAFFIC, step count); exact in float64, in [0, 1)
+struct CounterU {
+  uint32_t kenv, r2;
+  __device__ double u(long long d) const {
+    const uint32_t base = key_stream(kenv, (uint32_t)d);
+    const uint32_t h0 = elem(base, r2), h1 = elem(base, r2 + 1u);
+    return (double)(h0 >> 5) * 67108864.0 * 0x1p-53 + (double)(h1 >> 6) * 0x1p-53;
+  }
+  __device__ double expo(long long d, double mean) const { return __dmul_rn(-log1p(-u(d)), mean); }
+  __device__ static CounterU make(const InbTrafficArgs& A, long long li, long long n, int r) {
+    const long long e = li / A.R;
+    CounterU c;
+    c.kenv = key_env(A.s0, A.env_id[e], A.episode[e], CH_TRAFFIC, n);
+    c.r2 = 2u * (uint32_t)r;
+    return c;
+  }
+};
+
+template <class Rng>
 __global__ void __launch_bounds__(256) traffic_step_kernel(const InbTrafficArgs A) {
   const long long li = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const long long total = (long long)A.E * A.R;
@@ -49,14 +89,7 @@ __global__ void __launch_bounds__(256) traffic_step_kernel(const InbTrafficArgs 
 
   const long long n = A.calls[li];
   A.calls[li] = n + 1;
-  Philox rng;
-  rng.seed = A.seed;
-  rng.base = A.off0 + (unsigned long long)(n * A.ndraws * A.inc);
-  rng.inc = A.inc;
-  rng.sub = (unsigned long long)(li % A.stride);
-  const long long q = li / A.stride;
-  rng.call_off = (unsigned long long)(q >> 1) * 4ull;
-  rng.comp = (int)(q & 1);
+  const Rng rng = Rng::make(A, li, n, r);
 
   // columns of this robot before sorting: emission time, validity, bytes, model
   double t_c[INB_MAX_M];
@@ -170,7 +203,8 @@ extern "C" int inb_traffic_step(const InbTrafficArgs* args, void* stream) {
   const InbTrafficArgs& A = *args;
   if (A.E <= 0 || A.R <= 0 || A.M <= 0 || A.M > INB_MAX_M || A.n_src <= 0 || A.n_src > INB_MAX_SRC || A.N <= 0)
     return -2;
-  if (A.stride <= 0 || A.inc <= 0 || A.calls == nullptr) return -3;
+  if (A.calls == nullptr) return -3;
+  if (A.counter ? (A.env_id == nullptr || A.episode == nullptr) : (A.stride <= 0 || A.inc <= 0)) return -3;
   int cols = 0;
   for (int k = 0; k < A.n_src; ++k) {
     const InbTrafficSource& S = A.src[k];
@@ -182,6 +216,9 @@ extern "C" int inb_traffic_step(const InbTrafficArgs* args, void* stream) {
   const long long total = (long long)A.E * A.R;
   const int block = 256;
   const long long grid = (total + block - 1) / block;
-  inb::traffic_step_kernel<<<(unsigned)grid, block, 0, (cudaStream_t)stream>>>(A);
+  if (A.counter)
+    inb::traffic_step_kernel<inb::CounterU><<<(unsigned)grid, block, 0, (cudaStream_t)stream>>>(A);
+  else
+    inb::traffic_step_kernel<inb::Philox><<<(unsigned)grid, block, 0, (cudaStream_t)stream>>>(A);
   return cudaGetLastError() == cudaSuccess ? 0 : -100;
 }

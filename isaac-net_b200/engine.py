@@ -26,7 +26,7 @@ from .config import NRConfig
 from .phy import PhyTables
 from . import invariants as inv
 from .radio_map import cdf_table, load_radio_map
-from .traffic import DeviceTrafficGen, Requests, TrafficGen, generates
+from .traffic import CounterDraws, DeviceTrafficGen, Requests, TrafficGen, generates
 
 # counter-RNG constants (isaac_net/core/proto/rng.py:33-38, nr_rng.py:34, radio.py:53-56)
 M32 = 0xFFFFFFFF
@@ -82,7 +82,8 @@ def _ptr(t):
     return ctypes.c_void_p(t.data_ptr()) if t is not None else None
 
 
-def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, sizes=None, seed=None, strict=False):
+def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, sizes=None, seed=None, strict=False,
+                traffic_rng="generator"):
     """The B200 NR engine for E envs x R robots (isaac_net/core/engine.py:232-293)."""
     if level != "L2":
         raise ValueError(f"the B200 backend implements level 'L2' (the NR engine), not {level!r}")
@@ -93,7 +94,7 @@ def make_engine(level, E, R, device="cuda", config=None, backend="b200", *, size
         cfg = cfg.with_(msg_sizes=tuple(float(s) for s in sizes))
     if seed is None:
         seed = cfg.seed
-    return NRB200Engine(E, R, device, cfg, seed=seed)
+    return NRB200Engine(E, R, device, cfg, seed=seed, traffic_rng=traffic_rng)
 
 
 class NRB200Engine:
@@ -102,7 +103,14 @@ class NRB200Engine:
     level = "L2"
     backend = "b200"
 
-    def __init__(self, E, R, device, cfg: NRConfig, seed=None, graphs=True):
+    def __init__(self, E, R, device, cfg: NRConfig, seed=None, graphs=True, traffic_rng="generator"):
+        """traffic_rng: "generator" (the reference's arrival stream: the traffic models draw from a torch.Generator
+        seeded per engine, so the arrivals depend on how a batch is split over engines) or "counter" (an opt-in
+        stream with no counterpart in the reference: every uniform is keyed by the seed, the global env id, the
+        episode and the step, so an env's arrivals are the same in any shard, traffic.CounterDraws)."""
+        if traffic_rng not in ("generator", "counter"):
+            raise ValueError(f"traffic_rng must be 'generator' or 'counter', not {traffic_rng!r}")
+        self.traffic_rng = traffic_rng
         no = cfg.refusals()
         if no:
             raise B200Unsupported("the B200 engine does not implement " + "; ".join(f"{f}: {w}" for f, w in no))
@@ -143,7 +151,8 @@ class NRB200Engine:
         self._extras = False
         if generates(cfg.traffic):
             tseed = (int(self.seed) * 6364136223846793005 + 1442695040888963407) % 2 ** 62
-            self.traffic = TrafficGen(cfg.traffic, E, R, dev, cfg.control_step_ms, self.N, seed=tseed)
+            cd = CounterDraws(self.s0, self.env_id, self.episode, R) if traffic_rng == "counter" else None
+            self.traffic = TrafficGen(cfg.traffic, E, R, dev, cfg.control_step_ms, self.N, seed=tseed, counter=cd)
             self._extras = True
         # the arrivals of periodic / video / bursty models come from one kernel that replays the torch.Generator
         # stream; event models (host triggers) keep the torch path
@@ -1048,6 +1057,8 @@ class NRB200Engine:
                 sd[f"traffic.src{i}.deferred"] = src.deferred.clone()
             if self.dtraffic is not None:
                 sd["traffic.calls"] = self.dtraffic.calls.clone()
+            elif tg.counter is not None:     # host steps of the counter stream: its key
+                sd["traffic.calls"] = tg.calls.clone()
         return sd
 
     def load_state_dict(self, sd, strict=True):
@@ -1113,6 +1124,8 @@ class NRB200Engine:
                 cp(src.deferred, f"traffic.src{i}.deferred")
             if self.dtraffic is not None:
                 cp(self.dtraffic.calls, "traffic.calls")
+            elif tg.counter is not None:
+                cp(tg.calls, "traffic.calls")
 
     def save(self, path, extra=None):
         """state_dict() (plus `extra`) to a file (torch.save), as checkpoint.save(net, path, extra=...)."""

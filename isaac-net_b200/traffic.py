@@ -6,6 +6,12 @@ order and shapes, so an engine on the same device with the same seed sees the sa
 draws stay torch calls on purpose: the reference's arrival stream is defined by torch's generator (mt19937 on CPU,
 Philox on CUDA), and a re-implementation would change it.  Everything downstream of the arrivals (enqueue, the
 per-slot arrival gate, the MAC) runs in the B200 kernels.
+
+Opt-in (traffic_rng="counter", no counterpart in the reference): CounterDraws replaces both generators by a
+counter-keyed stream, the same models drawing the same number of uniforms in the same order, each uniform a hash of
+(seed key, global env id, episode, step count, draw index, robot).  The reference's arrivals depend on how the envs
+are split over engines (one generator per engine, isaac_net/core/sharded.py:21-25); these do not, so a batch split
+over GPUs sees the arrivals one engine over the whole batch would see.
 """
 from __future__ import annotations
 
@@ -16,6 +22,59 @@ from typing import Callable, Optional, Union
 import torch
 
 KINDS = ("periodic", "bursty", "video", "event", "policy")
+
+
+# ------------------------------------------------------------------ counter-keyed draws (opt-in)
+_M32, _C1, _C2, _GOLD = 0xFFFFFFFF, 0x21F0AAAD, 0x735A2D97, 0x9E3779B9
+CH_TRAFFIC, CH_TRAFFIC_RESET = 0x54, 0x55     # counter-RNG channels of this stream (step draws, reset draws)
+
+
+def _mix32(x):
+    """lowbias32 on int64 tensors holding 32-bit values (the counter RNG's mixer, proto/rng.py:42-48)."""
+    x = x ^ (x >> 16)
+    x = (x * _C1) & _M32
+    x = x ^ (x >> 15)
+    x = (x * _C2) & _M32
+    return x ^ (x >> 15)
+
+
+def _salt(v):
+    return (_mix32(v & _M32) + _GOLD) & _M32
+
+
+def _elem(base, i):
+    return _mix32(_mix32((base + i * _GOLD) & _M32) ^ base)
+
+
+class CounterDraws:
+    """The counter-keyed uniforms of traffic_rng="counter".  The key chain is the engine's counter RNG's
+    (proto/rng.py:164-185) under channels of its own: key = (s0, env id, episode, channel, counter), uniform d of
+    robot r = 53 bits of the element hashes 2r, 2r + 1 of stream d, ((h0 >> 5) 2^26 + (h1 >> 6)) 2^-53, exact in
+    float64.  Step draws use the robot's step count as the counter (CH_TRAFFIC), reset draws counter 0
+    (CH_TRAFFIC_RESET); env_id / episode are the engine's tensors, read at every call (updated in place by
+    set_env_offset and resets)."""
+
+    def __init__(self, s0, env_id, episode, R):
+        self.s0, self.env_id, self.episode = int(s0), env_id, episode
+        self.r2 = 2 * torch.arange(R, dtype=torch.long, device=env_id.device)
+        self.kenv, self.d = None, 0
+
+    def begin(self, channel, ctr):
+        """Start the draws of one step (ctr: [E,R] step counts) or one reset (ctr = 0)."""
+        env, ep = self.env_id[:, None], self.episode[:, None]
+        h = _mix32(self.s0 ^ _salt(env))
+        h = _mix32(h ^ _salt(ep))
+        h = _mix32(h ^ _salt(torch.full_like(h, channel)))
+        ctr = ctr if torch.is_tensor(ctr) else torch.full_like(h, int(ctr))
+        self.kenv = _mix32(h ^ _salt(ctr)).expand(-1, self.r2.numel())
+        self.d = 0
+
+    def next(self):
+        """The next uniform [E,R] (float64, in [0, 1))."""
+        base = _mix32(self.kenv ^ _salt(torch.full_like(self.kenv, self.d)))
+        self.d += 1
+        h0, h1 = _elem(base, self.r2), _elem(base, self.r2 + 1)
+        return (h0 >> 5).double() * 2.0 ** -27 + (h1 >> 6).double() * 2.0 ** -53
 
 
 @dataclass
@@ -151,9 +210,10 @@ class Arrivals:
 class _Source:
     """Per-robot state of one model [E,R]; draws from the engine's step / reset generators."""
 
-    def __init__(self, model, idx, E, R, dev, step_ms, gens):
+    def __init__(self, model, idx, E, R, dev, step_ms, gens, counter=None):
         self.m, self.E, self.R, self.dev, self.step_ms = model, E, R, dev, step_ms
-        self.gens = gens                      # [step generator, reset generator]; gens[2] selects the active one
+        self.gens = gens                      # [step generator, reset generator]
+        self.counter = counter                # CounterDraws (traffic_rng="counter") or None
         self.width = model.max_per_step(step_ms)
         self.tag = model.tag if model.tag is not None else idx + 1
         on = torch.zeros(R, dtype=torch.bool, device=dev)
@@ -187,6 +247,8 @@ class _Source:
         return min(loops, nb + 64)
 
     def _u(self):
+        if self.counter is not None:
+            return self.counter.next()
         return torch.rand(self.E, self.R, generator=self._gen, device=self.dev, dtype=torch.float64)
 
     def _expo(self, mean_ms):
@@ -302,8 +364,11 @@ class _Source:
 class TrafficGen:
     """All generating uplink models of a config for E envs x R robots; step() -> Arrivals [E,R,M]."""
 
-    def __init__(self, traffic, E, R, device, step_ms, slots_per_step, seed=None):
+    def __init__(self, traffic, E, R, device, step_ms, slots_per_step, seed=None, counter=None):
+        """counter: a CounterDraws for the opt-in counter-keyed stream (the generators are then unused)."""
         self.E, self.R, self.dev = E, R, torch.device(device)
+        self.counter = counter
+        self.calls = torch.zeros(E, R, dtype=torch.long, device=self.dev)   # steps generated (the counter stream's key)
         self.N = int(slots_per_step)
         self.step_ms, self.slot_ms = float(step_ms), float(step_ms) / self.N
         seed = 0 if seed is None else int(seed)
@@ -313,7 +378,7 @@ class TrafficGen:
         self.rgen.manual_seed((seed + 0x9E3779B97F4A7C15) % 2 ** 63)
         models = normalize_traffic(traffic) or ()
         gens = (self.gen, self.rgen)
-        self.sources = [_Source(m, i, E, R, self.dev, self.step_ms, gens)
+        self.sources = [_Source(m, i, E, R, self.dev, self.step_ms, gens, counter)
                         for i, m in enumerate(models) if m.generates]
         self.M = sum(s.width for s in self.sources)
         self.reset(None)
@@ -324,6 +389,8 @@ class TrafficGen:
 
     def reset(self, env_mask_e=None):
         m = torch.ones(self.E, dtype=torch.bool, device=self.dev) if env_mask_e is None else env_mask_e
+        if self.counter is not None:
+            self.counter.begin(CH_TRAFFIC_RESET, 0)
         for s in self.sources:
             s.reset(m)
         if env_mask_e is None:
@@ -333,6 +400,9 @@ class TrafficGen:
     def step(self, clock=None, triggers=None) -> Arrivals:
         E, R, d = self.E, self.R, self.dev
         cols = {k: [] for k in ("v", "b", "t", "tag", "prio", "dl", "det")}
+        if self.counter is not None:
+            self.counter.begin(CH_TRAFFIC, self.calls)
+        self.calls += 1
         for s in self.sources:
             v, b, t = s.step(clock, triggers)
             k = v.shape[-1]
@@ -385,6 +455,9 @@ class DeviceTrafficGen:
         a.E, a.R, a.M, a.N, a.n_src = E, R, M, tg.N, len(tg.sources)
         a.seed, a.off0 = tg.gen.initial_seed(), tg.gen.get_offset()
         a.stride, a.inc = stride, ((numel - 1) // (stride * 2) + 1) * 4
+        if tg.counter is not None:   # the counter-keyed stream: keys from the engine's env ids and episodes
+            a.counter, a.s0 = 1, tg.counter.s0
+            a.env_id, a.episode = tg.counter.env_id.data_ptr(), tg.counter.episode.data_ptr()
         a.step_ms, a.inv_slot_ms = tg.step_ms, 1.0 / tg.slot_ms
         self._keep = []
         col, nd = 0, 0
@@ -410,7 +483,9 @@ class DeviceTrafficGen:
                 nd += c.loops * (4 if c.off_ms > 0 else 3)
             col += s.width
         a.ndraws = nd
-        self.calls = torch.zeros(E, R, dtype=torch.long, device=d)
+        # steps generated: the torch stream's position (from construction on), or the counter stream's key (shared
+        # with the host TrafficGen, whose resets and host steps use the same count)
+        self.calls = tg.calls if tg.counter is not None else torch.zeros(E, R, dtype=torch.long, device=d)
         a.calls = self.calls.data_ptr()
         z = lambda dt: torch.zeros(E, R, M, dtype=dt, device=d)
         self.out = Arrivals(valid=z(torch.bool), nbytes=z(torch.float32), slot=z(torch.long), tag=z(torch.long),
@@ -427,5 +502,5 @@ class DeviceTrafficGen:
         return self.out
 
 
-__all__ = ["Requests", "TrafficModel", "TrafficGen", "DeviceTrafficGen", "Arrivals", "normalize_traffic",
-           "generates"]
+__all__ = ["Requests", "TrafficModel", "TrafficGen", "DeviceTrafficGen", "CounterDraws", "Arrivals",
+           "normalize_traffic", "generates"]

@@ -101,3 +101,66 @@ def test_engine_uses_the_traffic_kernel_and_graph_replay_matches():
         for k in x:
             assert torch.equal(x[k].nan_to_num(nan=7.0), y[k].nan_to_num(nan=7.0)) if x[k].is_floating_point() \
                 else torch.equal(x[k], y[k]), (s, k)
+
+
+@pytest.mark.parametrize("mix,E,R,steps", [("cfg2", 256, 32, 40), ("mixed", 37, 24, 50)])
+def test_counter_stream_kernel_equals_host(mix, E, R, steps):
+    """traffic_rng="counter": the kernel's counter-keyed uniforms and the host TrafficGen's (CounterDraws, torch
+    integer ops) give bitwise the same arrivals and model state, partial resets included (episodes advanced as an
+    engine advances them)."""
+    dev = torch.device("cuda:0")
+    env = torch.arange(E, dtype=torch.long, device=dev) + 1000
+    ep_a = torch.zeros(E, dtype=torch.long, device=dev)
+    ep_b = ep_a.clone()
+    a = tr.TrafficGen(MIXES[mix], E, R, dev, 5.0, 10, seed=3, counter=tr.CounterDraws(77, env, ep_a, R))
+    b = tr.TrafficGen(MIXES[mix], E, R, dev, 5.0, 10, seed=3, counter=tr.CounterDraws(77, env, ep_b, R))
+    d = tr.DeviceTrafficGen(b, nat.lib())
+    for s in range(steps):
+        if s == steps // 2:
+            m = torch.zeros(E, dtype=torch.bool, device=dev)
+            m[::3] = True
+            a.reset(m)
+            b.reset(m)
+            ep_a += m.long()
+            ep_b += m.long()
+        _check(a, b, a.step(), d.step(), s)
+
+
+@pytest.mark.parametrize("wl_i", (1, 2))
+def test_counter_stream_two_shards_equal_one_engine(wl_i):
+    """Engines with traffic_rng="counter": one engine over 8 envs and two shards of 4 (the second keyed by global env
+    ids 4..7 through set_env_offset, the same seed) give bitwise the same step outputs, a partial reset included;
+    with the reference's generator stream the shards' arrivals differ."""
+    from isaac_net_b200.presets import Motion, workload
+    wl = workload(wl_i)
+    cfg = wl.config()
+    E, R, dev = 8, wl.R, torch.device("cuda:0")
+    full = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed, traffic_rng="counter")
+    sh = [ib.make_engine("L2", E // 2, R, dev, cfg, seed=wl.seed, traffic_rng="counter") for _ in range(2)]
+    sh[1].set_env_offset(E // 2)
+    mo = Motion(wl_i, E, R, seed=9, step_ms=cfg.control_step_ms)
+    delivered = 0
+    for s in range(10):
+        if s == 5:
+            full.reset([1, 6])
+            sh[0].reset([1])
+            sh[1].reset([2])
+        pos = mo.current().to(dev)
+        o = full.step(None, pos)
+        parts = [x.step(None, pos[i * (E // 2):(i + 1) * (E // 2)]) for i, x in enumerate(sh)]
+        for k, v in o.items():
+            if not torch.is_tensor(v) or v.dim() == 0:
+                continue
+            w = torch.cat([p[k] for p in parts])
+            same = torch.equal(v.nan_to_num(nan=7.0), w.nan_to_num(nan=7.0)) if v.is_floating_point() \
+                else torch.equal(v, w)
+            assert same, (s, k)
+        delivered += int(o["delivered"].sum())
+        mo.advance()
+    assert delivered > 0
+    # the reference's stream: the second shard's arrivals are not the whole batch's rows 4..7
+    gf = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
+    gs = ib.make_engine("L2", E // 2, R, dev, cfg, seed=wl.seed)
+    gs.set_env_offset(E // 2)
+    x, y = gf.dtraffic.step(), gs.dtraffic.step()
+    assert not (torch.equal(x.valid[E // 2:], y.valid) and torch.equal(x.slot[E // 2:], y.slot))
