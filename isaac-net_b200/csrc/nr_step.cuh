@@ -123,9 +123,11 @@ struct Grp {
   // Per cell: the maximum of `key` over the group's lanes of cell c (c < C <= NC) with the lowest lane holding it
   // (mx, return value), and whether a lane of cell c has `flag` (anyf); the lanes of cell c must have keys > 0.
   // As argmax_u32 / any of each cell, but with GW > 32 one block barrier serves every cell and both results.
+  // anyc (optional, GW > 32): whether any cell of the block has a lane with a non-negative key (a candidate of the
+  // allocation rounds), read from the same shared-memory partials
   template <int NC>
   __device__ static int argmax_cell(uint32_t key, bool flag, int c, int C, uint32_t& mx, bool& anyf, SmemGroup* sm,
-                                    int& par) {
+                                    int& par, bool* anyc = nullptr) {
     if constexpr (GW <= 32) {
       int w = 0;
 #pragma unroll
@@ -160,10 +162,27 @@ struct Grp {
         b = sm->redc[par][c][w] > b ? sm->redc[par][c][w] : b;
         f |= sm->redf[par][c][w];
       }
+      if (anyc != nullptr) {
+        bool a = false;
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc)
+          for (int w = 0; w < GW / 32; ++w)
+            a = a || (cc < C && fkey_inv((uint32_t)(sm->redc[par][cc][w] >> 32)) >= 0.0f);
+        *anyc = a;
+      }
       par ^= 1;
       mx = (uint32_t)(b >> 32);
       anyf = f != 0u;
       return 255 - (int)(b & 0xFFu);
+    }
+  }
+  // whether a group (cell) of the warp (GW <= 32: one ballot of each lane's own result `own`) or of the block
+  // (GW > 32: the block-wide value `blk` an argmax already read from shared memory) has a candidate
+  __device__ static bool any_candidate(bool own, bool blk) {
+    if constexpr (GW > 32) {
+      return blk;
+    } else {
+      return __ballot_sync(0xFFFFFFFFu, own) != 0u;
     }
   }
   // true on every lane of the warp (GW <= 32) or block (GW > 32) when any lane there has v; a block barrier for
@@ -1005,16 +1024,18 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           }
           if (any_wr && !wr) mkey = -1.0f;
         }
-        bool oh;
+        bool oh, more;
         if constexpr (MC) {
           uint32_t mx;
-          bool unused;
-          const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), false, serv, C, mx, unused, sm, par);
+          bool unused, anyc = true;
+          const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), false, serv, C, mx, unused, sm, par, &anyc);
           oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+          more = Grp<GW>::any_candidate(fkey_inv(mx) >= 0.0f, anyc);
         } else {
           uint32_t mx;
           const int w = Grp<GW>::argmax_u32(fkey(mkey), mx, sm, par);
           oh = (w == r) && (fkey_inv(mx) >= 0.0f);
+          more = Grp<GW>::any_candidate(fkey_inv(mx) >= 0.0f, fkey_inv(mx) >= 0.0f);
         }
         if (oh) {
           won |= 1u << s;
@@ -1022,6 +1043,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           if (PFR) got = fa(got, RATE(s));
           if (!has_rx) left = fs(left, RATE(s));
         }
+        // `want` does not depend on s and only ever turns off: once no robot of the warp (block) is a candidate,
+        // no later round gives an RBG, so every lane leaves the rounds together
+        if (!more) break;
       }
       if (!lex) {
         // retransmissions that won fewer RBGs than their TB needs release them to the new-data robots (mac.py:353-379)
@@ -1035,15 +1059,18 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float mkey = want ? AMET(s) : -1.0f;
           uint32_t mx;
           bool av;
+          bool anyc = true;
           const int w = Grp<GW>::template argmax_cell<NC>(fkey(mkey), ((rel_rs >> s) & 1u) != 0u, serv, C, mx, av, sm,
-                                                          par);
+                                                          par, &anyc);
           const bool oh = (w == r) && (fkey_inv(mx) >= 0.0f) && av;
+          const bool more = Grp<GW>::any_candidate(fkey_inv(mx) >= 0.0f, anyc);
           if (oh) {
             won |= 1u << s;
             cnt += 1;
             if (PFR) got = fa(got, RATE(s));
             left = fs(left, RATE(s));
           }
+          if (!more) break;   // as in the rounds above: no candidate now, none later
         }
       }
     } else {
