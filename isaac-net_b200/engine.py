@@ -1127,6 +1127,20 @@ class NRB200Engine:
             elif tg.counter is not None:
                 cp(tg.calls, "traffic.calls")
 
+    def reference_checkpoint(self):
+        """This engine's state under the keys of the reference engine's state_dict() (isaac_net/core/checkpoint.py:
+        MAC, queue, fading, clocks, RNG counters, association, radio fields, traffic-model state, counters; the
+        mapping is in isaac-net_b200/checkpoint.py), CPU tensors."""
+        from . import checkpoint
+        return checkpoint.save(self)
+
+    def load_reference_checkpoint(self, sd, strict=False):
+        """Continue from a checkpoint the reference engine wrote (its state_dict(), a flat dict of tensors and host
+        values): the state is copied in place; returns the keys not used (constants, scratch and generator states
+        of the reference's object graph).  strict: raise when a key naming state could not be placed."""
+        from . import checkpoint
+        return checkpoint.load(self, sd, strict=strict)
+
     def save(self, path, extra=None):
         """state_dict() (plus `extra`) to a file (torch.save), as checkpoint.save(net, path, extra=...)."""
         torch.save({"format": 1, "state": self.state_dict(), "extra": extra}, path)

@@ -261,18 +261,81 @@ def run_policy_case(i, E, R, steps, resets, every, over, legacy_step):
     return rec
 
 
+# Checkpoint cases: the reference's own engine.state_dict() (isaac_net/core/checkpoint.py, the flat dict of its object
+# graph) after `warm` control steps, then `n` more steps with their poses, arrivals, the path gains the reference
+# computed and its outputs, and the counters at the end.  The B200 engine loads the checkpoint
+# (NRB200Engine.load_reference_checkpoint) and continues from it.
+# name: (workload id, E, R, warm steps, steps after the checkpoint, config overrides)
+CKPT_CASES = {
+    "k2": (2, 3, 32, 9, 3, dict(ue_tx_dbm=-8.0)),
+    "k3": (3, 2, 64, 7, 3, {}),
+    "k5": (5, 2, 48, 6, 3, {}),
+}
+
+
+def run_ckpt_case(i, E, R, warm, n, over):
+    from isaac_net import make_engine as ref_make
+    presets = importlib.import_module("isaac-net_b200.presets")
+    wl = presets.workload(i)
+    cfg = ref_config(wl, **over)
+    eng = ref_make("L2", E, R, "cpu", cfg, strict=None, seed=wl.seed)
+    cap = []
+    tstep = eng.traffic.step
+
+    def grab(clock=None, triggers=None):
+        a = tstep(clock, triggers)
+        cap.append(a)
+        return a
+    eng.traffic.step = grab
+    mot = presets.Motion(i, E, R, seed=wl.seed, step_ms=cfg.control_step_ms)
+    for _ in range(warm):
+        eng.step(None, mot.advance())
+    rec = {"E": np.int64(E), "R": np.int64(R), "steps": np.int64(n), "workload": np.int64(i)}
+    for k, v in eng.state_dict().items():
+        if torch.is_tensor(v) and v.dtype != torch.uint8:
+            rec["ckpt/" + k] = v.detach().cpu().clone().numpy()
+        elif isinstance(v, (bool, int, float)) and not isinstance(v, bool):
+            rec["ckpt/" + k] = np.array(v)
+    for k, v in ref_state(eng).items():
+        rec["ckst/" + k] = v
+    pgs = []
+    rpg = eng.radio.pathgain_db
+
+    def grab_pg(pos, *a, **k):
+        pg = rpg(pos, *a, **k)
+        pgs.append(pg)
+        return pg
+    eng.radio.pathgain_db = grab_pg
+    for s in range(n):
+        pos = mot.advance()
+        out = eng.step(None, pos)
+        rec[f"s{s}/pos"] = pos.numpy()
+        rec[f"s{s}/pg"] = pgs[-1].detach().cpu().numpy()
+        for nm in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det"):
+            rec[f"s{s}/arr.{nm}"] = getattr(cap[-1], nm).numpy()
+        for k, v in out.items():
+            rec[f"s{s}/out.{k}"] = v.detach().cpu().clone().numpy()
+    for k, v in eng.net.ul.ctr.items():
+        rec["end/ctr." + k] = v.detach().cpu().numpy()
+    rec["end/ntx_hist"] = eng.net.ul.ntx_hist.cpu().numpy()
+    rec["overrides"] = np.array(repr(over))
+    return rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF"),
                     help="source tree of the reference (isaac-net); default $ISAAC_NET_REF, else it must be importable")
-    ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES)))
+    ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES) + list(CKPT_CASES)))
     a = ap.parse_args()
     if a.ref:
         sys.path.insert(0, a.ref)
     sys.path.insert(0, ROOT)
     torch.set_num_threads(8)
     for c in a.cases.split(","):
-        if c in POLICY_CASES:
+        if c in CKPT_CASES:
+            rec = run_ckpt_case(*CKPT_CASES[c])
+        elif c in POLICY_CASES:
             rec = run_policy_case(*POLICY_CASES[c])
             rec["overrides"] = np.array(repr(POLICY_CASES[c][6]))
         else:

@@ -65,3 +65,51 @@ def test_refusals():
     with pytest.raises(KeyError):
         ib.make_engine("L2", 8, 16, dev, cfg, seed=0).load_state_dict(bad)
     ib.make_engine("L2", 8, 16, dev, cfg, seed=0).load_state_dict(bad, strict=False)
+
+
+class _Arr:
+    def __init__(self, d, dev):
+        for k, v in d.items():
+            setattr(self, k, torch.as_tensor(v).to(dev))
+
+
+@pytest.mark.parametrize("case", ("k2", "k3", "k5"))
+def test_continue_from_a_reference_checkpoint(case):
+    """The reference engine's own state_dict() (isaac_net/core/checkpoint.py format; fixtures cfgk*.npz) loaded into
+    the B200 engine: every state key is placed (strict), the engine written back under the reference's keys
+    reproduces the loaded values, and the following steps (the reference's arrivals and path gains fed in) give the
+    reference's outputs: integers bitwise, floats within 1e-5 relative / 1e-3 absolute; the counters end at the
+    reference's totals."""
+    import ast
+    import numpy as np
+    from golden_io import GOLDEN
+    d = np.load(f"{GOLDEN}/cfg{case}.npz")
+    wl = presets.workload(int(d["workload"]))
+    cfg = wl.config(**ast.literal_eval(str(d["overrides"])))
+    E, R, n = int(d["E"]), int(d["R"]), int(d["steps"])
+    dev = torch.device("cuda:0")
+    eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
+    ckpt = {k[5:]: torch.as_tensor(d[k]) if d[k].ndim else d[k].item() for k in d.files if k.startswith("ckpt/")}
+    eng.load_reference_checkpoint(ckpt, strict=True)
+    back = eng.reference_checkpoint()
+    for k, v in back.items():
+        if k in ckpt and not k.startswith("net.ul.ctr[") and k != "net.ul.ntx_hist":
+            want = torch.as_tensor(ckpt[k])
+            got = torch.as_tensor(v).to(want.dtype)
+            assert got.shape == want.shape and _same(got, want), k
+    for s in range(n):
+        pg = torch.as_tensor(d[f"s{s}/pg"])
+        pg = pg[..., 0] if eng.C == 1 else pg
+        arr = {m: d[f"s{s}/arr.{m}"] for m in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det")}
+        out = eng.step(None, None, _pathgain=pg.to(dev), _arrivals=_Arr(arr, dev))
+        for k in [x[len(f"s{s}/out."):] for x in d.files if x.startswith(f"s{s}/out.")]:
+            ref = d[f"s{s}/out.{k}"]
+            got = out[k].cpu().numpy()
+            if ref.dtype.kind == "f":
+                assert np.allclose(got.astype(np.float64), ref.astype(np.float64), rtol=1e-5, atol=1e-3,
+                                   equal_nan=True), (s, k)
+            else:
+                assert np.array_equal(got, ref), (s, k)
+    c = eng.counters()["ul"]
+    for k in ("tb_new", "tb_retx", "tb_ok", "tb_fail", "exhaust", "bytes_ok", "bytes_new", "prb_used", "prb_avail"):
+        assert c[k] == float(d[f"end/ctr.{k}"]), k
