@@ -8,6 +8,10 @@ cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g16_bsr(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g32_bsr(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g128_bsr(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_radio(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
@@ -68,14 +72,15 @@ int launch_all(const InbStepArgs& args, cudaStream_t s) {
     if (err != cudaSuccess) return -100 - (int)err;
   }
   if (!mac) return 0;
+  const bool b = p.bsr_on != 0;
   if (p.R <= 16)
-    err = launch_step_g16(a, s);
+    err = b ? launch_step_g16_bsr(a, s) : launch_step_g16(a, s);
   else if (p.R <= 32)
-    err = launch_step_g32(a, s);
+    err = b ? launch_step_g32_bsr(a, s) : launch_step_g32(a, s);
   else if (p.R <= 64)
-    err = launch_step_g64(a, s);
+    err = b ? launch_step_g64_bsr(a, s) : launch_step_g64(a, s);
   else
-    err = launch_step_g128(a, s);
+    err = b ? launch_step_g128_bsr(a, s) : launch_step_g128(a, s);
   if (err == cudaSuccess) err = launch_finish(a, s);
   return err == cudaSuccess ? 0 : -100 - (int)err;
 }

@@ -397,8 +397,9 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 // schedulers' per-RBG rounds are left out of it, and it out of theirs, which keeps each instance's code smaller); 2 is
 // the PF instance with pf_update = "rbg" (the per-RBG metric over the bytes granted so far); 0 is every other case.
 // NCT: the number of cells; NCT > 1 (MC) adds the A3 association and handover, per-cell schedulers, UL power control
-// and interference
-template <int GW, int NCT, int SV>
+// and interference.  BSR: the SR / BSR grant pipeline (p.bsr_on) replaces the lumped SR grant; compiled only into the
+// instances that run it, so the other instances carry none of its code.
+template <int GW, int NCT, int SV, bool BSR>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr bool MC = NCT > 1;   // several cells
   constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
@@ -703,7 +704,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     csi_src = -2;
     sr_t = -1;
     bsr = enq - sent;
-    if (p.bsr_on) bsr_handover(st, p, er, enq, sent);
+    if constexpr (BSR) bsr_handover(st, p, er, enq, sent);
   };
 
 
@@ -728,8 +729,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     // ---- SR (UlMac.sr_step, mac_ul.py:66-71; the BSR pipeline's, mac_ul.py:280-287)
     if (srf && act) {
-      if (p.bsr_on) bsr_sr_step(st, er, enq, sent, g, sr_t);
-      else if ((enq - sent > 0) && bsr <= 0 && sr_t < 0) sr_t = g;
+      if constexpr (BSR) bsr_sr_step(st, er, enq, sent, g, sr_t);
+      if (!BSR && (enq - sent > 0) && bsr <= 0 && sr_t < 0) sr_t = g;
     }
     if (!uls) continue;
 
@@ -739,7 +740,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const long long g_csi = (long long)u * plane, g_gain = g_csi + plane;
     // lumped SR grant (mac_ul.py:140-147), or the BSR pipeline's bootstrap grant and matured reports
     long long need_bsr = 0;
-    if (p.bsr_on) {
+    if constexpr (BSR) {
       if (act) need_bsr = bsr_pre_slot(st, p, er, enq, g, sr_t);
     } else if (sr_t >= 0 && g - sr_t >= p.sr_delay) {
       bsr = bsr < 1 ? 1 : bsr;
@@ -760,7 +761,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     const bool any_free = p_new >= 0;
     if (p_new < 0) p_new = 0;
-    const long long need = p.bsr_on ? need_bsr : (bsr < unsent ? bsr : unsent);
+    const long long need = BSR ? need_bsr : (bsr < unsent ? bsr : unsent);
     bool new_el = act && any_free && need > 0 && !has_rx;
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
@@ -1282,7 +1283,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     long long cap_b = tbs_new / 8 - p.tb_oh;
     cap_b = cap_b < 1 ? 1 : cap_b;
-    const long long byt_new = (p.bsr_on && tx_new) ? bsr_tb_payload(st, p, er, enq, sent, cap_b, g)
+    const long long byt_new = (BSR && tx_new) ? bsr_tb_payload(st, p, er, enq, sent, cap_b, g)
                                                    : (cap_b < unsent ? cap_b : unsent);
     // ---- bind the TB to its HARQ process (mac.py:406-423)
     const int p_tx = tx_rx ? rx_p : p_new;
@@ -1447,7 +1448,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       const float up = fm(p.olla_up, ok ? 1.0f : 0.0f), dn = fm(p.olla_dn, fail ? 1.0f : 0.0f);
       olla = clampf_t(fs(fa(olla, up), dn), -10.0f, 10.0f);
     }
-    if (p.bsr_on) {
+    if constexpr (BSR) {
       if (act) bsr_post_slot(st, p, er, enq, sent, g, tx, tx_new, tbs_new);
     } else if (tx) {
       bsr = enq - sent;

@@ -2,5 +2,5 @@
 // parallel).
 #include "nr_step_launch.cuh"
 namespace inb {
-cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<128>(a, stream); }
+cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<128, false>(a, stream); }
 }  // namespace inb

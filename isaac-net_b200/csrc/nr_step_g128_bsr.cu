@@ -1,0 +1,6 @@
+// Instantiation of the fused step kernel for groups of 128 lanes with the SR / BSR grant pipeline (its own translation
+// unit, compiled in parallel with the others).
+#include "nr_step_launch.cuh"
+namespace inb {
+cudaError_t launch_step_g128_bsr(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<128, true>(a, stream); }
+}  // namespace inb

@@ -1,0 +1,6 @@
+// Instantiation of the fused step kernel for groups of 32 lanes with the SR / BSR grant pipeline (its own translation
+// unit, compiled in parallel with the others).
+#include "nr_step_launch.cuh"
+namespace inb {
+cudaError_t launch_step_g32_bsr(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<32, true>(a, stream); }
+}  // namespace inb

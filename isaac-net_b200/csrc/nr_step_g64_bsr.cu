@@ -1,0 +1,6 @@
+// Instantiation of the fused step kernel for groups of 64 lanes with the SR / BSR grant pipeline (its own translation
+// unit, compiled in parallel with the others).
+#include "nr_step_launch.cuh"
+namespace inb {
+cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<64, true>(a, stream); }
+}  // namespace inb
