@@ -48,6 +48,9 @@ class NRConfig:
     dl_ctrl_symbols: int = 1
     ul_data_symbols: int = 12
     ul_mini_slot_symbols: int | None = None
+    mini_slot_dl: bool = False
+    dl_n_prb: int | None = None
+    dl_bandwidth_mhz: int | None = None
     dmrs_re_per_prb: int = 12
     overhead_re_per_prb: int = 0
     # MAC timing (slots)
@@ -74,6 +77,9 @@ class NRConfig:
     tbs_mode: str = "38214"
     bler_target: float = 0.1
     ul_mcs_max: int | None = None
+    dl_mcs_max: int | None = None
+    cqi_table: str = "mcs"               # DL CQI quantization: the MCS grid ("mcs") or TS 38.214's 4-bit CQI ("38214")
+    dl_snr_offset_db: float = 10.0       # SNR input: default DL per-PRB SNR = UL input SNR + offset
     olla: bool = True
     olla_up_db: float = 0.05
     scheduler: str = "pf"

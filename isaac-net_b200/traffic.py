@@ -186,13 +186,18 @@ def normalize_traffic(traffic):
     for m in traffic:
         if not isinstance(m, TrafficModel) or m.kind not in KINDS:
             raise TypeError(f"NRConfig.traffic takes TrafficModel objects, got {m!r}")
-        if m.direction != "ul":
-            raise ValueError("downlink traffic models need the downlink MAC, which the B200 engine does not build")
+        if m.direction not in ("ul", "dl"):
+            raise ValueError(f"traffic model {m.kind}: direction must be 'ul' or 'dl', not {m.direction!r}")
+        if m.direction == "dl" and (m.kind == "policy" or m.det):
+            raise ValueError(f"traffic model {m.kind}: a downlink model cannot be policy() or carry det=True "
+                             "(isaac_net/core/traffic.py:189-195)")
     return traffic or None
 
 
-def generates(traffic):
-    return traffic is not None and any(m.generates for m in traffic)
+def generates(traffic, direction="ul"):
+    """A model of `direction` ("ul" / "dl"; None = either) that generates messages (traffic.py:199-203)."""
+    return traffic is not None and any(m.generates and (direction is None or m.direction == direction)
+                                       for m in traffic)
 
 
 @dataclass
@@ -364,8 +369,9 @@ class _Source:
 class TrafficGen:
     """All generating uplink models of a config for E envs x R robots; step() -> Arrivals [E,R,M]."""
 
-    def __init__(self, traffic, E, R, device, step_ms, slots_per_step, seed=None, counter=None):
-        """counter: a CounterDraws for the opt-in counter-keyed stream (the generators are then unused)."""
+    def __init__(self, traffic, E, R, device, step_ms, slots_per_step, seed=None, counter=None, direction="ul"):
+        """counter: a CounterDraws for the opt-in counter-keyed stream (the generators are then unused); direction:
+        the models of that link only ("dl": the downlink's generator, isaac_net/core/traffic.py:373-391)."""
         self.E, self.R, self.dev = E, R, torch.device(device)
         self.counter = counter
         self.calls = torch.zeros(E, R, dtype=torch.long, device=self.dev)   # steps generated (the counter stream's key)
@@ -379,7 +385,7 @@ class TrafficGen:
         models = normalize_traffic(traffic) or ()
         gens = (self.gen, self.rgen)
         self.sources = [_Source(m, i, E, R, self.dev, self.step_ms, gens, counter)
-                        for i, m in enumerate(models) if m.generates]
+                        for i, m in enumerate(models) if m.generates and m.direction == direction]
         self.M = sum(s.width for s in self.sources)
         self.reset(None)
 

@@ -135,6 +135,16 @@ def ref_state(eng):
             for nm in ("sf_los", "sf_nlos", "los_field"):
                 fld = getattr(ch, nm)
                 st[f"radio.{nm}.k"], st[f"radio.{nm}.phi"] = fld.k, fld.phi
+    if net.dl is not None:     # the downlink MacLink and its queue
+        dl, dq = net.dl, net.dl.q
+        for n in ("sent", "floor", "olla", "avg", "bsr", "sr_t", "last_tx", "csi", "h_state", "h_lo", "h_hi",
+                  "h_ready", "h_ntx", "h_mcs", "h_tbs", "h_nsb", "h_comb"):
+            st["dl." + n] = getattr(dl, n)
+        for n in ("cap", "start", "end", "lost", "fin", "enq", "cls", "off", "tag", "prio", "dline"):
+            if hasattr(dq, n):
+                st["dq." + n] = getattr(dq, n)
+        for k, v in dl.ctr.items():
+            st["dctr." + k] = v
     if net.C > 1:
         for n in ("serv", "pending", "a3_cand", "a3_cnt", "ho_end", "n_ho"):
             st["assoc." + n] = getattr(net.assoc, n)
@@ -145,6 +155,27 @@ def ref_state(eng):
     st["ctr.ntx_hist"], st["ctr.rv_tx"], st["ctr.rv_fail"] = ul.ntx_hist, ul.rv_tx, ul.rv_fail
     st["ctr.prb_used_env"] = ul.prb_used_env
     return {k: v.detach().cpu().clone().numpy() for k, v in st.items()}
+
+
+# Downlink cases (dl=True, one cell): a TDD pattern with D, S and U slots, DL traffic models (direction="dl") beside
+# the uplink's, CQI reports, DL HARQ with the HARQ-ACK timing; the fixture adds the DL arrivals of each step.
+def dl_traffic(i, R):
+    """The DL traffic models of the DL cases next to workload i's uplink models."""
+    TM = importlib.import_module("isaac-net_b200.traffic").TrafficModel
+    ul = importlib.import_module("isaac-net_b200.presets").workload(i).fields["traffic"]
+    half = R // 2
+    return tuple(ul) + (TM.bursty(3000, rate_hz=120, burst_size=1, on_off=(1.0, 0.0), direction="dl",
+                                  deadline_ms=25.0),
+                        TM.periodic(400, period_ms=5.0, jitter_ms=1.0, direction="dl", tag=9).on(range(0, half)))
+
+
+DL_CASES = {
+    "d1": (1, 4, 16, 24, {11: [1]}, 1, dict(tdd_pattern="DDDSU", dl=True)),
+    "d2": (2, 3, 32, 20, {9: [2]}, 2, dict(tdd_pattern="DDSUU", dl=True)),
+    # weak links both ways: DL HARQ failures and exhaustion, purged and refused DL frames; the PF switches
+    "d2s": (2, 3, 32, 20, {9: [0]}, 1, dict(tdd_pattern="DDDSU", dl=True, ue_tx_dbm=-8.0, gnb_tx_dbm=12.0,
+                                             timeout_steps=6, frame_buffer=8, max_harq_tx=2, pf_update="rbg")),
+}
 
 
 def run_case(i, E, R, steps, resets, every, over, speed=1.0):
@@ -162,6 +193,15 @@ def run_case(i, E, R, steps, resets, every, over, speed=1.0):
         cap.append(a)
         return a
     eng.traffic.step = grab
+    cap_dl = []
+    if eng.traffic_dl is not None:
+        tstep_dl = eng.traffic_dl.step
+
+        def grab_dl(clock=None, triggers=None):
+            a = tstep_dl(clock, triggers)
+            cap_dl.append(a)
+            return a
+        eng.traffic_dl.step = grab_dl
     mot = presets.Motion(i, E, R, seed=wl.seed, step_ms=cfg.control_step_ms)
     mot.speed = mot.speed * speed
     rec = {"E": np.int64(E), "R": np.int64(R), "steps": np.int64(steps), "workload": np.int64(i)}
@@ -180,6 +220,9 @@ def run_case(i, E, R, steps, resets, every, over, speed=1.0):
         rec[f"s{s}/pos"] = pos.numpy()
         for n in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det"):
             rec[f"s{s}/arr.{n}"] = getattr(a, n).numpy()
+        if cap_dl:
+            for n in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det"):
+                rec[f"s{s}/dlarr.{n}"] = getattr(cap_dl[-1], n).numpy()
         for k, v in out.items():
             rec[f"s{s}/out.{k}"] = v.detach().cpu().clone().numpy()
         if s % every == 0 or s == steps - 1 or (s + 1) in resets:
@@ -326,7 +369,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("ISAAC_NET_REF"),
                     help="source tree of the reference (isaac-net); default $ISAAC_NET_REF, else it must be importable")
-    ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES) + list(CKPT_CASES)))
+    ap.add_argument("--cases", default=",".join([str(k) for k in CASES] + list(POLICY_CASES) + list(CKPT_CASES) +
+                                                 list(DL_CASES)))
     a = ap.parse_args()
     if a.ref:
         sys.path.insert(0, a.ref)
@@ -335,6 +379,12 @@ def main():
     for c in a.cases.split(","):
         if c in CKPT_CASES:
             rec = run_ckpt_case(*CKPT_CASES[c])
+        elif c in DL_CASES:
+            i, E, R, steps, resets, every, over = DL_CASES[c]
+            over = dict(over, traffic=dl_traffic(i, R))
+            rec = run_case(i, E, R, steps, resets, every, over)
+            rec["overrides"] = np.array(repr(DL_CASES[c][6]))
+            rec["dl_traffic"] = np.int64(1)
         elif c in POLICY_CASES:
             rec = run_policy_case(*POLICY_CASES[c])
             rec["overrides"] = np.array(repr(POLICY_CASES[c][6]))

@@ -9,6 +9,7 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t", "5", "5s", "1b", "2r", "3r", "2v", "3v", "1v", "2g", "3g")
 BSR_CASES = ("2g", "3g")   # the SR / BSR grant pipeline (ul_grant_model = "bsr") on one and three cells
 ORACLE_ONLY_CASES = ()     # every fixture runs on the kernel too
+DL_CASES = ("d1", "d2", "d2s")   # the downlink MAC with CQI and DL traffic models (TDD patterns with D, S, U slots)
 POLICY_CASES = ("1p",)   # policy submits + SNR input (tests/golden/make_golden.py POLICY_CASES)
 
 
@@ -25,7 +26,19 @@ class Golden:
         return importlib.import_module("isaac-net_b200.presets").workload(self.workload_id)
 
     def config(self):
-        return self.workload().config(**self.overrides)
+        over = dict(self.overrides)
+        if "dl_traffic" in self.d.files:     # the DL cases' traffic models (make_golden.dl_traffic)
+            import sys
+            sys.path.insert(0, GOLDEN)
+            from make_golden import dl_traffic
+            over["traffic"] = dl_traffic(self.workload_id, self.R)
+        return self.workload().config(**over)
+
+    def dl_arrivals(self, s):
+        """The DL traffic arrivals of step s (DL cases), else None."""
+        if f"s{s}/dlarr.valid" not in self.d.files:
+            return None
+        return {n: self.d[f"s{s}/dlarr.{n}"] for n in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det")}
 
     def pos(self, s):
         return self.d[f"s{s}/pos"]

@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import BSR_CASES, CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
+from golden_io import BSR_CASES, CASES, DL_CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -22,6 +22,11 @@ FLOAT_OUT = ("delay", "queue_bytes", "sinr_db", "arrival")
 
 def _arr(g, s, dev="cpu"):
     return {k: torch.as_tensor(v).to(dev) for k, v in g.arrivals(s).items()}
+
+
+def _dlarr(g, s, dev="cpu"):
+    a = g.dl_arrivals(s)
+    return None if a is None else {k: torch.as_tensor(v).to(dev) for k, v in a.items()}
 
 
 def _eq(a, b):
@@ -40,7 +45,7 @@ def _state_diff(o, ref):
     return bad
 
 
-@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES)
+@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES + DL_CASES)
 def test_oracle_aten_bitwise_free_running(case):
     g = Golden(case)
     wl = g.workload()
@@ -50,7 +55,7 @@ def test_oracle_aten_bitwise_free_running(case):
         ids = g.reset_ids(s)
         if ids:
             o.reset(ids)
-        out = o.step(torch.as_tensor(g.pos(s)), _arr(g, s))
+        out = o.step(torch.as_tensor(g.pos(s)), _arr(g, s), dl_arrivals=_dlarr(g, s))
         ref = g.outputs(s)
         assert set(ref) == set(out), (set(ref) ^ set(out))
         for k, v in ref.items():
