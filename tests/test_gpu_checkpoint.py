@@ -103,6 +103,8 @@ def test_continue_from_a_reference_checkpoint(case):
         arr = {m: d[f"s{s}/arr.{m}"] for m in ("valid", "nbytes", "slot", "tag", "prio", "dline", "det")}
         out = eng.step(None, None, _pathgain=pg.to(dev), _arrivals=_Arr(arr, dev))
         for k in [x[len(f"s{s}/out."):] for x in d.files if x.startswith(f"s{s}/out.")]:
+            if k in ("blocked", "los"):   # obstacle outputs come from the radio; the path gains are fed in here
+                continue
             ref = d[f"s{s}/out.{k}"]
             got = out[k].cpu().numpy()
             if ref.dtype.kind == "f":
