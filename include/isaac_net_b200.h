@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 13
+#define INB_ABI_VERSION 14
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -99,6 +99,9 @@ typedef struct {
   /* obstacle outputs of the serving link (NULL: not produced; only with blockage and poses through the radio) */
   uint8_t *blocked;                                        /* [E,R] a blockage region is on the direct path */
   uint8_t *los;                                            /* [E,R] LOS state (InbParams.los_const) */
+  /* downlink finish (InbStepArgs.dl): timed out or dropped this step, and generated by a DL traffic model (cls < 0),
+   * [E,R,F]; every output of a DL call may be NULL (not produced) */
+  uint8_t *lost_any, *generated;
 } InbOutputs;
 
 /* Traffic arrivals of this step [E,R,M] (TrafficGen.step, sorted by slot), or M = 0. */
@@ -174,6 +177,12 @@ typedef struct {
    * an SR until the bootstrap grant, its bytes, the report delay, the RLC timer; header bytes of a report, of the
    * gNB's estimate, and the RLC residue a buffer-draining TB leaves behind */
   int32_t bsr_on, sr_boot_slots, sr_boot_bytes, bsr_delay, rlc_tail_slots, bsr_hdr, bsr_est_hdr, rlc_tail_bytes;
+  /* downlink (dl = True, one cell; InbStepArgs.dl): the fading launch also writes the gain of every row that carries
+   * DL data or a CQI report, as gain row n_ul_rows + 1 + j (j = rows_dl[k][3], the row's index among those rows);
+   * per row: DL data symbols (0 = none), CQI report, HARQ-ACK slot + gnb_proc_slots relative to the step's first slot,
+   * DL gain-row index or -1 */
+  int32_t dl_on, n_ul_rows, n_dl_rows;
+  int32_t rows_dl[INB_MAX_ROWS][4];
 } InbParams;
 
 /* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes
@@ -208,7 +217,7 @@ typedef struct {
   uint8_t *blk;                 /* [E, R] out: bit c = a region is on the direct path to cell c */
 } InbRadio;
 
-typedef struct {
+typedef struct InbStepArgs_ {
   InbParams p;
   InbState s;
   InbOutputs o;
@@ -240,12 +249,20 @@ typedef struct {
                                    2 = fading, 4 = MAC and finish.  Radio and fading need no arrivals and not each
                                    other, so a caller may run them on two streams beside the step's traffic arrivals
                                    and the MAC phase after all of them. */
+  /* the downlink link of the step (p.dl_on; NULL = uplink only): a host-memory InbStepArgs for the DL MAC and finish
+   * launches, which run after the fading and before the uplink MAC (the uplink MAC advances rng_ctr): its p carries
+   * the DL MCS cap, the DL reference SINR constants (ul_ref0 = float32(gnb_tx_dbm - 10 log10(nprb)), noise_prb = the
+   * UE's noise per PRB), no PHR cap, TDMA, previous-PRB AMC or BSR; s the DL link's state (csi = the CQI estimate), o
+   * the DL outputs (newest, queue_len and the dl_* frame outputs; gen_accepted / gen_bytes = gen_dl_*), a the DL
+   * arrivals, ctr the DL counters; the rest as this struct (DlMac, isaac_net/core/mac_dl.py:1-49) */
+  const struct InbStepArgs_ *dl;
 } InbStepArgs;
 
 /* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.
  * With rm.on and pathgain_in NULL the radio launch evaluates the poses and the MAC reads rm.pg; a pathgain_in
  * skips it.  -11: a radio pointer or size is missing or out of range, or o.blocked is set without the launch.
- * -12: p.bsr_on without the InbState.bsr_* buffers (or a negative pipeline delay). */
+ * -12: p.bsr_on without the InbState.bsr_* buffers (or a negative pipeline delay).
+ * -13: p.dl_on with several cells, without InbStepArgs.dl, or with DL args / DL rows that do not fit the step. */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
 
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array

@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 13
+ABI_VERSION = 14
 MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -33,7 +33,7 @@ STATE_FIELDS = ("sent", "floor_", "bsr", "sr_t", "last_tx", "enq", "olla", "avg"
 BSR_DEPTH = 4          # INB_BSR_DEPTH
 OUT_FIELDS = ("delivered", "timed_out", "dropped", "deadline_miss", "cap", "cls", "arrival_slot", "tag", "priority",
               "bytes", "delay", "arrival", "newest", "queue_len", "gen_accepted", "gen_bytes", "queue_bytes",
-              "sinr_db", "pathgain", "det_env", "serving_cell", "blocked", "los")
+              "sinr_db", "pathgain", "det_env", "serving_cell", "blocked", "los", "lost_any", "generated")
 ARR_FIELDS = ("valid", "det", "nbytes", "slot", "tag", "prio", "dline")
 TAB_FIELDS = ("bler", "thr_ref", "se", "beta", "rate", "w", "lw", "lw10", "la_tbs", "la_i0", "la_wi", "la_ncb", "fk",
               "fphi", "gnb")
@@ -78,7 +78,8 @@ class InbParams(ctypes.Structure):
                 + [("los_const", i32), ("pf_rbg", i32), ("pf_freeze", i32), ("field_fma", i32), ("tdma", i32),
                    ("amc_prev", i32), ("lena_ctr", i32)]
                 + [(n, i32) for n in ("bsr_on", "sr_boot_slots", "sr_boot_bytes", "bsr_delay", "rlc_tail_slots",
-                                      "bsr_hdr", "bsr_est_hdr", "rlc_tail_bytes")])
+                                      "bsr_hdr", "bsr_est_hdr", "rlc_tail_bytes")]
+                + [(n, i32) for n in ("dl_on", "n_ul_rows", "n_dl_rows")] + [("rows_dl", (i32 * 4) * MAX_ROWS)])
 
 
 class InbRadio(ctypes.Structure):
@@ -95,7 +96,8 @@ class InbStepArgs(ctypes.Structure):
     _fields_ = [("p", InbParams), ("s", InbState), ("o", InbOutputs), ("a", InbArrivals), ("t", InbTables),
                 ("pos", P), ("pathgain_in", P), ("ul_ref_in", P), ("env_id", P), ("episode", P), ("rng_ctr", P),
                 ("epoch", P), ("last_hid", P), ("ctr", P), ("status", P), ("T_dev", P),
-                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P), ("rm", InbRadio), ("det_hid", P), ("phases", i32)]
+                ("trace", P), ("gain", P), ("gain_cap", i64), ("o_base", P), ("rm", InbRadio), ("det_hid", P), ("phases", i32),
+                ("dl", P)]
 
 
 class InbResetArgs(ctypes.Structure):

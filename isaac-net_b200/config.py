@@ -311,16 +311,28 @@ class NRConfig:
         a = self.cell_arena_m
         return [((j % cols + 0.5) * a / cols, (j // cols + 0.5) * a / rows) for j in range(n)]
 
+    def next_ul_capable(self, g):
+        """Smallest slot index >= g that is UL-capable (config.py:1070-1076)."""
+        for d in range(len(self.tdd_pattern)):
+            if self.ul_capable(g + d):
+                return g + d
+        raise ValueError("pattern has no UL-capable slot")
+
     def schedule(self, g0):
-        """Scheduled slots of the control step starting at slot g0: [(rel, ul data symbols, sr opportunity)], the
-        uplink rows of NRNet._schedule (isaac_net/core/nr_engine.py:506-523)."""
+        """Scheduled slots of the control step starting at slot g0, the rows of NRNet._schedule
+        (isaac_net/core/nr_engine.py:506-523): [(rel, DL data symbols, UL data symbols, SR opportunity, CQI report,
+        HARQ-ACK slot relative to g0)]."""
         out = []
         for rel in range(self.slots_per_step):
             g = g0 + rel
-            uls = self.slot_symbols(g)[1] if self.ul else 0
+            dls, uls = self.slot_symbols(g)
+            dls = dls if self.dl else 0
+            uls = uls if self.ul else 0
             sr = self.first_ul_in_window(g, self.sr_period_slots) and self.ul
-            if uls or sr:
-                out.append((rel, uls, bool(sr)))
+            cqi = self.first_ul_in_window(g, self.cqi_period_slots) and self.dl
+            if dls or uls or cqi or sr:
+                ack = self.next_ul_capable(g + self.k1) - g0 if self.dl else 0
+                out.append((rel, dls, uls, bool(sr), bool(cqi), ack))
         return out
 
     def schedule_period(self):
@@ -349,8 +361,10 @@ class NRConfig:
         d = NRConfig()
         # the SR/BSR pipeline fields (sr_boot_*, bsr_*, rlc_tail_*) are read only under ul_grant_model="bsr"
         # (reference config.py:119, 307), so a lumped config keeps whatever values they hold
-        chk = [("dl", "the downlink MAC is not built (uplink control-step path only)"),
-               ("ul_mini_slot_symbols", "mini-slot occasions are not built"),
+        chk = [("ul_mini_slot_symbols", "mini-slot occasions are not built"),
+               ("mini_slot_dl", "mini-slot occasions are not built"),
+               ("dl_n_prb", "FDD's paired downlink carrier is not built"),
+               ("dl_bandwidth_mhz", "FDD's paired downlink carrier is not built"),
                ("n_layers_max", "rank-2 MIMO is not built"),
                ("ul_tpc", "closed-loop power control is not built"),
                ("eff_sinr", "only EESM is built"),
@@ -391,6 +405,10 @@ class NRConfig:
             out.append(("Rician K from the LOS state", "only a fixed rician_k_db is built"))
         if self.n_cells > 3:
             out.append((f"n_cells={self.n_cells}", "at most 3 cells (more need an ordered interference sum)"))
+        if self.dl and self.n_cells > 1:
+            out.append(("dl with n_cells > 1", "the downlink with several cells (DL interference) is not built"))
+        if self.dl and self.cqi_table != "mcs":
+            out.append((f"cqi_table={self.cqi_table!r}", "only the MCS-grid CQI report is built"))
         if self.channel not in ("log_distance", "tr38901", "radio_map"):
             out.append((f"channel={self.channel!r}", "channels built: log_distance, tr38901, radio_map"))
         if self.channel == "tr38901" and self.tr38901_los == "stochastic":

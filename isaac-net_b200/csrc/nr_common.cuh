@@ -16,7 +16,7 @@ namespace inb {
 constexpr uint32_t M32 = 0xFFFFFFFFu;
 constexpr uint32_t C1 = 0x21F0AAADu, C2 = 0x735A2D97u, GOLD = 0x9E3779B9u;
 constexpr uint32_t CH_STEP = 2u, CH_RESET = 3u;
-constexpr int SITE_FADING = 1, SITE_BLER_UL = 2, SITE_H0 = 4, SITE_KPHI = 6;
+constexpr int SITE_FADING = 1, SITE_BLER_UL = 2, SITE_BLER_DL = 3, SITE_H0 = 4, SITE_KPHI = 6;
 constexpr long long BIGI = 1LL << 62;
 
 __device__ __forceinline__ float fm(float a, float b) { return __fmul_rn(a, b); }

@@ -10,7 +10,8 @@
 // state h [E,R,S,2] and the CSI state (the gain of the last UL row, the CSI report rule of MacLink, mac.py:485) are
 // written back in place.  With C > 1 cells every link (robot, cell) fades on its own (h [E,R,C,S,2], hash elements
 // ((r C + c) S + s) 2 + {0, 1}) and gain row u is the u-th UL row's gain of every link, [E R][C][S]; the CSI then
-// depends on the serving cell and its handovers, so the MAC kernel keeps it.
+// depends on the serving cell and its handovers, so the MAC kernel keeps it.  With the downlink (p.dl_on, one cell) the
+// gain of every row that carries DL data or a CQI report also goes to gain row n_ul_rows + 1 + rows_dl[k][3].
 #include <cmath>
 #include <cstdint>
 
@@ -70,7 +71,8 @@ __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
       hr = fa(fm(rho, hr), fm(fm(c1, zr), p.inv_sqrt2));
       hi = fa(fm(rho, hi), fm(fm(c1, zi), p.inv_sqrt2));
     }
-    if (uls) {
+    const int dlr = p.dl_on ? p.rows_dl[k][3] : -1;
+    if (uls || dlr >= 0) {
       float g = 0.0f;
       if (p.fading) {
         float pw;
@@ -82,10 +84,13 @@ __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
         }
         g = fm(10.0f, log10f(clamp_min_t(pw, 1e-6f)));
       }
-      if (C == 1) ++u;
-      gout[(long long)u * plane] = g;
-      if (C > 1) ++u;
-      last = g;
+      if (dlr >= 0) gout[(long long)(p.n_ul_rows + 1 + dlr) * plane] = g;
+      if (uls) {
+        if (C == 1) ++u;
+        gout[(long long)u * plane] = g;
+        if (C > 1) ++u;
+        last = g;
+      }
     }
   }
   if (p.fading) reinterpret_cast<float2*>(st.h)[t] = make_float2(hr, hi);

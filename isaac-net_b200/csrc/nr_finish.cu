@@ -70,14 +70,16 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
   const InbParams& p = A.p;
   const InbState& st = A.s;
   const long long ob = A.o_base != nullptr ? *A.o_base : 0;
-  InbOutputs o;   // the output pointers of this step
-  o.delivered = out_ptr(A.o.delivered, ob); o.timed_out = out_ptr(A.o.timed_out, ob);
-  o.dropped = out_ptr(A.o.dropped, ob); o.deadline_miss = out_ptr(A.o.deadline_miss, ob);
-  o.cap = out_ptr(A.o.cap, ob); o.cls = out_ptr(A.o.cls, ob); o.arrival_slot = out_ptr(A.o.arrival_slot, ob);
-  o.tag = out_ptr(A.o.tag, ob); o.priority = out_ptr(A.o.priority, ob); o.bytes = out_ptr(A.o.bytes, ob);
-  o.delay = out_ptr(A.o.delay, ob); o.arrival = out_ptr(A.o.arrival, ob); o.newest = out_ptr(A.o.newest, ob);
-  o.queue_len = out_ptr(A.o.queue_len, ob); o.queue_bytes = out_ptr(A.o.queue_bytes, ob);
-  o.det_env = out_ptr(A.o.det_env, ob);
+  InbOutputs o;   // the output pointers of this step (NULL: not produced, e.g. the downlink call's UL-only outputs)
+  auto op = [ob](auto* x) { return x != nullptr ? out_ptr(x, ob) : x; };
+  o.delivered = op(A.o.delivered); o.timed_out = op(A.o.timed_out);
+  o.dropped = op(A.o.dropped); o.deadline_miss = op(A.o.deadline_miss);
+  o.cap = op(A.o.cap); o.cls = op(A.o.cls); o.arrival_slot = op(A.o.arrival_slot);
+  o.tag = op(A.o.tag); o.priority = op(A.o.priority); o.bytes = op(A.o.bytes);
+  o.delay = op(A.o.delay); o.arrival = op(A.o.arrival); o.newest = op(A.o.newest);
+  o.queue_len = op(A.o.queue_len); o.queue_bytes = op(A.o.queue_bytes);
+  o.det_env = op(A.o.det_env);
+  o.lost_any = op(A.o.lost_any); o.generated = op(A.o.generated);
   const int R = p.R, F = p.F, P = p.P;
   const long long e = blockIdx.x;
   const int seg = threadIdx.x / FW, l = threadIdx.x % FW;
@@ -142,20 +144,22 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
       if (delivered && cap[j] > newest) newest = cap[j];
       if (delivered && det[j] && hid[j] == last_hid) det_hit = true;
       if (fv) {
-        o.delivered[at] = delivered;
-        o.timed_out[at] = timed;
-        o.dropped[at] = dropped;
-        o.cap[at] = valid ? cap[j] - epoch : -1;
-        o.cls[at] = valid ? cls[j] : 0;
+        if (o.delivered) o.delivered[at] = delivered;
+        if (o.timed_out) o.timed_out[at] = timed;
+        if (o.dropped) o.dropped[at] = dropped;
+        if (o.lost_any) o.lost_any[at] = timed || dropped;            // the DL's dl_lost (engine.py:691)
+        if (o.generated) o.generated[at] = valid && cls[j] < 0;      // dl_generated (engine.py:694)
+        if (o.cap) o.cap[at] = valid ? cap[j] - epoch : -1;
+        if (o.cls) o.cls[at] = valid ? cls[j] : 0;
         const float delay = (float)dsb(dsb(fin[j], (double)cap[j]), off[j]);
-        o.delay[at] = delivered ? delay : NAN;
-        o.arrival[at] = valid ? da((double)(cap[j] - epoch), off[j]) : NAN;
-        o.arrival_slot[at] = valid ? (long long)rint(dm(off[j], (double)p.N)) : -1;
-        o.tag[at] = valid ? tag[j] : 0;
-        o.priority[at] = valid ? prio[j] : 0;
-        o.bytes[at] = valid ? end_[j] - start[j] : 0;
+        if (o.delay) o.delay[at] = delivered ? delay : NAN;
+        if (o.arrival) o.arrival[at] = valid ? da((double)(cap[j] - epoch), off[j]) : NAN;
+        if (o.arrival_slot) o.arrival_slot[at] = valid ? (long long)rint(dm(off[j], (double)p.N)) : -1;
+        if (o.tag) o.tag[at] = valid ? tag[j] : 0;
+        if (o.priority) o.priority[at] = valid ? prio[j] : 0;
+        if (o.bytes) o.bytes[at] = valid ? end_[j] - start[j] : 0;
         const bool late = delivered && (dm((double)delay, p.ctl_ms) > dline[j]);
-        o.deadline_miss[at] = late || ((timed || dropped) && isfinite(dline[j]));
+        if (o.deadline_miss) o.deadline_miss[at] = late || ((timed || dropped) && isfinite(dline[j]));
       }
       const bool g_ = !fv || delivered || timed || dropped || !valid;
       gone |= (unsigned long long)Seg<FW>::mask_bits(g_) << (j * FW);
@@ -222,16 +226,16 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
     }
     const long long qb = enq - ack_of(pend, floor_, sent);
     if (act && l == 0) {
-      o.newest[er] = newest >= 0 ? newest - epoch : -1;
-      o.queue_len[er] = n_keep;
-      o.queue_bytes[er] = (float)(qb > 0 ? qb : 0);
+      if (o.newest) o.newest[er] = newest >= 0 ? newest - epoch : -1;
+      if (o.queue_len) o.queue_len[er] = n_keep;
+      if (o.queue_bytes) o.queue_bytes[er] = (float)(qb > 0 ? qb : 0);
       st.sent[er] = sent;
       st.floor_[er] = floor_;
       st.bsr[er] = bsr;
     }
   }
   const int any = __syncthreads_or(det_hit ? 1 : 0);
-  if (threadIdx.x == 0) o.det_env[e] = any ? 1 : 0;
+  if (threadIdx.x == 0 && o.det_env) o.det_env[e] = any ? 1 : 0;
 }
 
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream) {

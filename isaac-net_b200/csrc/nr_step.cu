@@ -12,6 +12,10 @@ cudaError_t launch_step_g16_bsr(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g32_bsr(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_step_g128_bsr(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g16_dl(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g32_dl(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g64_dl(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g128_dl(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_radio(const InbStepArgs& a, cudaStream_t stream);
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
@@ -50,7 +54,18 @@ int check_args(const InbStepArgs& a, long long* gain_need) {
   if (a.o.blocked != nullptr && !(radio && rm.blockage)) return -11;   // blocked bits exist only after the launch
   int n_ul = 0;
   for (int k = 0; k < p.K_rows; ++k) n_ul += p.rows[k][1] > 0 ? 1 : 0;
-  *gain_need = p.C > 1 ? (long long)n_ul * p.C * p.S * p.E * p.R : (long long)(n_ul + 1) * p.S * p.E * p.R;
+  if (p.dl_on) {   // the downlink: one cell, its own args (state, outputs, arrivals, counters), DL gain rows
+    const InbStepArgs* d = a.dl;
+    if (p.C > 1 || d == nullptr || p.n_ul_rows != n_ul || p.n_dl_rows < 0 || d->p.E != p.E || d->p.R != p.R ||
+        d->p.S != p.S || d->p.P < 1 || d->p.P > INB_MAX_P || d->p.F < 1 || d->p.F > INB_MAX_F || d->p.M < 0 ||
+        d->p.M > INB_MAX_M || d->p.K_rows != p.K_rows || d->p.mcs_max < 0 || d->p.mcs_max >= d->p.MCS ||
+        d->p.bsr_on || d->p.tdma || d->p.amc_prev || d->p.phr_cap)
+      return -13;
+    for (int k = 0; k < p.K_rows; ++k)
+      if (p.rows_dl[k][3] >= p.n_dl_rows || d->p.rows_dl[k][3] != p.rows_dl[k][3]) return -13;
+  }
+  *gain_need = p.C > 1 ? (long long)n_ul * p.C * p.S * p.E * p.R
+                       : (long long)(n_ul + 1 + (p.dl_on ? p.n_dl_rows : 0)) * p.S * p.E * p.R;
   return 0;
 }
 
@@ -72,6 +87,23 @@ int launch_all(const InbStepArgs& args, cudaStream_t s) {
     if (err != cudaSuccess) return -100 - (int)err;
   }
   if (!mac) return 0;
+  if (p.dl_on) {   // the downlink MAC and finish first: the uplink MAC advances the step's RNG counter
+    InbStepArgs d = *a.dl;
+    d.gain = a.gain;
+    d.gain_cap = a.gain_cap;
+    d.pathgain_in = a.pathgain_in != nullptr ? a.pathgain_in : d.pathgain_in;
+    d.dl = nullptr;
+    if (p.R <= 16)
+      err = launch_step_g16_dl(d, s);
+    else if (p.R <= 32)
+      err = launch_step_g32_dl(d, s);
+    else if (p.R <= 64)
+      err = launch_step_g64_dl(d, s);
+    else
+      err = launch_step_g128_dl(d, s);
+    if (err == cudaSuccess) err = launch_finish(d, s);
+    if (err != cudaSuccess) return -100 - (int)err;
+  }
   const bool b = p.bsr_on != 0;
   if (p.R <= 16)
     err = b ? launch_step_g16_bsr(a, s) : launch_step_g16(a, s);

@@ -398,8 +398,12 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 // the PF instance with pf_update = "rbg" (the per-RBG metric over the bytes granted so far); 0 is every other case.
 // NCT: the number of cells; NCT > 1 (MC) adds the A3 association and handover, per-cell schedulers, UL power control
 // and interference.  BSR: the SR / BSR grant pipeline (p.bsr_on) replaces the lumped SR grant; compiled only into the
-// instances that run it, so the other instances carry none of its code.
-template <int GW, int NCT, int SV, bool BSR>
+// instances that run it, so the other instances carry none of its code.  DL: the downlink link (one cell; DlMac,
+// isaac_net/core/mac_dl.py:1-49) on the same slot machinery: its own state, queue, arrivals and counters, the DL data
+// rows and CQI reports of the schedule (InbParams.rows_dl), the scheduler's estimate from the last CQI report (the
+// MCS threshold SINR the UE reported, csi = thr[m] - ref), no power split, HARQ-ACK timing (an ACKed process waits in
+// state 2 until its HARQ-ACK reaches the gNB, a NACK until then too), the BLER_DL draws.
+template <int GW, int NCT, int SV, bool BSR, bool DL>
 __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
   constexpr bool MC = NCT > 1;   // several cells
   constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
@@ -492,12 +496,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   float last_nprb = 0.0f;   // PRBs of the last PUSCH (ul_amc_alloc = "previous")
   if (act && p.amc_prev) last_nprb = st.last_nprb[CK(er, NER, 1)];
   // HARQ process states as bit masks (state 1: holds a TB awaiting its retransmission or ACK; state 0: free)
-  uint32_t pend = 0u, freem = 0u;
+  uint32_t pend = 0u, freem = 0u, ackm = 0u;   // ackm (DL): state 2, decoded and waiting for its HARQ-ACK
   if (act) {
     for (int q = 0; q < P; ++q) {
       const long long hs = st.h_state[CK(eP + q, NERP, 4)];
       if (hs == 1) pend |= 1u << q;
       else if (hs == 0) freem |= 1u << q;
+      else if (DL && hs == 2) ackm |= 1u << q;
     }
   }
   const long long last_hid = env_ok ? A.last_hid[CK(e, p.E, 10)] : 0;
@@ -525,7 +530,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         st.end_[CK(at, NERF, 3)] = enq + nb;
         st.lost[CK(at, NERF, 3)] = 0;
         st.fin[CK(at, NERF, 3)] = INFINITY;
-        st.cls[CK(at, NERF, 3)] = 0;
+        // a generated DL message carries cls = -tag, at most -1 (NREngine._inject_dl, engine.py:660-662)
+        st.cls[CK(at, NERF, 3)] = DL ? -(A.a.tag[CK(em, NERM, 7)] > 1 ? A.a.tag[CK(em, NERM, 7)] : 1) : 0;
         st.det[CK(at, NERF, 3)] = A.a.det[CK(em, NERM, 7)] != 0 ? 1 : 0;
         st.hid[CK(at, NERF, 3)] = last_hid;
         st.off[CK(at, NERF, 3)] = dm((double)A.a.slot[CK(em, NERM, 7)], p.inv_N_d);
@@ -710,7 +716,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
 
   // ======================================================================= slot loop (nr_engine.py:656-667)
   for (int k = 0; k < p.K_rows; ++k) {
-    const int rel = p.rows[k][0], uls = p.rows[k][1], srf = p.rows[k][2];
+    // uls: the data symbols of this link's slot (the DL instance: the row's DL data symbols); srf: SR opportunity
+    const int rel = p.rows[k][0], uls = DL ? p.rows_dl[k][0] : p.rows[k][1], srf = DL ? 0 : p.rows[k][2];
     const long long g = T * p.N + rel;
     if constexpr (MC) {   // A3 handovers due by this slot fire before it (nr_engine.py:748-752)
       if (act && k_ho >= 0 && k_ho <= rel && !fired) {
@@ -727,6 +734,19 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       }
       enq = vis > base ? vis : base;
     }
+    // ---- DL CQI report (DlMac.cqi_report, mac_dl.py:28-39; NRNet.step, nr_engine.py:660-661), before the row's DL
+    // data slot: per RBG the highest MCS (<= the DL cap) whose threshold the SINR ref + gain meets; the gNB keeps that
+    // MCS's threshold SINR, csi = thr[m] - ref
+    if constexpr (DL) {
+      if (p.rows_dl[k][1] && act) {
+        const long long gq = (long long)(p.n_ul_rows + 1 + p.rows_dl[k][3]) * plane + er * S;
+        for (int s = 0; s < S; ++s) {
+          const float rs = REF(s);
+          const int m = mcs_at(s_thr, p.mcs_max, thr_mono, fa(rs, A.gain[CK(gq + s, GCAP, 13)]));
+          st.csi[CK(eS + s, NERS, 5)] = fs(s_thr[m], rs);
+        }
+      }
+    }
     // ---- SR (UlMac.sr_step, mac_ul.py:66-71; the BSR pipeline's, mac_ul.py:280-287)
     if (srf && act) {
       if constexpr (BSR) bsr_sr_step(st, er, enq, sent, g, sr_t);
@@ -734,15 +754,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     if (!uls) continue;
 
-    // =================================================================== UL data slot (MacLink.slot, mac.py:228-508)
+    // =================================================================== data slot (MacLink.slot, mac.py:228-508)
     const long long unsent = enq - sent;
-    // the CSI of this decision is gain row u (the gain of the previous UL row), this row's fading gain is row u + 1
-    const long long g_csi = (long long)u * plane, g_gain = g_csi + plane;
+    // the CSI of this decision is gain row u (the gain of the previous UL row), this row's fading gain is row u + 1;
+    // the DL instance reads its CSI state (the CQI reports) and the row's DL gain row
+    const long long g_csi = (long long)u * plane;
+    const long long g_gain = DL ? (long long)(p.n_ul_rows + 1 + p.rows_dl[k][3]) * plane : g_csi + plane;
+    if constexpr (DL) {   // DL processes whose HARQ-ACK has reached the gNB become free (mac.py:238-239)
+      for (uint32_t m_ = ackm; m_; m_ &= m_ - 1u) {
+        const int q = __ffs(m_) - 1;
+        if (st.h_ready[CK(eP + q, NERP, 4)] <= g) {
+          st.h_state[CK(eP + q, NERP, 4)] = 0;
+          ackm &= ~(1u << q);
+          freem |= 1u << q;
+        }
+      }
+    }
     // lumped SR grant (mac_ul.py:140-147), or the BSR pipeline's bootstrap grant and matured reports
     long long need_bsr = 0;
     if constexpr (BSR) {
       if (act) need_bsr = bsr_pre_slot(st, p, er, enq, g, sr_t);
-    } else if (sr_t >= 0 && g - sr_t >= p.sr_delay) {
+    } else if (!DL && sr_t >= 0 && g - sr_t >= p.sr_delay) {
       bsr = bsr < 1 ? 1 : bsr;
       sr_t = -1;
     }
@@ -761,7 +793,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     const bool any_free = p_new >= 0;
     if (p_new < 0) p_new = 0;
-    const long long need = BSR ? need_bsr : (bsr < unsent ? bsr : unsent);
+    const long long need = DL ? unsent : (BSR ? need_bsr : (bsr < unsent ? bsr : unsent));   // DL: MacLink._need
     bool new_el = act && any_free && need > 0 && !has_rx;
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
@@ -800,6 +832,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             float est;
             if constexpr (MC) {
               est = fa(fs(REF(s), fmaxf(s_lw10[s], pcv)), CSI_A(csi_src, er, serv, s));
+            } else if constexpr (DL) {   // DlMac._sched_estimate (mac_dl.py:41-42): ref + csi
+              est = fa(REF(s), st.csi[CK(eS + s, NERS, 5)]);
             } else {
               est = fa(fs(REF(s), s_lw10[s]), A.gain[CK(g_csi + er * S + s, GCAP, 13)]);
             }
@@ -827,6 +861,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             float est;
             if constexpr (MC) {   // one RBG at the power-control PSD (mac_ul.py:160-161)
               est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), CSI_A(csrc_a, ra / S, serv_a, s));
+            } else if constexpr (DL) {
+              est = fa(refs, st.csi[CK(ra + s, NERS, 5)]);
             } else {
               est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
             }
@@ -1101,7 +1137,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const bool tx_new = new_el && (n_sb > 0);
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
-    float split = fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    // (the DL has none: est_tx = est and the decode SINR ref + gain, mac_dl.py:44-45; ref - 0 is ref exactly)
+    float split = DL ? 0.0f : fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
     if constexpr (MC) split = fmaxf(split, pcv);   // at least the power-control backoff (mac_ul.py:176-180)
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
@@ -1215,7 +1252,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
         if (in && !rest_only) {
           const int s = lane;
           const float refs = REF_A(s, ta, ref_a, serv_a);
-          const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s) : A.gain[CK(g_csi + ra + s, GCAP, 13)];
+          const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s)
+                                 : (DL ? st.csi[CK(ra + s, NERS, 5)] : A.gain[CK(g_csi + ra + s, GCAP, 13)]);
           const float est_tx = fa(fs(refs, split_a), csi_s);
           ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
@@ -1403,19 +1441,29 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       cidx(p, cbs, i0, wi);
       const float b = bler_lookup(bgrid, mcs, eff_used, i0, wi);
       const float p_err = fs(1.0f, powf(fs(1.0f, b), ncb));
-      const float u = uniform_at(key_stream(kenv, (uint32_t)((SITE_BLER_UL << 16) | rel)), (uint32_t)r);
+      const float u = uniform_at(key_stream(kenv, (uint32_t)(((DL ? SITE_BLER_DL : SITE_BLER_UL) << 16) | rel)),
+                                 (uint32_t)r);
       ok = u >= p_err;
       fail = !ok;
       exh = fail && ntx >= p.max_tx;
+      // HARQ times (MacLink._harq_times): UL, an ACK frees the process now and a NACK waits ul_rtt; DL
+      // (mac_dl.py:47-49), both wait for the HARQ-ACK slot + gnb_proc_slots, an ACKed process in state 2
+      const long long r_ack = T * p.N + p.rows_dl[k][2];
       if (ok) {
-        st.h_state[CK(hp, NERP, 4)] = 0;
         pend &= ~(1u << p_tx);
-        freem |= 1u << p_tx;
-        st.h_ready[CK(hp, NERP, 4)] = g;
+        if constexpr (DL) {
+          st.h_state[CK(hp, NERP, 4)] = 2;
+          ackm |= 1u << p_tx;
+          st.h_ready[CK(hp, NERP, 4)] = r_ack;
+        } else {
+          st.h_state[CK(hp, NERP, 4)] = 0;
+          freem |= 1u << p_tx;
+          st.h_ready[CK(hp, NERP, 4)] = g;
+        }
       }
       st.h_ntx[CK(hp, NERP, 4)] = ntx;
       st.h_comb[CK(hp, NERP, 4)] = comb;
-      if (fail) st.h_ready[CK(hp, NERP, 4)] = g + p.ul_rtt;
+      if (fail) st.h_ready[CK(hp, NERP, 4)] = DL ? r_ack : g + p.ul_rtt;
       if (exh) {
         if (!p.harq_drop) {
           st.h_ntx[CK(hp, NERP, 4)] = 0;
@@ -1450,7 +1498,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
     if constexpr (BSR) {
       if (act) bsr_post_slot(st, p, er, enq, sent, g, tx, tx_new, tbs_new);
-    } else if (tx) {
+    } else if (!DL && tx) {
       bsr = enq - sent;
     }
     if constexpr (MC) csi_src = u;   // the serving link's gain of this row is the CSI of the next decision
@@ -1537,15 +1585,15 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       st.serv[CK(er, NER, 1)] = serv;
       st.ho_end[CK(er, NER, 1)] = ho_end;
       st.n_ho[CK(er, NER, 1)] = n_ho;
-    } else {
+    } else if (!DL) {
       out_ptr(o.sinr_db, ob)[CK(er, NER, 1)] = sinr_obs;
       if (o.serving_cell) out_ptr(o.serving_cell, ob)[CK(er, NER, 1)] = 0;
       if (o.pathgain) out_ptr(o.pathgain, ob)[CK(er, NER, 1)] = pg;
       if (o.blocked) out_ptr(o.blocked, ob)[CK(er, NER, 1)] = A.rm.blk[CK(er, NER, 1)] & 1;
     }
     if (o.los) out_ptr(o.los, ob)[CK(er, NER, 1)] = (uint8_t)p.los_const;
-    out_ptr(o.gen_accepted, ob)[CK(er, NER, 1)] = n_acc;
-    out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
+    if (o.gen_accepted) out_ptr(o.gen_accepted, ob)[CK(er, NER, 1)] = n_acc;
+    if (o.gen_bytes) out_ptr(o.gen_bytes, ob)[CK(er, NER, 1)] = full_enq - n0;
     st.sent[CK(er, NER, 1)] = sent; st.floor_[CK(er, NER, 1)] = floor_; st.bsr[CK(er, NER, 1)] = bsr; st.sr_t[CK(er, NER, 1)] = sr_t; st.last_tx[CK(er, NER, 1)] = last_tx;
     st.enq[CK(er, NER, 1)] = enq; st.olla[CK(er, NER, 1)] = olla; st.avg[CK(er, NER, 1)] = avg;
     if (p.amc_prev) st.last_nprb[CK(er, NER, 1)] = last_nprb;
@@ -1569,7 +1617,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     for (int i = r; i < INB_NCTR; i += GW)
       if (sc[i]) atomicAdd((unsigned long long*)&c[i], sc[i]);
   }
-  if (env_ok && r == 0) A.rng_ctr[CK(e, p.E, 10)] += 1;
+  // the step's counter-RNG call ends here (the DL instance runs before this one and leaves it alone)
+  if (!DL && env_ok && r == 0) A.rng_ctr[CK(e, p.E, 10)] += 1;
 #undef CK
 }
 

@@ -1,0 +1,6 @@
+// Instantiation of the fused step kernel's downlink instances for groups of 64 lanes (its own translation unit,
+// compiled in parallel with the others).
+#include "nr_step_launch.cuh"
+namespace inb {
+cudaError_t launch_step_g64_dl(const InbStepArgs& a, cudaStream_t stream) { return launch_gw_dl<64>(a, stream); }
+}  // namespace inb

@@ -3,7 +3,7 @@
 // Launch of the fused step kernel for one group width GW (robots per env rounded up to a power of two).
 #include "nr_step.cuh"
 namespace inb {
-template <int GW, int NCT, int SV, bool BSR>
+template <int GW, int NCT, int SV, bool BSR, bool DL = false>
 cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
   constexpr int NT = GW > 32 ? GW : 128;
   const int gpb = GW > 32 ? 1 : 128 / GW;
@@ -16,7 +16,7 @@ cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 0 || dev >= 64 || smem > configured[dev].load(std::memory_order_acquire)) {
-      e = cudaFuncSetAttribute(nr_step_kernel<GW, NCT, SV, BSR>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      e = cudaFuncSetAttribute(nr_step_kernel<GW, NCT, SV, BSR, DL>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       if (e != cudaSuccess) return e;
       if (dev >= 0 && dev < 64) {   // raise the remembered size (several threads may race here; the max wins)
         size_t cur = configured[dev].load(std::memory_order_relaxed);
@@ -26,7 +26,7 @@ cudaError_t launch_gw_mc(const InbStepArgs& a, cudaStream_t stream) {
     }
   }
   dim3 grid((a.p.E + gpb - 1) / gpb), block(NT);
-  nr_step_kernel<GW, NCT, SV, BSR><<<grid, block, smem, stream>>>(a);
+  nr_step_kernel<GW, NCT, SV, BSR, DL><<<grid, block, smem, stream>>>(a);
   return cudaGetLastError();
 }
 
@@ -43,5 +43,13 @@ cudaError_t launch_gw(const InbStepArgs& a, cudaStream_t stream) {
   if (a.p.sched == 2) return launch_gw_sv<GW, 1, BSR>(a, stream);   // round robin
   if (a.p.pf_rbg) return launch_gw_sv<GW, 2, BSR>(a, stream);       // PF with the per-RBG metric
   return launch_gw_sv<GW, 0, BSR>(a, stream);
+}
+
+// the downlink instances of one group width (one cell, no BSR pipeline)
+template <int GW>
+cudaError_t launch_gw_dl(const InbStepArgs& a, cudaStream_t stream) {
+  if (a.p.sched == 2) return launch_gw_mc<GW, 1, 1, false, true>(a, stream);
+  if (a.p.pf_rbg) return launch_gw_mc<GW, 1, 2, false, true>(a, stream);
+  return launch_gw_mc<GW, 1, 0, false, true>(a, stream);
 }
 }  // namespace inb

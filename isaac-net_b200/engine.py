@@ -26,6 +26,7 @@ from .config import NRConfig
 from .phy import PhyTables
 from . import invariants as inv
 from .radio_map import cdf_table, load_radio_map
+from .downlink import REF as DL_REF, Downlink
 from .traffic import CounterDraws, DeviceTrafficGen, Requests, TrafficGen, generates
 
 # counter-RNG constants (isaac_net/core/proto/rng.py:33-38, nr_rng.py:34, radio.py:53-56)
@@ -157,13 +158,19 @@ class NRB200Engine:
         # the arrivals of periodic / video / bursty models come from one kernel that replays the torch.Generator
         # stream; event models (host triggers) keep the torch path
         self.dtraffic = DeviceTrafficGen(self.traffic, self.L) if DeviceTrafficGen.supports(self.traffic) else None
+        # the downlink (dl=True, one cell): its state, counters and DL traffic models (downlink.py)
+        self.dl = None
+        if cfg.dl:
+            if traffic_rng != "generator" and generates(cfg.traffic, "dl"):
+                raise B200Unsupported("traffic_rng='counter' with downlink traffic models is not built")
+            self.dl = Downlink(self)
         self._fields = None
         self._radio_ready = False          # the radio's draws exist (made at the first step with poses)
         self._gnb = torch.tensor(cfg.gnb_xy(), dtype=torch.float32, device=dev).contiguous()
         self._sched = {}
         # CUDA graphs: one captured step (traffic draws + the fused launch) per schedule key, replayed with the poses
         # copied into a static buffer and the control step read from device memory
-        self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ()))
+        self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ())) and not cfg.dl
         self._graphs = {}
         self._pool = None
         # a captured step reads its control step and the address of its output block from here (inb_store2)
@@ -258,6 +265,7 @@ class NRB200Engine:
         p.pf_rbg, p.pf_freeze = int(cfg.pf_update == "rbg"), int(cfg.pf_avg_idle == "freeze")
         p.tdma, p.amc_prev = int(cfg.ul_retx_sched == "tdma"), int(cfg.ul_amc_alloc == "previous")
         p.lena_ctr = int(bool(cfg.lena_mac_switches()))
+        p.dl_on = int(bool(cfg.dl))
         p.bsr_on = int(cfg.ul_grant_model == "bsr")
         if p.bsr_on:   # the SR / BSR pipeline's timing and header sizes (config.py:588-594, 1088-1090)
             p.sr_boot_slots, p.sr_boot_bytes = int(cfg.sr_boot_slots), int(cfg.sr_boot_bytes)
@@ -327,7 +335,7 @@ class NRB200Engine:
                                                 self.ctr.data_ptr(), self.status.data_ptr())
         # fading-gain rows of one step: the CSI before the step + one row per UL slot (at most slots_per_step); with
         # several cells one row per UL slot holds every link's gain
-        rows = self.N * self.C if self.C > 1 else self.N + 1
+        rows = self.N * self.C if self.C > 1 else self.N + 1 + (self.N if cfg.dl else 0)   # + the DL gain rows
         self._gain = torch.empty(rows * self.S * self.E * self.R, dtype=torch.float32, device=self.dev)
         a.gain, a.gain_cap = self._gain.data_ptr(), self._gain.numel()
 
@@ -499,6 +507,8 @@ class NRB200Engine:
         if ids is None:
             if self.traffic is not None:
                 self.traffic.reset(None)
+            if self.dl is not None:
+                self.dl.reset(None)
             self._kernel_reset(None)
             self.ctr.zero_()
             if self.C > 1:
@@ -516,6 +526,8 @@ class NRB200Engine:
         m[ids] = True
         if self.traffic is not None:
             self.traffic.reset(m)
+        if self.dl is not None:
+            self.dl.reset(m)
         self._kernel_reset(m)
         self.epoch.index_fill_(0, ids, self.T)
         self._uniform_epoch = None
@@ -598,6 +610,13 @@ class NRB200Engine:
         st["enq"].add_(nb * acc)
         return acc
 
+    def add_dl_frames(self, t, nbytes, cls=None):
+        """One downlink frame of nbytes [E,R] application bytes per robot (0 = none) at capture step t, cls [E,R]
+        tagging it (NREngine.add_dl_frames, engine.py:825-827); returns accepted [E,R]."""
+        if self.dl is None:
+            raise ValueError("add_dl_frames needs config.dl = True")
+        return self.dl.add_frames(self._now(t), nbytes, cls)
+
     def add_frames(self, t, send, det, hid, snr_db):
         """Legacy wrapper (NetSlot API)."""
         self.submit(t, Requests(send, det, hid), snr_db)
@@ -611,17 +630,23 @@ class NRB200Engine:
         key = (g0 % cfg.schedule_period(), dt0 if cfg.fading else 0)
         ent = self._sched.get(key)
         if ent is None:
-            rows, rowf = [], []
+            rows, rowf, rows_dl = [], [], []
             prev = None
-            for rel, uls, sr in sched:
+            j = 0
+            for rel, dls, uls, sr, cqi, ack in sched:
                 dt = dt0 if prev is None else rel - prev
                 prev = rel
                 rho = cfg.fading_rho_per_ms ** (dt * cfg.slot_ms)
                 rows.append((rel, uls, int(sr), int(dt > 0)))
                 rowf.append((_f32(rho), _f32(math.sqrt(1 - rho ** 2))))
+                # the downlink's view of the row: DL symbols, CQI report, HARQ-ACK slot + gNB processing (relative to
+                # g0, mac_dl.py:47-49), index of its DL gain row (rows with DL data or a CQI report) or -1
+                need = bool(dls or cqi)
+                rows_dl.append((dls, int(cqi), ack + cfg.gnb_proc_slots, j if need else -1))
+                j += int(need)
             if len(rows) > nat.MAX_ROWS:
                 raise B200Unsupported(f"{len(rows)} scheduled slots per control step (at most {nat.MAX_ROWS})")
-            ent = (rows, rowf, sum(1 for r in rows if r[1]))
+            ent = (rows, rowf, sum(1 for r in rows if r[1]), rows_dl, j, sum(1 for r in rows_dl if r[0]))
             self._sched[key] = ent
         if sched and cfg.fading:
             self.last_g = g0 + sched[-1][0]
@@ -667,7 +692,7 @@ class NRB200Engine:
         return out, o
 
     def step(self, t=None, x=None, cur_hid=None, *, snr_db=None, dl_snr_db=None, pathgain_db=None, vel=None,
-             triggers=None, blockers=None, fetch=None, _pathgain=None, _arrivals=None):
+             triggers=None, blockers=None, fetch=None, _pathgain=None, _arrivals=None, _dl_arrivals=None):
         """Advance [t, t+1). x: poses [E,R,2|3] (through the engine's radio) or SNR [E,R] dB; snr_db= [E,R] or
         [E,R,S]; triggers= feeds event traffic models.  Returns the step dict (or (newest, det_env) in the legacy
         form step(t, snr, cur_hid)).
@@ -684,7 +709,8 @@ class NRB200Engine:
             x, staged = self._stage_poses(x)
         q_before = self.queued().clone() if self.debug_invariants else None
         res = self._step(t, x, cur_hid, snr_db=snr_db, dl_snr_db=dl_snr_db, pathgain_db=pathgain_db, vel=vel,
-                         triggers=triggers, blockers=blockers, _pathgain=_pathgain, _arrivals=_arrivals)
+                         triggers=triggers, blockers=blockers, _pathgain=_pathgain, _arrivals=_arrivals,
+                         _dl_arrivals=_dl_arrivals)
         if q_before is not None and isinstance(res, dict):
             # submitted messages are queued already when the step starts; the step adds the traffic models' ones
             acc = res["gen_accepted"] if "gen_accepted" in res else torch.zeros_like(q_before)
@@ -751,10 +777,11 @@ class NRB200Engine:
         if ev is not None:
             ev.synchronize()
 
-    def _step(self, t, x, cur_hid, *, snr_db, dl_snr_db, pathgain_db, vel, triggers, blockers, _pathgain, _arrivals):
+    def _step(self, t, x, cur_hid, *, snr_db, dl_snr_db, pathgain_db, vel, triggers, blockers, _pathgain, _arrivals,
+              _dl_arrivals=None):
         cfg = self.config
-        if dl_snr_db is not None:
-            raise B200Unsupported("dl_snr_db: the downlink is not built")
+        if dl_snr_db is not None and self.dl is None:
+            raise ValueError("dl_snr_db= needs config.dl = True")
         if pathgain_db is not None:
             if self.C == 1:
                 raise ValueError("pathgain_db= needs config.n_cells > 1; use x (poses or SNR) with one cell")
@@ -768,6 +795,7 @@ class NRB200Engine:
         det_hid = cur_hid.to(self.dev, torch.long).contiguous() if legacy else None
         E, R, S, a, p = self.E, self.R, self.S, self._args, self._args.p
         if (self.graphs and self._steps_done > 0 and not legacy and _pathgain is None and _arrivals is None
+                and _dl_arrivals is None
                 and snr_db is None and x is not None and x.dim() == 3 and self._radio_ready
                 and getattr(self, "trace_buf", None) is None and getattr(self, "_kernel_events", None) is None):
             return self._graph_step(T, x)
@@ -779,7 +807,7 @@ class NRB200Engine:
             a.det_hid = det_hid.data_ptr()
         # inputs
         a.pos = a.pathgain_in = a.ul_ref_in = None
-        snr_out = None
+        snr_out = snr_in = None
         if _pathgain is not None:
             pg = _pathgain.to(self.dev, torch.float32).contiguous()
             keep.append(pg)
@@ -787,6 +815,7 @@ class NRB200Engine:
         elif snr_db is not None or (x is not None and x.dim() == 2):
             s = snr_db if snr_db is not None else x
             s = s.to(self.dev, torch.float32)
+            snr_in = s
             ref = (s if s.dim() == 3 else s[..., None].expand(E, R, S)).contiguous()
             zero = torch.zeros(E, R, device=self.dev)
             keep += [ref, zero]
@@ -800,11 +829,15 @@ class NRB200Engine:
             a.pos = pos.data_ptr()
         else:
             raise ValueError("step needs poses [E,R,2|3] or an SNR [E,R] (x= or snr_db=)")
-        rows, rowf, n_ul = self._rows(T * self.N)
+        rows, rowf, n_ul, rows_dl, n_dlg, n_dl = self._rows(T * self.N)
         p.K_rows = len(rows)
         for k, (r4, f2) in enumerate(zip(rows, rowf)):
             p.rows[k][0], p.rows[k][1], p.rows[k][2], p.rows[k][3] = r4
             p.rowf[k][0], p.rowf[k][1] = f2
+        if self.dl:
+            p.n_ul_rows, p.n_dl_rows = n_ul, n_dlg
+            for k, r4 in enumerate(rows_dl):
+                p.rows_dl[k][0], p.rows_dl[k][1], p.rows_dl[k][2], p.rows_dl[k][3] = r4
         p.T = T
         p.s0 = self.s0
         out, o = self._alloc_outputs()
@@ -842,10 +875,17 @@ class NRB200Engine:
             p.M = 0
             for n in nat.ARR_FIELDS:
                 setattr(a.a, n, None)
+        dl_out = None
+        a.dl = None
+        if self.dl is not None:      # the DL MAC and finish run inside the same call, before the uplink MAC
+            d, dl_out = self.dl.launch_args(a, snr=snr_in, dl_snr=dl_snr_db, arrivals=_dl_arrivals)
+            a.dl = ctypes.addressof(d)
         nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
         if ev is not None:
             ev[1].record()
         self.prb_avail += float(cfg.nprb) * E * n_ul * self.C     # every cell's PRBs (mac.py:491)
+        if self.dl is not None:
+            self.dl.prb_avail += float(cfg.nprb) * E * n_dl
         self.T = T + 1
         sinr = out.pop("sinr_db") if snr_out is None else snr_out.clone()
         self.pathgain = out.pop("pathgain")
@@ -866,6 +906,9 @@ class NRB200Engine:
         for k in ("los", "blocked"):
             if k in out:
                 res[k] = out[k]
+        if dl_out is not None:         # dl_newest, dl_queue_len; with DL traffic models the dl_* frame outputs
+            dl_out["dl_newest"] = dl_out["dl_newest"]
+            res.update(dl_out)
         self._keep = keep                           # the launch is asynchronous: keep its inputs alive
         return res
 
@@ -942,7 +985,7 @@ class NRB200Engine:
         cfg, E, R = self.config, self.E, self.R
         if self._pos_buf is None:
             self._pos_buf = torch.empty(E, R, 2, dtype=torch.float32, device=self.dev)
-        rows, rowf, n_ul = self._rows(T * self.N)
+        rows, rowf, n_ul = self._rows(T * self.N)[:3]
         key = self._rows_key
         ent = self._graphs.get(key)
         if ent is None:
@@ -980,8 +1023,12 @@ class NRB200Engine:
 
     # ------------------------------------------------------------------ observability
     def counters(self):
-        """{"ul": counters} as NRNet.counters() (nr_engine.py:916-925), folded from the per-env device words."""
-        return self.fold_counters(self.ctr.sum(0), self.prb_avail)
+        """{"ul": counters[, "dl": counters]} as NRNet.counters() (nr_engine.py:916-925), folded from the per-env
+        device words."""
+        res = self.fold_counters(self.ctr.sum(0), self.prb_avail)
+        if self.dl is not None:
+            res["dl"] = self.dl.counters()
+        return res
 
     def fold_counters(self, c, prb_avail):
         """counters() from a summed counter vector c [INB_NCTR] and the PRBs offered (also for sums over shards)."""
@@ -1040,6 +1087,19 @@ class NRB200Engine:
             sd["host." + n] = getattr(self, n)
         if getattr(self, "pathgain", None) is not None:
             sd["eng.pathgain"] = self.pathgain.clone()
+        if self.dl is not None:            # the downlink: state, counters, DL traffic models
+            for n, t in self.dl.st.items():
+                sd["dl.st." + n] = t.clone()
+            sd["dl.ctr"], sd["dl.prb_avail"] = self.dl.ctr.clone(), self.dl.prb_avail
+            tg = self.dl.traffic
+            if tg is not None:
+                sd["dl.traffic.gen"], sd["dl.traffic.rgen"] = tg.gen.get_state(), tg.rgen.get_state()
+                for i, src in enumerate(tg.sources):
+                    for n in src.names:
+                        sd[f"dl.traffic.src{i}.{n}"] = getattr(src, n).clone()
+                    sd[f"dl.traffic.src{i}.deferred"] = src.deferred.clone()
+                if self.dl.dtraffic is not None:
+                    sd["dl.traffic.calls"] = self.dl.dtraffic.calls.clone()
         if self._radio_ready:
             sd["radio.ready"] = True
             if self._fields is not None:
@@ -1100,6 +1160,22 @@ class NRB200Engine:
             self._graphs.clear()
         if "eng.pathgain" in sd:
             self.pathgain = sd["eng.pathgain"].to(self.dev).clone()
+        if self.dl is not None:
+            for n, t in self.dl.st.items():
+                cp(t, "dl.st." + n)
+            cp(self.dl.ctr, "dl.ctr")
+            self.dl.prb_avail = sd.get("dl.prb_avail", self.dl.prb_avail)
+            tg = self.dl.traffic
+            if tg is not None:
+                if "dl.traffic.gen" in sd:
+                    tg.gen.set_state(sd["dl.traffic.gen"])
+                    tg.rgen.set_state(sd["dl.traffic.rgen"])
+                for i, src in enumerate(tg.sources):
+                    for n in src.names:
+                        cp(getattr(src, n), f"dl.traffic.src{i}.{n}")
+                    cp(src.deferred, f"dl.traffic.src{i}.deferred")
+                if self.dl.dtraffic is not None:
+                    cp(self.dl.dtraffic.calls, "dl.traffic.calls")
         if sd.get("radio.ready"):
             if not self._radio_ready:
                 self._make_radio()
@@ -1185,6 +1261,9 @@ class NRB200Engine:
         if self._fields is not None and self.config.channel in self._FIELD_KEYS:
             kk, pk = self._FIELD_KEYS[self.config.channel]
             out[kk], out[pk] = self._fields
+        if self.dl is not None:            # the downlink MacLink and its queue (net.dl.*, net.dl.q.*)
+            for k, v in DL_REF.items():
+                out[k] = self.dl.st[v]
         return out
 
     def load_reference_state(self, snap):
@@ -1201,6 +1280,8 @@ class NRB200Engine:
                 fld[k] = t
             elif k in self._REF and self._REF[k] in self.st:
                 self.st[self._REF[k]].copy_(t.to(self.dev))
+            elif k in DL_REF and self.dl is not None:
+                self.dl.st[DL_REF[k]].copy_(t.to(self.dev))
             elif k == "net.last_g":
                 self.last_g = None if int(t) < 0 else int(t)
             elif k == "rng.episode":

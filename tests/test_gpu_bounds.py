@@ -22,7 +22,8 @@ bad = []
 for wl_i, E, R, over in ((1, 8, 16, {}), (2, 16, 32, {}), (2, 8, 32, dict(scheduler="rr", retx_priority=False)),
                          (3, 4, 64, {}), (5, 4, 48, {}), (1, 4, 16, dict(blockage=True, blockage_model="stochastic")),
                          (4, 2, 128, {}), (2, 8, 32, dict(ul_grant_model="bsr")),
-                         (3, 4, 64, dict(ul_grant_model="bsr", a3_ttt_ms=2.0, a3_hyst_db=0.5))):
+                         (3, 4, 64, dict(ul_grant_model="bsr", a3_ttt_ms=2.0, a3_hyst_db=0.5)),
+                         (2, 4, 32, dict(tdd_pattern="DDSUU", dl=True))):
     wl = presets.workload(wl_i)
     cfg = wl.config(**over)
     eng = ib.make_engine("L2", E, R, dev, cfg, seed=wl.seed)
