@@ -98,6 +98,11 @@ VARIANTS = {   # scheduler / priority settings the fixtures do not hold: round r
     # groups of 16 and 128 lanes
     "1_saturated": (1, 8, 16, dict(traffic=(_bursty(1500, 2000),), ue_tx_dbm=-6.0)),
     "4_saturated": (4, 2, 128, dict(traffic=(_bursty(8192, 400),), msg_sizes=(8192.0,), ue_tx_dbm=-8.0)),
+    # one cell on groups of 64 lanes (the single-warp allocation rounds): PF, and the per-RBG PF metric without
+    # retransmission priority (the release of short retransmissions' RBGs), on weak links
+    "1_r48": (1, 4, 48, dict(ue_tx_dbm=-14.0, max_harq_tx=2)),
+    "2_r64_rbg_norp": (2, 4, 64, dict(pf_update="rbg", retx_priority=False, ue_tx_dbm=-10.0)),
+    "4_norp": (4, 2, 128, dict(retx_priority=False, ue_tx_dbm=-12.0)),
     # the SR / BSR grant pipeline with the round-robin instance and on groups of 128 lanes
     "1_bsr": (1, 8, 16, dict(ul_grant_model="bsr", ue_tx_dbm=-12.0, max_harq_tx=2)),
     "4_bsr": (4, 2, 128, dict(ul_grant_model="bsr", ue_tx_dbm=-8.0)),
