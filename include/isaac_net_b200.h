@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 14
+#define INB_ABI_VERSION 15
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -183,6 +183,10 @@ typedef struct {
    * DL gain-row index or -1 */
   int32_t dl_on, n_ul_rows, n_dl_rows;
   int32_t rows_dl[INB_MAX_ROWS][4];
+  /* the DL call's link-adaptation tables: la_sets stacked [NPRB+1, M] sets (one per DL data-symbol count: a D slot's
+   * and, with special_dl_data, an S slot's), dl_nsym_tab[nsym] = the set of a slot with nsym DL data symbols */
+  int32_t la_sets;
+  int32_t dl_nsym_tab[16];
 } InbParams;
 
 /* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes

@@ -492,7 +492,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   const long long T = (A.T_dev != nullptr) ? *A.T_dev : p.T;
 #ifdef INB_CHECK
   const long long NER = (long long)p.E * R, NERF = NER * F, NERP = NER * P, NERS = NER * S, NERM = NER * p.M;
-  const long long NFK = (long long)p.E * p.Kf, NLA = (long long)(p.nprb + 1) * p.MCS, GCAP = A.gain_cap;
+  const long long NFK = (long long)p.E * p.Kf, GCAP = A.gain_cap;
+  const long long NLA = (long long)(p.nprb + 1) * p.MCS * (p.la_sets > 1 ? p.la_sets : 1);
 #define CK(i, n, code) ck((i), (n), (code), A.status)
 #else
 #define CK(i, n, code) (i)
@@ -1374,7 +1375,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
           const float est_tx = fa(fs(refs, split_a), csi_s);
           ng = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
         }
-        const long long trow_g = (long long)(int)nprb_a * p.MCS;   // this grant's TBS row
+        // this grant's TBS row (the DL: in the table set of this slot's DL data symbols)
+        const long long tab0 = DL ? (long long)p.dl_nsym_tab[uls] * (p.nprb + 1) * p.MCS : 0;
+        const long long trow_g = tab0 + (long long)(int)nprb_a * p.MCS;
         const long long trow = (p.amc_prev && lnp_a > 0.0f) ? (long long)(int)lnp_a * p.MCS : trow_g;   // MCS row
         // candidates: MCS <= mcs_max with a TBS; the highest first (one lane per RBG), which is the usual outcome;
         // if it fails, every other candidate at once (one lane per MCS) and the highest that passes

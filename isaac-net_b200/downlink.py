@@ -66,6 +66,15 @@ class Downlink:
         # nr_engine.py:624-631)
         self.ref0 = _f32(cfg.gnb_tx_dbm - 10 * math.log10(cfg.nprb))
         self.noise = _f32(cfg.noise_dbm_per_prb("ue"))
+        # link-adaptation tables of every DL data-symbol count of the pattern (a D slot's, an S slot's), stacked
+        nsyms = sorted({cfg.slot_symbols(g)[0] for g in range(len(cfg.tdd_pattern))} - {0})
+        self.nsym_tab = [0] * 16
+        sets = [tab.la_tables(n) for n in nsyms]
+        for j, n in enumerate(nsyms):
+            self.nsym_tab[n] = j
+        self.la_sets = max(1, len(sets))
+        self.la = [torch.cat([s_[i] for s_ in sets]).contiguous() for i in range(4)] if sets else \
+            [tab.la_tbs, tab.la_i0, tab.la_wi, tab.la_ncb]
         self.traffic = self.dtraffic = None
         if generates(cfg.traffic, "dl"):
             dseed = (int(eng.seed) * 2862933555777941757 + 3037000493) % 2 ** 62
@@ -136,6 +145,10 @@ class Downlink:
         p.mcs_max, p.thr_mono = self.mcs_max, self.thr_mono
         p.phr_cap = p.tdma = p.amc_prev = p.bsr_on = 0
         p.ul_ref0, p.noise_prb = self.ref0, self.noise
+        p.la_sets = self.la_sets
+        for n in range(16):
+            p.dl_nsym_tab[n] = self.nsym_tab[n]
+        d.t.la_tbs, d.t.la_i0, d.t.la_wi, d.t.la_ncb = (x.data_ptr() for x in self.la)
         d.s = self.state_struct()
         d.ctr = self.ctr.data_ptr()
         d.trace = d.det_hid = d.dl = None

@@ -101,17 +101,20 @@ class PhyTables:
         self.lw = torch.log(self.w.float()).contiguous()
         self.lw10 = (10 * torch.log10(self.w / cfg.snr_ref_prbs)).contiguous()
         # link adaptation tables over (PRBs 0..NPRB, MCS) at the UL data-slot symbols
-        nprb = int(sum(S_prbs))
-        n = torch.arange(nprb + 1, device=dev, dtype=torch.float32)
-        tbs = tbs_38214(self.qm, self.r, n[:, None], cfg.ul_data_symbols, cfg.dmrs_re_per_prb,
-                        cfg.overhead_re_per_prb)
+        self.nprb, self.cfg = int(sum(S_prbs)), cfg
+        self.la_tbs, self.la_i0, self.la_wi, self.la_ncb = self.la_tables(cfg.ul_data_symbols)
+        self.rate = self.r.contiguous()
+
+    def la_tables(self, nsym):
+        """TBS (bits), BLER-table code-block index and weight, code blocks over (PRBs 0..NPRB, MCS) of a data slot of
+        nsym symbols (PHY.tbs_all + segment, phy.py:77-119): int32, int32, float32, float32 [NPRB+1, M]."""
+        cfg = self.cfg
+        n = torch.arange(self.nprb + 1, device=self.qm.device, dtype=torch.float32)
+        tbs = tbs_38214(self.qm, self.r, n[:, None], nsym, cfg.dmrs_re_per_prb, cfg.overhead_re_per_prb)
         cbs, c = segment(tbs, self.r)
         i0, wi = self._cidx(cbs.float())
-        self.la_tbs = tbs.to(torch.int32).contiguous()
-        self.la_i0 = i0.to(torch.int32).contiguous()
-        self.la_wi = wi.float().contiguous()
-        self.la_ncb = c.float().contiguous()
-        self.rate = self.r.contiguous()
+        return (tbs.to(torch.int32).contiguous(), i0.to(torch.int32).contiguous(), wi.float().contiguous(),
+                c.float().contiguous())
 
     def _cidx(self, cbs):
         x = ((cbs - self.c0) / self.dc).clamp(0, self.C - 1)
