@@ -11,7 +11,7 @@
 namespace inb {
 // Gain rows of inb_nr_step_noalloc, one array per device the library runs on.  Its contents need no initial value:
 // the fading launch of a step writes every row the MAC launch of that step reads.
-__device__ __align__(256) float g_gain_scratch[INB_NOALLOC_GAIN_MAX];
+static __device__ __align__(256) float g_gain_scratch[INB_NOALLOC_GAIN_MAX];
 constexpr int kMaxDevices = 64;
 static float* g_scratch_addr[kMaxDevices];
 static std::mutex g_scratch_mu;
