@@ -42,17 +42,6 @@ struct SmemGroup {
   int32_t bc[2][INB_MAX_C];       // per-cell value broadcast by one lane (GW > 32), double-buffered
 };
 
-// The allocation state of an env's robots for the single-warp allocation rounds of the one-cell instances with more
-// than 32 lanes (one env per block): written by every robot, read and updated by warp 0, read back by every robot.
-template <int GW>
-struct SmemAlloc {
-  static constexpr int N = GW > 32 ? GW : 1;
-  float left[N], got[N], base[N], prio[N], rr[N];
-  int32_t wantc[N], cnt[N], nsb[N];
-  uint32_t won[N];
-  uint8_t rx[N], nel[N];
-};
-
 // float -> order-preserving u32 (non-NaN inputs)
 __device__ __forceinline__ uint32_t fkey(float f) {
   uint32_t u = __float_as_uint(f);
@@ -433,7 +422,6 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   // several cells: per env, the gNBs' N+I per PRB (mW) and its dB value at the start of the slot, this slot's
   // interference accumulator and N+I (dB)
   __shared__ float s_ni[MC ? NG : 1][NC][MC ? INB_MAX_S : 1], s_nidb[MC ? NG : 1][NC][MC ? INB_MAX_S : 1];
-  __shared__ SmemAlloc<(GW > 32 && !MC && !RRK) ? GW : 1> s_al;   // single-warp allocation rounds (one cell, > 32 lanes)
   __shared__ float s_if[MC ? NG : 1][NC][MC ? INB_MAX_S : 1], s_nadb[MC ? NG : 1][NC][MC ? INB_MAX_S : 1];
   extern __shared__ float dyn[];   // [2 or 3][S][NP]: rate / -lin, PF metric, ref (optional)
   const int tid = threadIdx.x;
@@ -1057,111 +1045,6 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             if (!progress) break;
           }
         }
-      }
-    } else if (contested && !RRK && GW > 32 && !MC) {
-      // One cell, one env per block: the allocation rounds below, run by warp 0 alone on the group's state in shared
-      // memory (two block barriers per slot instead of one or two per RBG).  Lane l of warp 0 serves robots l, l + 32,
-      // ...; each round takes the same keys (metric + priority, -1 for robots that no longer want, the retransmission
-      // mask), the same arg-max (highest key, lowest robot on ties: one 64-bit maximum of key << 32 | 255 - robot),
-      // the same float updates of the winner and the same early stop; the release of short retransmissions' RBGs
-      // (retx_priority off) follows the same way.
-      if constexpr (GW > 32 && !MC && !RRK) {
-      constexpr int NB = GW / 32;
-      s_al.left[r] = left; s_al.got[r] = got; s_al.base[r] = pf_base; s_al.prio[r] = prio; s_al.rr[r] = rr_metric;
-      s_al.wantc[r] = act ? want_cnt : 0; s_al.cnt[r] = cnt; s_al.nsb[r] = rx_nsb; s_al.won[r] = 0u;
-      s_al.rx[r] = has_rx ? 1 : 0; s_al.nel[r] = (act && new_el) ? 1 : 0;
-      __syncthreads();
-      if (tid < 32) {
-        auto key_of_robot = [&](int rk, int s_) -> float {   // AMET of robot rk, RBG s_ (its columns of d_x / d_m)
-          const float rate = d_x[s_ * NP + rk];
-          if constexpr (PFR) return x_fdv(rate, fmaxf(fa(s_al.base[rk], fm(p.pf_b, s_al.got[rk])), 1e-9f));
-          return p.sched == 2 ? s_al.rr[rk] : (p.sched == 1 ? rate : d_m[s_ * NP + rk]);
-        };
-        auto take = [&](int rk, int s_, bool new_data) {   // the winner of RBG s_
-          const float rate = d_x[s_ * NP + rk];
-          s_al.won[rk] |= 1u << s_;
-          s_al.cnt[rk] += 1;
-          if (PFR) s_al.got[rk] = fa(s_al.got[rk], rate);
-          if (new_data) s_al.left[rk] = fs(s_al.left[rk], rate);
-        };
-#pragma unroll 1
-        for (int s = 0; s < S; ++s) {
-          bool any_wr = false;
-          if (lex_mask) {
-            bool wr_l = false;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-              const int rk = b * 32 + lane;
-              wr_l = wr_l || (s_al.rx[rk] && s_al.cnt[rk] < s_al.wantc[rk]);
-            }
-            any_wr = __any_sync(0xFFFFFFFFu, wr_l);
-          }
-          unsigned long long best = 0ull;
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const int rk = b * 32 + lane;
-            const bool rx_k = s_al.rx[rk] != 0;
-            const bool want = (s_al.cnt[rk] < s_al.wantc[rk]) && (rx_k || s_al.left[rk] > 0.0f);
-            float mkey = want ? fa(key_of_robot(rk, s), s_al.prio[rk]) : -1.0f;
-            if (lex_mask && any_wr && !(want && rx_k)) mkey = -1.0f;
-            const unsigned long long k64 = ((unsigned long long)fkey(mkey) << 32) | (unsigned)(255 - rk);
-            best = k64 > best ? k64 : best;
-          }
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) {
-            const unsigned long long v = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-            best = v > best ? v : best;
-          }
-          if (!(fkey_inv((uint32_t)(best >> 32)) >= 0.0f)) break;   // no candidate now, none later
-          const int wk = 255 - (int)(best & 0xFFu);
-          if (lane == (wk & 31)) take(wk, s, s_al.rx[wk] == 0);
-          __syncwarp();
-        }
-        if (!lex) {
-          // retransmissions that won fewer RBGs than their TB needs release them to the new-data robots
-          // (mac.py:353-379)
-          uint32_t rel_l = 0u;
-#pragma unroll
-          for (int b = 0; b < NB; ++b) {
-            const int rk = b * 32 + lane;
-            const uint32_t w_ = s_al.won[rk];
-            if (s_al.rx[rk] && __popc(w_) != s_al.nsb[rk]) {
-              rel_l |= w_;
-              s_al.won[rk] = 0u;
-            }
-            s_al.cnt[rk] = __popc(s_al.won[rk]);
-          }
-          const uint32_t rel_all = __reduce_or_sync(0xFFFFFFFFu, rel_l);
-          __syncwarp();
-#pragma unroll 1
-          for (int s = 0; s < S; ++s) {
-            unsigned long long best = 0ull;
-#pragma unroll
-            for (int b = 0; b < NB; ++b) {
-              const int rk = b * 32 + lane;
-              const bool want = (s_al.cnt[rk] < s_al.wantc[rk]) && s_al.nel[rk] && (s_al.left[rk] > 0.0f);
-              const float mkey = want ? key_of_robot(rk, s) : -1.0f;
-              const unsigned long long k64 = ((unsigned long long)fkey(mkey) << 32) | (unsigned)(255 - rk);
-              best = k64 > best ? k64 : best;
-            }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const unsigned long long v = __shfl_xor_sync(0xFFFFFFFFu, best, o);
-              best = v > best ? v : best;
-            }
-            if (!(fkey_inv((uint32_t)(best >> 32)) >= 0.0f)) break;
-            const int wk = 255 - (int)(best & 0xFFu);
-            if (((rel_all >> s) & 1u) && lane == (wk & 31)) take(wk, s, true);
-            __syncwarp();
-          }
-        }
-      }
-      __syncthreads();
-      won = s_al.won[r];
-      cnt = s_al.cnt[r];
-      left = s_al.left[r];
-      got = s_al.got[r];
-      // (s_al is rewritten only in the next slot's allocation, after that slot's block-wide count of candidates)
       }
     } else if (contested && !RRK) {
 #pragma unroll 1

@@ -21,7 +21,7 @@ import importlib
 import pytest
 import torch
 
-from golden_io import CASES, Golden
+from golden_io import CASES, DL_CASES, Golden
 from oracle.nr_oracle import OracleEngine
 
 ib = importlib.import_module("isaac-net_b200")
@@ -34,6 +34,13 @@ pytestmark = pytest.mark.gpu
 
 def _arr(eng):
     return {k: getattr(eng.last_arrivals, k) for k in ARR}
+
+
+def _dl_arr(eng):
+    """The DL arrivals the engine's DL traffic models made this step (None without the downlink)."""
+    if eng.dl is None or getattr(eng.dl, "last_arrivals", None) is None:
+        return None
+    return {k: getattr(eng.dl.last_arrivals, k) for k in ARR}
 
 
 def _snap(orc):
@@ -88,23 +95,23 @@ def _run(case, teacher_forced, radio=False):
         pos = torch.as_tensor(g.pos(s)).to(dev)
         out = eng.step(None, pos)
         if radio:
-            ref = orc.step(pos, _arr(eng))
+            ref = orc.step(pos, _arr(eng), dl_arrivals=_dl_arr(eng))
             d = (eng.pathgain.reshape(orc.pathgain.shape) - orc.pathgain).abs().max().item()
             assert d <= RADIO_ATOL, (s, d)
         else:
-            ref = orc.step(None, _arr(eng), pathgain=eng.pathgain.clone())
+            ref = orc.step(None, _arr(eng), pathgain=eng.pathgain.clone(), dl_arrivals=_dl_arr(eng))
         _check_outputs(out, ref, s, RADIO_ATOL if radio else SINR_ATOL)
         _check_state(eng, orc, s, radio)
 
 
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", CASES + DL_CASES)
 def test_kernel_equals_aten_cuda_free_running(case):
     """Every step of every golden case, the oracle fed the kernel's arrivals and path gains: integer outputs and
     integer state bitwise, floats as the module docstring bounds them."""
     _run(case, teacher_forced=False)
 
 
-@pytest.mark.parametrize("case", CASES)
+@pytest.mark.parametrize("case", CASES + DL_CASES)
 def test_kernel_equals_aten_cuda_teacher_forced(case):
     """As above with the engine loaded with the oracle's state before every step (no carry-over of any difference)."""
     _run(case, teacher_forced=True)
