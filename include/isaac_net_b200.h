@@ -34,7 +34,7 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 15
+#define INB_ABI_VERSION 16
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
@@ -268,6 +268,12 @@ typedef struct InbStepArgs_ {
  * -12: p.bsr_on without the InbState.bsr_* buffers (or a negative pipeline delay).
  * -13: p.dl_on with several cells, without InbStepArgs.dl, or with DL args / DL rows that do not fit the step. */
 int inb_nr_step(const InbStepArgs *args, void *cuda_stream);
+
+/* inb_nr_step whose MAC launches also wait for `mac_wait_event` (a cudaEvent_t recorded by the caller, or NULL),
+ * while the radio and fading launches do not: a caller that produces the step's arrivals on another stream
+ * (NREngine's traffic generation, engine.py:505-573) lets them run beside the fading, in one call.  No counterpart in
+ * the reference (its step is one sequence of torch ops on one stream). */
+int inb_nr_step_after(const InbStepArgs *args, void *cuda_stream, void *mac_wait_event);
 
 /* inb_nr_step for callers that cannot hand the library a scratch buffer: the gain rows live in a fixed device array
  * inside the library (INB_NOALLOC_GAIN_MAX float32 elements per device), so `gain` / `gain_cap` are ignored and

@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 15
+ABI_VERSION = 16
 MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -143,7 +143,7 @@ class InbObsArgs(ctypes.Structure):
                 + [(n, P) for n in OBS_IN + OBS_OUT])
 
 
-EXPORTS = ("inb_nr_step", "inb_nr_step_noalloc", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step",
+EXPORTS = ("inb_nr_step", "inb_nr_step_after", "inb_nr_step_noalloc", "inb_nr_reset", "inb_rng_draw", "inb_traffic_step",
            "inb_store2", "inb_net_obs", "inb_abi_version")
 NOALLOC_GAIN_MAX = 1 << 25
 _lib = None
@@ -164,6 +164,8 @@ def lib():
         raise RuntimeError(f"{LIB_PATH} has ABI {L.inb_abi_version()}, expected {ABI_VERSION}: rebuild it")
     L.inb_nr_step.restype = ctypes.c_int
     L.inb_nr_step.argtypes = [ctypes.POINTER(InbStepArgs), P]
+    L.inb_nr_step_after.restype = ctypes.c_int
+    L.inb_nr_step_after.argtypes = [ctypes.POINTER(InbStepArgs), P, P]
     L.inb_nr_step_noalloc.restype = ctypes.c_int
     L.inb_nr_step_noalloc.argtypes = [ctypes.POINTER(InbStepArgs), P]
     L.inb_nr_reset.restype = ctypes.c_int

@@ -91,6 +91,11 @@ __device__ __forceinline__ float wave_phase(float x, float y, float kx, float ky
   return fused ? __fmaf_rn(y, ky, fm(x, kx)) : fa(fm(x, kx), fm(y, ky));
 }
 
+// The envs [e0, e1) of one launch of a step (the entry points launch the whole batch)
+struct Range {
+  int e0 = 0, e1 = 0;
+};
+
 // an output pointer of InbOutputs: absolute, or a byte offset from the block address `base` (InbStepArgs.o_base)
 template <typename T>
 __device__ __forceinline__ T* out_ptr(T* p, long long base) {

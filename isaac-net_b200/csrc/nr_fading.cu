@@ -19,19 +19,13 @@
 
 namespace inb {
 
-__global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
+// The (robot, cell, RBG) element t of the step (RBGs fastest): its AR(1) rows, gain rows and CSI
+__device__ __forceinline__ void fade_element(const InbStepArgs& A, const uint32_t* s_salt, long long t) {
   const InbParams& p = A.p;
-  // the stream salt of each row's FADING draws (the same for every thread): computed once per block
-  __shared__ uint32_t s_salt[INB_MAX_ROWS];
-  for (int k = threadIdx.x; k < p.K_rows; k += blockDim.x)
-    s_salt[k] = salt((uint32_t)((SITE_FADING << 16) | p.rows[k][0]));
-  __syncthreads();
   const long long NER = (long long)p.E * p.R;
-  const long long t = (long long)blockIdx.x * blockDim.x + threadIdx.x;   // (robot, cell, RBG), RBGs fastest
   const int S = p.S;
   const int C = p.C > 1 ? p.C : 1;
   const long long plane = NER * C * S;
-  if (t >= plane) return;
   const long long ec = t / S;                  // link (robot, cell)
   const int s = (int)(t - ec * S);
   const long long er = ec / C;
@@ -97,10 +91,25 @@ __global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A) {
   if (C == 1) st.csi[t] = last;
 }
 
-cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream) {
-  const long long n = (long long)a.p.E * a.p.R * (a.p.C > 1 ? a.p.C : 1) * a.p.S;
+// Elements [t_begin, t_end) (whole envs), one per thread
+__global__ void __launch_bounds__(256) nr_fading_kernel(const InbStepArgs A, long long t_begin, long long t_end) {
+  const InbParams& p = A.p;
+  // the stream salt of each row's FADING draws (the same for every thread): computed once per block
+  __shared__ uint32_t s_salt[INB_MAX_ROWS];
+  for (int k = threadIdx.x; k < p.K_rows; k += blockDim.x)
+    s_salt[k] = salt((uint32_t)((SITE_FADING << 16) | p.rows[k][0]));
+  __syncthreads();
+  const long long t = t_begin + (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < t_end) fade_element(A, s_salt, t);
+}
+
+cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
+  const long long per_env = (long long)a.p.R * (a.p.C > 1 ? a.p.C : 1) * a.p.S;
+  const long long t0 = (long long)rg.e0 * per_env, t1 = (long long)rg.e1 * per_env;
   const int block = 256;
-  nr_fading_kernel<<<(unsigned)((n + block - 1) / block), block, 0, stream>>>(a);
+  const long long grid = (t1 - t0 + block - 1) / block;
+  if (grid <= 0) return cudaSuccess;
+  nr_fading_kernel<<<(unsigned)grid, block, 0, stream>>>(a, t0, t1);
   return cudaGetLastError();
 }
 

@@ -66,7 +66,7 @@ __device__ __forceinline__ int nth_set64(unsigned long long m, int n) {
 }
 
 template <int FW, int FPL>                     // lanes per robot, frames per lane (F <= FW * FPL)
-__global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) {
+__global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A, const int e_begin) {
   const InbParams& p = A.p;
   const InbState& st = A.s;
   const long long ob = A.o_base != nullptr ? *A.o_base : 0;
@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
   o.det_env = op(A.o.det_env);
   o.lost_any = op(A.o.lost_any); o.generated = op(A.o.generated);
   const int R = p.R, F = p.F, P = p.P;
-  const long long e = blockIdx.x;
+  const long long e = (long long)e_begin + blockIdx.x;   // one block per env of the launch's range
   const int seg = threadIdx.x / FW, l = threadIdx.x % FW;
   const int segs = blockDim.x / FW;
   const long long T = (A.T_dev != nullptr) ? *A.T_dev : p.T;
@@ -238,7 +238,7 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A) 
   if (threadIdx.x == 0 && o.det_env) o.det_env[e] = any ? 1 : 0;
 }
 
-cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream) {
+cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
   const InbParams& p = a.p;
   const int FW = (p.P > 16 || p.F > 32) ? 32 : 16;   // lanes per robot: P <= FW, F <= 2 FW
   const int FPL = p.F > FW ? 2 : 1;
@@ -246,14 +246,16 @@ cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream) {
   while (rp < p.R) rp <<= 1;
   int threads = rp * FW;
   threads = threads < 32 ? 32 : (threads > 512 ? 512 : threads);
+  const int n = rg.e1 - rg.e0;
+  if (n <= 0) return cudaSuccess;
   if (FW == 16 && FPL == 1)
-    nr_finish_kernel<16, 1><<<p.E, threads, 0, stream>>>(a);
+    nr_finish_kernel<16, 1><<<n, threads, 0, stream>>>(a, rg.e0);
   else if (FW == 16)
-    nr_finish_kernel<16, 2><<<p.E, threads, 0, stream>>>(a);
+    nr_finish_kernel<16, 2><<<n, threads, 0, stream>>>(a, rg.e0);
   else if (FPL == 1)
-    nr_finish_kernel<32, 1><<<p.E, threads, 0, stream>>>(a);
+    nr_finish_kernel<32, 1><<<n, threads, 0, stream>>>(a, rg.e0);
   else
-    nr_finish_kernel<32, 2><<<p.E, threads, 0, stream>>>(a);
+    nr_finish_kernel<32, 2><<<n, threads, 0, stream>>>(a, rg.e0);
   return cudaGetLastError();
 }
 

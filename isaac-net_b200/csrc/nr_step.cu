@@ -4,21 +4,21 @@
 // (nr_finish.cu).
 #include "nr_step_entry.cuh"
 namespace inb {
-cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g16_bsr(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g32_bsr(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g128_bsr(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g16_dl(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g32_dl(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g64_dl(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_step_g128_dl(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_step_g16(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g32(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g64(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g16_bsr(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g32_bsr(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g128_bsr(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g16_dl(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g32_dl(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g64_dl(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_step_g128_dl(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
+cudaError_t launch_fading(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
 cudaError_t launch_radio(const InbStepArgs& a, cudaStream_t stream);
-cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream);
+cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream, const Range& rg);
 
 int check_args(const InbStepArgs& a, long long* gain_need) {
   const InbParams& p = a.p;
@@ -69,7 +69,43 @@ int check_args(const InbStepArgs& a, long long* gain_need) {
   return 0;
 }
 
-int launch_all(const InbStepArgs& args, cudaStream_t s) {
+namespace {
+// The DL and UL MAC launches and the finish launches of the envs of rg
+int launch_mac(const InbStepArgs& a, cudaStream_t s, const Range& rg) {
+  const InbParams& p = a.p;
+  cudaError_t err = cudaSuccess;
+  if (p.dl_on) {   // the downlink MAC and finish first: the uplink MAC advances the step's RNG counter
+    InbStepArgs d = *a.dl;
+    d.gain = a.gain;
+    d.gain_cap = a.gain_cap;
+    d.pathgain_in = a.pathgain_in != nullptr ? a.pathgain_in : d.pathgain_in;
+    d.dl = nullptr;
+    if (p.R <= 16)
+      err = launch_step_g16_dl(d, s, rg);
+    else if (p.R <= 32)
+      err = launch_step_g32_dl(d, s, rg);
+    else if (p.R <= 64)
+      err = launch_step_g64_dl(d, s, rg);
+    else
+      err = launch_step_g128_dl(d, s, rg);
+    if (err == cudaSuccess) err = launch_finish(d, s, rg);
+    if (err != cudaSuccess) return -100 - (int)err;
+  }
+  const bool b = p.bsr_on != 0;
+  if (p.R <= 16)
+    err = b ? launch_step_g16_bsr(a, s, rg) : launch_step_g16(a, s, rg);
+  else if (p.R <= 32)
+    err = b ? launch_step_g32_bsr(a, s, rg) : launch_step_g32(a, s, rg);
+  else if (p.R <= 64)
+    err = b ? launch_step_g64_bsr(a, s, rg) : launch_step_g64(a, s, rg);
+  else
+    err = b ? launch_step_g128_bsr(a, s, rg) : launch_step_g128(a, s, rg);
+  if (err == cudaSuccess) err = launch_finish(a, s, rg);
+  return err == cudaSuccess ? 0 : -100 - (int)err;
+}
+}  // namespace
+
+int launch_all(const InbStepArgs& args, cudaStream_t s, cudaEvent_t mac_wait) {
   InbStepArgs a = args;
   const InbParams& p = a.p;
   cudaError_t err = cudaSuccess;
@@ -82,39 +118,15 @@ int launch_all(const InbStepArgs& args, cudaStream_t s) {
     }
     a.pathgain_in = a.rm.pg;
   }
+  Range whole;
+  whole.e1 = p.E;
   if (fading) {
-    err = launch_fading(a, s);
+    err = launch_fading(a, s, whole);
     if (err != cudaSuccess) return -100 - (int)err;
   }
   if (!mac) return 0;
-  if (p.dl_on) {   // the downlink MAC and finish first: the uplink MAC advances the step's RNG counter
-    InbStepArgs d = *a.dl;
-    d.gain = a.gain;
-    d.gain_cap = a.gain_cap;
-    d.pathgain_in = a.pathgain_in != nullptr ? a.pathgain_in : d.pathgain_in;
-    d.dl = nullptr;
-    if (p.R <= 16)
-      err = launch_step_g16_dl(d, s);
-    else if (p.R <= 32)
-      err = launch_step_g32_dl(d, s);
-    else if (p.R <= 64)
-      err = launch_step_g64_dl(d, s);
-    else
-      err = launch_step_g128_dl(d, s);
-    if (err == cudaSuccess) err = launch_finish(d, s);
-    if (err != cudaSuccess) return -100 - (int)err;
-  }
-  const bool b = p.bsr_on != 0;
-  if (p.R <= 16)
-    err = b ? launch_step_g16_bsr(a, s) : launch_step_g16(a, s);
-  else if (p.R <= 32)
-    err = b ? launch_step_g32_bsr(a, s) : launch_step_g32(a, s);
-  else if (p.R <= 64)
-    err = b ? launch_step_g64_bsr(a, s) : launch_step_g64(a, s);
-  else
-    err = b ? launch_step_g128_bsr(a, s) : launch_step_g128(a, s);
-  if (err == cudaSuccess) err = launch_finish(a, s);
-  return err == cudaSuccess ? 0 : -100 - (int)err;
+  if (mac_wait != nullptr && cudaStreamWaitEvent(s, mac_wait, 0) != cudaSuccess) return -100 - (int)cudaGetLastError();
+  return launch_mac(a, s, whole);
 }
 
 }  // namespace inb
@@ -127,7 +139,18 @@ extern "C" int inb_nr_step(const InbStepArgs* args, void* cuda_stream) {
   const int rc = inb::check_args(a, &need);
   if (rc != 0) return rc;
   if (a.gain == nullptr || a.gain_cap < need) return -6;
-  return inb::launch_all(a, (cudaStream_t)cuda_stream);
+  return inb::launch_all(a, (cudaStream_t)cuda_stream, nullptr);
+}
+
+extern "C" int inb_nr_step_after(const InbStepArgs* args, void* cuda_stream, void* mac_wait_event) {
+  if (args == nullptr) return -1;
+  const InbStepArgs& a = *args;
+  if (a.p.E <= 0) return 0;
+  long long need = 0;
+  const int rc = inb::check_args(a, &need);
+  if (rc != 0) return rc;
+  if (a.gain == nullptr || a.gain_cap < need) return -6;
+  return inb::launch_all(a, (cudaStream_t)cuda_stream, (cudaEvent_t)mac_wait_event);
 }
 
 namespace inb {

@@ -227,6 +227,44 @@ struct Grp {
       return res;
     }
   }
+  // whether the sum of v (>= 0) over the group's lanes of some cell (this lane's cell c < C <= NC) exceeds lim: the
+  // same on every lane of the warp (GW <= 32: every group's and cell's sum by warp reductions) or of the block
+  // (GW > 32: per-warp partial sums through shared memory, one block barrier)
+  template <int NC>
+  __device__ static bool any_cell_sum_over(int v, int c, int C, int lim, SmemGroup* sm, int& par) {
+    const int lane = threadIdx.x & 31;
+    bool over = false;
+    if constexpr (GW <= 32) {
+#pragma unroll
+      for (int gq = 0; gq < 32 / GW; ++gq) {
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          if (cc >= C) continue;
+          const unsigned t = __reduce_add_sync(0xFFFFFFFFu, (lane / GW == gq && c == cc) ? (unsigned)v : 0u);
+          over = over || t > (unsigned)lim;
+        }
+      }
+    } else {
+      const int wid = threadIdx.x >> 5;
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        const unsigned t = __reduce_add_sync(0xFFFFFFFFu, c == cc ? (unsigned)v : 0u);
+        if (lane == 0) sm->redf[par][cc][wid] = t;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int cc = 0; cc < NC; ++cc) {
+        if (cc >= C) continue;
+        unsigned t = 0u;
+#pragma unroll
+        for (int w = 0; w < GW / 32; ++w) t += sm->redf[par][cc][w];
+        over = over || t > (unsigned)lim;
+      }
+      par ^= 1;
+    }
+    return over;
+  }
   // as two_or_more_uniform, counting the lanes of each cell (cell index c < C) separately
   __device__ static bool two_or_more_in_a_cell_uniform(bool v, int c, int C) {
     bool multi = false;
@@ -404,7 +442,8 @@ __device__ __forceinline__ int mcs_at(const float* thr, int mcs_max, bool mono, 
 // MCS threshold SINR the UE reported, csi = thr[m] - ref), no power split, HARQ-ACK timing (an ACKed process waits in
 // state 2 until its HARQ-ACK reaches the gNB, a NACK until then too), the BLER_DL draws.
 template <int GW, int NCT, int SV, bool BSR, bool DL>
-__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr_step_kernel(const InbStepArgs A) {
+__global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
+    nr_step_kernel(const InbStepArgs A, const int e_begin, const int e_end) {
   constexpr bool MC = NCT > 1;   // several cells
   constexpr int NC = NCT;        // cells this instance is compiled for (== p.C)
   constexpr bool RRK = SV == 1;  // round-robin allocation by runs (p.sched == 2)
@@ -429,9 +468,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   const int gi = GW > 32 ? 0 : tid / GW;
   const int r = GW > 32 ? tid : tid % GW;
   SmemGroup* sm = &smem_all[gi];
-  const long long e = (long long)blockIdx.x * gpb + gi;
+  const long long e = (long long)e_begin + (long long)blockIdx.x * gpb + gi;   // envs [e_begin, e_end) of the launch
   const int R = p.R, S = p.S, P = p.P, F = p.F;
-  const bool env_ok = e < p.E;
+  const bool env_ok = e < e_end;
   const bool act = env_ok && r < R;
   int par = 0;
   for (int i = tid; i < S; i += NT) {
@@ -454,7 +493,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   unsigned long long* const sc = s_ctr[gi];
   for (int i = r; i < INB_NCTR; i += GW) sc[i] = 0ull;
   const int C = MC ? p.C : 1;
-  if (A.pos != nullptr && A.pathgain_in == nullptr && e < p.E) {
+  if (A.pos != nullptr && A.pathgain_in == nullptr && env_ok) {
     for (int i = r; i < C * p.Kf * 3; i += GW) {
       const int cc = i / (p.Kf * 3), k = (i / 3) % p.Kf, q = i % 3;
       const long long fo = ((long long)cc * p.E + e) * p.Kf + k;
@@ -462,7 +501,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     }
   }
   if constexpr (MC) {
-    if (e < p.E) {
+    if (env_ok) {
       for (int i = r; i < C * S; i += GW) {
         s_ni[gi][i / S][i % S] = A.s.ni_ul[e * C * S + i];
         s_if[gi][i / S][i % S] = 0.0f;
@@ -498,13 +537,27 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   if (act && p.amc_prev) last_nprb = st.last_nprb[CK(er, NER, 1)];
   // HARQ process states as bit masks (state 1: holds a TB awaiting its retransmission or ACK; state 0: free)
   uint32_t pend = 0u, freem = 0u, ackm = 0u;   // ackm (DL): state 2, decoded and waiting for its HARQ-ACK
-  if (act) {
-    for (int q = 0; q < P; ++q) {
-      const long long hs = st.h_state[CK(eP + q, NERP, 4)];
-      if (hs == 1) pend |= 1u << q;
-      else if (hs == 0) freem |= 1u << q;
-      else if (DL && hs == 2) ackm |= 1u << q;
+  auto harq_state = [&](long long hs, int q) {
+    if (hs == 1) pend |= 1u << q;
+    else if (hs == 0) freem |= 1u << q;
+    else if (DL && hs == 2) ackm |= 1u << q;
+  };
+#ifndef INB_CHECK
+  // a robot's P states are contiguous: 16-byte loads where P is even and the array 16-byte aligned
+  const bool vec_h = (P & 1) == 0 && (reinterpret_cast<uintptr_t>(st.h_state) & 15u) == 0;
+#else
+  const bool vec_h = false;
+#endif
+  if (act && vec_h) {
+    const longlong2* hv = reinterpret_cast<const longlong2*>(st.h_state + eP);
+#pragma unroll 4
+    for (int q2 = 0; q2 < P / 2; ++q2) {
+      const longlong2 v = hv[q2];
+      harq_state(v.x, 2 * q2);
+      harq_state(v.y, 2 * q2 + 1);
     }
+  } else if (act) {
+    for (int q = 0; q < P; ++q) harq_state(st.h_state[CK(eP + q, NERP, 4)], q);
   }
   const long long last_hid = env_ok ? A.last_hid[CK(e, p.E, 10)] : 0;
 
@@ -517,8 +570,20 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
   long long n_acc = 0;
   int cnt_q = 0;
   if (act) {
+#ifndef INB_CHECK
+    if ((F & 1) == 0 && (reinterpret_cast<uintptr_t>(st.cap) & 15u) == 0) {   // 16-byte loads, as the HARQ states
+      const longlong2* cv = reinterpret_cast<const longlong2*>(st.cap + eF);
+#pragma unroll 4
+      for (int f2 = 0; f2 < F / 2; ++f2) {
+        const longlong2 v = cv[f2];
+        cnt_q += (v.x >= 0 ? 1 : 0) + (v.y >= 0 ? 1 : 0);
+      }
+    } else
+#endif
+    {
 #pragma unroll 8
-    for (int f = 0; f < F; ++f) cnt_q += st.cap[CK(eF + f, NERF, 3)] >= 0 ? 1 : 0;
+      for (int f = 0; f < F; ++f) cnt_q += st.cap[CK(eF + f, NERF, 3)] >= 0 ? 1 : 0;
+    }
     for (int m = 0; m < M; ++m) {
       const long long em = er * M + m;
       const bool v = A.a.valid[CK(em, NERM, 7)] != 0;
@@ -825,10 +890,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     const float rr_metric = (float)(g - last_tx);
     {
       const uint32_t wm0 = __ballot_sync(0xFFFFFFFFu, has_rx || new_el);
-      if (__popc(wm0) * 4 > S * 3) {
-        // most robots of the warp want RBGs (loaded cells: the multi-cell configs, a saturated uplink): each lane
-        // evaluates its own robot, RBG by RBG (the same expressions), instead of one robot at a time
+      if (MC ? __popc(wm0) >= 6 : __popc(wm0) * 4 > S * 3) {
+        // many robots of the warp want RBGs (loaded cells: the multi-cell configs, a saturated uplink): each lane
+        // evaluates its own robot, RBG by RBG (the same expressions), instead of one robot at a time (measured:
+        // one cell from three quarters of S robots on, several cells from six)
         if (has_rx || new_el) {
+          // the rates first (no call in the loop, so the CSI loads of several RBGs are in flight together), then the
+          // PF metrics
           for (int s = 0; s < S; ++s) {
             float est;
             if constexpr (MC) {
@@ -840,10 +908,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             }
             const float eo = p.olla_on ? fa(est, olla) : fa(est, 0.0f);
             const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
-            const float rt = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
-            v_x[s * NP] = rt;
-            if (p.sched == 0) v_m[s * NP] = x_fdv(rt, avg_den);
+            v_x[s * NP] = fm(fm(fm(s_se[m], re_prb), s_w[s]), 0.125f);
           }
+          if (p.sched == 0)
+            for (int s = 0; s < S; ++s) v_m[s * NP] = x_fdv(v_x[s * NP], avg_den);
         }
       } else {
         for (uint32_t wm = wm0; wm; wm &= wm - 1u) {
@@ -897,9 +965,10 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       if (anyrx) new_el = false;
       if (adm && p.lena_ctr && rx_nsb < S) atomicAdd(sc + INB_CTR_RETX_BLOCK, 1ull);
       has_rx = adm;
-    } else if (Grp<GW>::any_uniform(has_rx, sm, par)) {
+    } else if (Grp<GW>::template any_cell_sum_over<NC>(has_rx ? rx_nsb : 0, serv, C, S, sm, par)) {
       // retransmission admission: rank by metric sum (stable, descending), admit while RBG counts fit
-      // (mac.py:300-312)
+      // (mac.py:300-312).  Where the retransmissions of every cell need S RBGs or fewer in all, each one's count
+      // plus those ranked before it fits, so all are admitted and the ranking is skipped (the branch's condition).
       float rkey = -1.0f;
       if (has_rx) {
         float sum = 0.0f;
@@ -1148,12 +1217,26 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     long long tbs_new = 0;
     uint32_t la_serial = __ballot_sync(0xFFFFFFFFu, tx);   // robots served one at a time below
     bool rest_only = false;                                // ... for the lane-per-MCS search only
-    if constexpr (MC) {
-      if (__popc(la_serial) >= 6) {
-        // Six or more robots of the warp transmit (the loaded multi-cell configs): each lane evaluates its own robot's
-        // grant, lnw and the top MCS, with the same expressions in the same order (the max order-free, the sums
-        // left to right over the won RBGs); only robots whose top MCS fails take the lane-per-MCS search below, with
-        // their -SINR_lin already in their column.
+    // the CSI of this lane's robot on RBG s_ (the scheduler's, as the estimate above read it)
+#define CSI_OWN(s_) (MC ? CSI_A(csi_src, er, serv, (s_)) \
+                        : (DL ? st.csi[CK(eS + (s_), NERS, 5)] : A.gain[CK(g_csi + er * S + (s_), GCAP, 13)]))
+    // Several robots of the warp transmit: unless one of them holds many more RBGs than there are transmitters, each
+    // lane evaluates its own robot's per-RBG work (a chain per won RBG, all lanes at once) for link adaptation and the
+    // decode SINR, instead of the warp serving the robots one at a time (one chain per robot, a lane per RBG).  The
+    // same expressions in the same order (the max order-free, the sums left to right over the won RBGs).
+    const int k_tx = __popc(la_serial);
+    const int won_max = (int)__reduce_max_sync(0xFFFFFFFFu, tx ? (unsigned)__popc(won) : 0u);
+    // (measured: one cell, any two or more transmitters whose largest grant is under 5 k_tx - 4 RBGs; several cells,
+    // where the loaded cells grant many RBGs per robot, six or more for link adaptation and, for the decode and the
+    // interference, only while no grant is larger than the number of transmitters: a round-robin run of most of the
+    // band makes its lane the longest chain).  The same on every lane of the warp.
+    const bool lane_one = k_tx >= 2 && won_max + 4 <= 5 * k_tx;
+    const bool lane_own = MC ? k_tx >= 6 : lane_one;                    // link adaptation
+    const bool lane_dec = MC ? (k_tx >= 6 && won_max <= k_tx) : lane_one;   // decode SINR, interference
+    {
+      // link adaptation: grant, lnw and the top MCS per lane; only robots whose top MCS fails take the lane-per-MCS
+      // search below, with their -SINR_lin already in their column
+      if (lane_own) {
         bool more = false;
         if (tx) {
           uint32_t kmx = 0u;
@@ -1170,12 +1253,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
             const float off_ = p.olla_on ? olla : 0.0f;
             for (uint32_t bb = won; bb; bb &= bb - 1u) {
               const int s_ = __ffs(bb) - 1;
-              const float est_tx = fa(fs(REF(s_), split), CSI_A(csi_src, er, serv, s_));
+              const float est_tx = fa(fs(REF(s_), split), CSI_OWN(s_));
               v_x[s_ * NP] = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
             }
-            // the TBS row of this grant, and the row the MCS is chosen on (the last PUSCH's PRBs under
-            // ul_amc_alloc = "previous", mac.py:393-400)
-            const long long trow_g = (long long)(int)n_prb * p.MCS;
+            // the TBS row of this grant (the DL: in the table set of this slot's DL data symbols), and the row the
+            // MCS is chosen on (the last PUSCH's PRBs under ul_amc_alloc = "previous", mac.py:393-400)
+            const long long tab0_ = DL ? (long long)p.dl_nsym_tab[uls] * (p.nprb + 1) * p.MCS : 0;
+            const long long trow_g = tab0_ + (long long)(int)n_prb * p.MCS;
             const long long trow = (p.amc_prev && last_nprb > 0.0f) ? (long long)(int)last_nprb * p.MCS : trow_g;
             int mtop = -1, n_cand = 0;
             for (int m = min(p.mcs_max, p.MCS - 1); m >= 0; --m) {
@@ -1348,7 +1432,19 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
     // most one robot per cell holds an RBG, so with C <= 3 every (cell, RBG) sum has at most two non-zero terms and
     // its value does not depend on the order of the shared-memory additions.
     if constexpr (MC) {
-      for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+      if (lane_dec && tx) {   // each lane its own robot's RBGs (see lane_dec); the sums do not depend on the order
+#pragma unroll
+        for (int cc = 0; cc < NC; ++cc) {
+          if (cc >= C || cc == serv) continue;
+          const float psd = fs(fs(fa(pg_c[cc], p.ue_tx), p.ref_db), split);
+          for (uint32_t bb = won; bb; bb &= bb - 1u) {
+            const int s = __ffs(bb) - 1;
+            const float prx = powf(10.0f, fm(fa(psd, A.gain[CK(GIDX(u, er, cc, s), GCAP, 13)]), 0.1f));
+            atomicAdd(&s_if[gi][cc][s], prx);
+          }
+        }
+      }
+      for (uint32_t tm = lane_dec ? 0u : __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
         const int a = __ffs(tm) - 1;
         const int ta = wbase + a;
         const long long er_a = __shfl_sync(0xFFFFFFFFu, er, a);
@@ -1398,9 +1494,37 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7) nr
       lo_tx = st.h_lo[CK(hp, NERP, 4)];
       hi_tx = st.h_hi[CK(hp, NERP, 4)];
     }
-    // EESM SINR of the TB's MCS on this row's channel (PHY.eff_sinr, phy.py:311-321), one lane per RBG
+    // EESM SINR of the TB's MCS on this row's channel (PHY.eff_sinr, phy.py:311-321): each lane its own robot's (see
+    // lane_dec), or one robot at a time with one lane per RBG
     float eff_tx = 0.0f;
-    for (uint32_t tm = __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
+    if (lane_dec && tx) {
+      const float beta = s_beta[mcs];
+      uint32_t kx = 0u;
+      for (uint32_t bb = won; bb; bb &= bb - 1u) {
+        const int s = __ffs(bb) - 1;
+        float a_;
+        if constexpr (MC) {   // this slot's interference replaces the N+I the estimate used (nr_engine.py:815)
+          a_ = fa(fs(REF(s), split), A.gain[CK(GIDX(u, er, serv, s), GCAP, 13)]);
+          a_ = fs(a_, fs(s_nadb[MC ? gi : 0][serv][s], s_nidb[MC ? gi : 0][serv][s]));
+        } else {
+          a_ = fa(fs(REF(s), split), A.gain[CK(g_gain + er * S + s, GCAP, 13)]);
+        }
+        const float negl = -powf(10.0f, fm(clampf_t(a_, -30.0f, 60.0f), 0.1f));
+        const float x = fa(x_fdv(negl, beta), s_lw[s]);
+        v_x[s * NP] = x;   // this thread's column is free once link adaptation is done
+        kx = max(kx, fkey(isnan(x) ? -INFINITY : x));
+      }
+      const float mx = fkey_inv(kx);
+      const float m0 = isinf(mx) ? 0.0f : mx;
+      float se = 0.0f;
+      for (uint32_t bb = won; bb; bb &= bb - 1u) {
+        const float ev = expf(fs(v_x[(__ffs(bb) - 1) * NP], m0));
+        se = bb == won ? ev : fa(se, ev);
+      }
+      const float lse = fa(logf(se), m0);
+      eff_tx = db_of(fm(-beta, fs(lse, lnw)));
+    }
+    for (uint32_t tm = lane_dec ? 0u : __ballot_sync(0xFFFFFFFFu, tx); tm; tm &= tm - 1u) {
       const int a = __ffs(tm) - 1;
       const int ta = wbase + a;
       const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;

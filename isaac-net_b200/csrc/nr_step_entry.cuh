@@ -8,7 +8,8 @@ namespace inb {
 // the step's gain rows: (UL rows + 1) S E R with one cell, UL rows x C S E R with C > 1 cells.
 int check_args(const InbStepArgs& a, long long* gain_need);
 // The launches of a checked call on stream `s` (radio, fading, MAC, finish, as a.phases selects); 0 or -100 - error.
-int launch_all(const InbStepArgs& a, cudaStream_t s);
+// mac_wait: an event (or NULL) the MAC launches wait for, after the fading launch.
+int launch_all(const InbStepArgs& a, cudaStream_t s, cudaEvent_t mac_wait);
 // Whether a call with these phases launches the fading or the MAC kernel, the two that use the gain rows.
 inline bool uses_gain_rows(int phases) { return phases == 0 || (phases & 6) != 0; }
 }  // namespace inb

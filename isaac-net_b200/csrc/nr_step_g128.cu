@@ -2,5 +2,7 @@
 // parallel).
 #include "nr_step_launch.cuh"
 namespace inb {
-cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<128, false>(a, stream); }
+cudaError_t launch_step_g128(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
+  return launch_gw<128, false>(a, stream, rg);
+}
 }  // namespace inb

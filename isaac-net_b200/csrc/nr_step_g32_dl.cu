@@ -2,5 +2,7 @@
 // compiled in parallel with the others).
 #include "nr_step_launch.cuh"
 namespace inb {
-cudaError_t launch_step_g32_dl(const InbStepArgs& a, cudaStream_t stream) { return launch_gw_dl<32>(a, stream); }
+cudaError_t launch_step_g32_dl(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
+  return launch_gw_dl<32>(a, stream, rg);
+}
 }  // namespace inb

@@ -2,5 +2,7 @@
 // unit, compiled in parallel with the others).
 #include "nr_step_launch.cuh"
 namespace inb {
-cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream) { return launch_gw<64, true>(a, stream); }
+cudaError_t launch_step_g64_bsr(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
+  return launch_gw<64, true>(a, stream, rg);
+}
 }  // namespace inb

@@ -47,5 +47,5 @@ extern "C" int inb_nr_step_noalloc(const InbStepArgs* args, void* cuda_stream) {
     a.gain = scratch;
     a.gain_cap = INB_NOALLOC_GAIN_MAX;
   }
-  return inb::launch_all(a, (cudaStream_t)cuda_stream);
+  return inb::launch_all(a, (cudaStream_t)cuda_stream, nullptr);
 }

@@ -133,13 +133,23 @@ class Downlink:
         return acc
 
     # ------------------------------------------------------------------ one step
-    def launch_args(self, a, snr=None, dl_snr=None, arrivals=None):
-        """The DL launch arguments of this step from the uplink's `a` (already filled): the DL parameters, state,
-        counters, arrivals and a fresh set of DL outputs.  snr / dl_snr: the step's SNR input (the DL reference is
-        dl_snr, else snr + dl_snr_offset_db, NRNet.step, nr_engine.py:651-653); arrivals: given DL arrivals in place
-        of the DL traffic models' (tests feed the reference's).  Returns (args, outputs)."""
-        eng, cfg, E, R, S, F, dev = self.eng, self.eng.config, self.eng.E, self.eng.R, self.eng.S, self.eng.F, \
-            self.eng.dev
+    # DL outputs: always, and with DL traffic models; (name, dtype, shape) and the InbOutputs field each goes to
+    OUT_BASE = (("dl_newest", torch.long, "ER", "newest"), ("dl_queue_len", torch.long, "ER", "queue_len"))
+    OUT_TRAFFIC = (("dl_delivered", torch.bool, "ERF", "delivered"), ("dl_lost", torch.bool, "ERF", "lost_any"),
+                   ("dl_delay", torch.float32, "ERF", "delay"), ("dl_tag", torch.long, "ERF", "tag"),
+                   ("dl_generated", torch.bool, "ERF", "generated"), ("dl_bytes", torch.long, "ERF", "bytes"),
+                   ("dl_deadline_miss", torch.bool, "ERF", "deadline_miss"),
+                   ("gen_dl_accepted", torch.long, "ER", "gen_accepted"), ("gen_dl_bytes", torch.long, "ER", "gen_bytes"))
+
+    def out_spec(self):
+        """(name, dtype, shape, InbOutputs field) of this link's step outputs."""
+        E, R, F = self.eng.E, self.eng.R, self.eng.F
+        dims = {"ER": (E, R), "ERF": (E, R, F)}
+        outs = self.OUT_BASE + (self.OUT_TRAFFIC if self.traffic is not None else ())
+        return [(n, dt, dims[d], f) for n, dt, d, f in outs]
+
+    def _base_args(self, a):
+        """The DL launch arguments from the uplink's `a` (already filled): the DL parameters, state and counters."""
         d = nat.InbStepArgs.from_buffer_copy(a)
         p = d.p
         p.mcs_max, p.thr_mono = self.mcs_max, self.thr_mono
@@ -152,6 +162,46 @@ class Downlink:
         d.s = self.state_struct()
         d.ctr = self.ctr.data_ptr()
         d.trace = d.det_hid = d.dl = None
+        return d
+
+    def _set_arrivals(self, d, arr, keep):
+        p = d.p
+        if arr is None:
+            p.M = 0
+            for n in nat.ARR_FIELDS:
+                setattr(d.a, n, None)
+            return
+        for n in nat.ARR_FIELDS:
+            v = getattr(arr, n).contiguous()
+            keep.append(v)
+            setattr(d.a, n, v.data_ptr())
+        p.M = arr.valid.shape[-1]
+        if p.M > 64:
+            raise ValueError(f"{p.M} DL traffic arrivals per robot per step (at most 64)")
+
+    def graph_args(self, a, arr, offsets, bias):
+        """The DL launch arguments of a step captured in a CUDA graph (pose input, no SNR input): as launch_args, with
+        the arrivals `arr` of the DL traffic models (produced inside the graph) and every output as its byte offset
+        plus `bias` from the output block whose address the graph's kernels read (InbStepArgs.o_base)."""
+        d = self._base_args(a)
+        keep = []
+        self._set_arrivals(d, arr if self.traffic is not None else None, keep)
+        o = nat.InbOutputs()
+        for n, dt, shape, f in self.out_spec():
+            setattr(o, f, bias + offsets[n])
+        d.o = o
+        self._graph_keep = getattr(self, "_graph_keep", []) + [d, keep]
+        return d
+
+    def launch_args(self, a, snr=None, dl_snr=None, arrivals=None):
+        """The DL launch arguments of this step from the uplink's `a` (already filled): the DL parameters, state,
+        counters, arrivals and a fresh set of DL outputs.  snr / dl_snr: the step's SNR input (the DL reference is
+        dl_snr, else snr + dl_snr_offset_db, NRNet.step, nr_engine.py:651-653); arrivals: given DL arrivals in place
+        of the DL traffic models' (tests feed the reference's).  Returns (args, outputs)."""
+        eng, cfg, E, R, S, F, dev = self.eng, self.eng.config, self.eng.E, self.eng.R, self.eng.S, self.eng.F, \
+            self.eng.dev
+        d = self._base_args(a)
+        p = d.p
         keep = []
         if snr is not None:
             dref = dl_snr.to(dev, torch.float32) if dl_snr is not None else snr.to(dev, torch.float32) + \
@@ -159,38 +209,19 @@ class Downlink:
             ref = (dref if dref.dim() == 3 else dref[..., None].expand(E, R, S)).contiguous()
             keep.append(ref)
             d.ul_ref_in = ref.data_ptr()
-        out = {"dl_newest": torch.empty(E, R, dtype=torch.long, device=dev),
-               "dl_queue_len": torch.empty(E, R, dtype=torch.long, device=dev)}
-        o = nat.InbOutputs()
-        o.newest, o.queue_len = out["dl_newest"].data_ptr(), out["dl_queue_len"].data_ptr()
+        arr = None
         if self.traffic is not None:
             if arrivals is not None:
                 arr = arrivals
             else:
                 arr = self.dtraffic.step() if self.dtraffic is not None else self.traffic.step(eng.clock, None)
             self.last_arrivals = arr
-            for n in nat.ARR_FIELDS:
-                v = getattr(arr, n).contiguous()
-                keep.append(v)
-                setattr(d.a, n, v.data_ptr())
-            p.M = arr.valid.shape[-1]
-            if p.M > 64:
-                raise ValueError(f"{p.M} DL traffic arrivals per robot per step (at most 64)")
-            for n, dt, shape in (("dl_delivered", torch.bool, (E, R, F)), ("dl_lost", torch.bool, (E, R, F)),
-                                 ("dl_delay", torch.float32, (E, R, F)), ("dl_tag", torch.long, (E, R, F)),
-                                 ("dl_generated", torch.bool, (E, R, F)), ("dl_bytes", torch.long, (E, R, F)),
-                                 ("dl_deadline_miss", torch.bool, (E, R, F)), ("gen_dl_accepted", torch.long, (E, R)),
-                                 ("gen_dl_bytes", torch.long, (E, R))):
-                out[n] = torch.empty(shape, dtype=dt, device=dev)
-            for f, n in (("delivered", "dl_delivered"), ("lost_any", "dl_lost"), ("delay", "dl_delay"),
-                         ("tag", "dl_tag"), ("generated", "dl_generated"), ("bytes", "dl_bytes"),
-                         ("deadline_miss", "dl_deadline_miss"), ("gen_accepted", "gen_dl_accepted"),
-                         ("gen_bytes", "gen_dl_bytes")):
-                setattr(o, f, out[n].data_ptr())
-        else:
-            p.M = 0
-            for n in nat.ARR_FIELDS:
-                setattr(d.a, n, None)
+        self._set_arrivals(d, arr, keep)
+        out = {}
+        o = nat.InbOutputs()
+        for n, dt, shape, f in self.out_spec():
+            out[n] = torch.empty(shape, dtype=dt, device=dev)
+            setattr(o, f, out[n].data_ptr())
         d.o = o
         self._keep = (d, keep, out)          # the launch reads them (and `d` lives in host memory)
         return d, out

@@ -170,7 +170,7 @@ class NRB200Engine:
         self._sched = {}
         # CUDA graphs: one captured step (traffic draws + the fused launch) per schedule key, replayed with the poses
         # copied into a static buffer and the control step read from device memory
-        self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ())) and not cfg.dl
+        self.graphs = bool(graphs) and not any(m.kind == "event" for m in (cfg.traffic or ()))
         self._graphs = {}
         self._pool = None
         # a captured step reads its control step and the address of its output block from here (inb_store2)
@@ -653,7 +653,9 @@ class NRB200Engine:
         self._rows_key = key
         return ent
 
-    def _out_layout(self, M):
+    def _out_layout(self, M, dl=False):
+        """(name, dtype, shape, byte offset, bytes) of every step output in one block, and the block's size; dl: with
+        the downlink's outputs (the CUDA-graph step's block; an eager step's DL outputs are the DL call's own)."""
         E, R, F = self.E, self.R, self.F
         spec = [("delivered", torch.bool, (E, R, F)), ("timed_out", torch.bool, (E, R, F)),
                 ("dropped", torch.bool, (E, R, F)), ("deadline_miss", torch.bool, (E, R, F)),
@@ -670,6 +672,8 @@ class NRB200Engine:
             spec.append(("blocked", torch.bool, (E, R)))
             if self.config.channel == "tr38901":
                 spec.append(("los", torch.bool, (E, R)))
+        if dl and self.dl is not None:
+            spec += [(n, dt, shape) for n, dt, shape, f in self.dl.out_spec()]
         off, lay = 0, []
         for n, dt, shape in spec:
             nb = math.prod(shape) * torch.empty((), dtype=dt).element_size()
@@ -913,32 +917,53 @@ class NRB200Engine:
         return res
 
     # ------------------------------------------------------------------ CUDA-graph step
-    def _capture(self, key, rows, rowf):
-        """Capture one control step (traffic generation + the fused launch) for this schedule key."""
+    def _capture(self, key, sched):
+        """Capture one control step (traffic generation + the fused launch; with the downlink also its traffic and its
+        MAC / finish launches) for this schedule key."""
+        rows, rowf, n_ul, rows_dl, n_dlg, n_dl = sched
         a = nat.InbStepArgs.from_buffer_copy(self._args)
         p = a.p
         p.K_rows = len(rows)
         for k, (r4, f2) in enumerate(zip(rows, rowf)):
             p.rows[k][0], p.rows[k][1], p.rows[k][2], p.rows[k][3] = r4
             p.rowf[k][0], p.rowf[k][1] = f2
+        if self.dl is not None:
+            p.n_ul_rows, p.n_dl_rows = n_ul, n_dlg
+            for k, r4 in enumerate(rows_dl):
+                p.rows_dl[k][0], p.rows_dl[k][1], p.rows_dl[k][2], p.rows_dl[k][3] = r4
         p.T, p.s0 = 0, self.s0
         a.T_dev = self._ctl.data_ptr()
         a.pos, a.pathgain_in, a.ul_ref_in, a.trace = self._pos_buf.data_ptr(), None, None, None
         a.det_hid = None
         # output pointers as offsets from the block address stored at _ctl[1] (never 0: a null pointer means "absent")
-        if getattr(self, "_lay", None) is None:
-            self._lay = self._out_layout(0)
+        if getattr(self, "_glay", None) is None:
+            self._glay = self._out_layout(0, dl=True)
         o = nat.InbOutputs()
-        for n, dt, shape, off, nb in self._lay[0]:
-            setattr(o, n, self._OFF + off)
+        dl_names = {n for n, dt, shape, f in self.dl.out_spec()} if self.dl is not None else set()
+        for n, dt, shape, off, nb in self._glay[0]:
+            if n not in dl_names:
+                setattr(o, n, self._OFF + off)
         a.o = o
         a.o_base = self._ctl.data_ptr() + 8
+        a.dl = None
+        dl_offsets = {n: off for n, dt, shape, off, nb in self._glay[0] if n in dl_names}
+        dl_tr = self.dl.traffic if self.dl is not None else None
         if self._pool is None:
             self._pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
         if self.traffic is not None and self.dtraffic is None:
             g.register_generator_state(self.traffic.gen)
-        arr = None
+        if dl_tr is not None and self.dl.dtraffic is None:
+            g.register_generator_state(dl_tr.gen)
+        arr = dl_arr = None
+
+        def dl_arrivals():
+            if dl_tr is None:
+                return None
+            return self.dl.dtraffic.step() if self.dl.dtraffic is not None else \
+                dl_tr.step(self._T_dev - self.epoch, None)
+
+        dl_args = []
         with torch.cuda.graph(g, pool=self._pool):
             if self.dtraffic is not None and self.concurrent_traffic:
                 # the traffic kernel and the radio launch on a side stream, concurrent with the fading launch (none
@@ -954,16 +979,20 @@ class NRB200Engine:
                     for n in nat.ARR_FIELDS:
                         setattr(a.a, n, getattr(arr, n).data_ptr())
                     p.M = arr.valid.shape[-1]
+                    dl_arr = dl_arrivals()
                     if a.rm.on:
                         a.phases = 1
                         nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
                     join = torch.cuda.Event()
                     join.record(self._side)
-                a.phases = 2
-                nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
-                main.wait_event(join)
-                a.phases = 4
-                nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
+                # fading and MAC in one call; the MAC launches also wait for the side stream's arrivals and path
+                # gains
+                if self.dl is not None:
+                    dl_args.append(self.dl.graph_args(a, dl_arr, dl_offsets, self._OFF))
+                    a.dl = ctypes.addressof(dl_args[-1])
+                a.phases = 6
+                nat.check(self.L.inb_nr_step_after(ctypes.byref(a), self._stream(), join._as_parameter_),
+                          "inb_nr_step_after")
                 a.phases = 0
             else:
                 if self.traffic is not None:
@@ -974,8 +1003,12 @@ class NRB200Engine:
                     p.M = arr.valid.shape[-1]
                 else:
                     p.M = 0
+                if self.dl is not None:
+                    dl_arr = dl_arrivals()
+                    dl_args.append(self.dl.graph_args(a, dl_arr, dl_offsets, self._OFF))
+                    a.dl = ctypes.addressof(dl_args[-1])
                 nat.check(self.L.inb_nr_step(ctypes.byref(a), self._stream()), "inb_nr_step")
-        ent = {"graph": g, "args": a, "arr": arr}
+        ent = {"graph": g, "args": a, "arr": arr, "dl_arr": dl_arr, "dl_args": dl_args}
         self._graphs[key] = ent
         return ent
 
@@ -985,13 +1018,14 @@ class NRB200Engine:
         cfg, E, R = self.config, self.E, self.R
         if self._pos_buf is None:
             self._pos_buf = torch.empty(E, R, 2, dtype=torch.float32, device=self.dev)
-        rows, rowf, n_ul = self._rows(T * self.N)[:3]
+        sched = self._rows(T * self.N)
+        n_ul, n_dl = sched[2], sched[5]
         key = self._rows_key
         ent = self._graphs.get(key)
         if ent is None:
-            ent = self._capture(key, rows, rowf)
+            ent = self._capture(key, sched)
         # a new output block for this step (the caller owns fresh tensors); the graph writes into it through _ctl[1]
-        spec, total = self._lay
+        spec, total = self._glay
         blob = torch.empty(total, dtype=torch.uint8, device=self.dev)
         self._pos_buf.copy_(x[..., :2], non_blocking=True)
         nat.check(self.L.inb_store2(self._ctl.data_ptr(), T, blob.data_ptr() - self._OFF, self._stream()),
@@ -1019,6 +1053,11 @@ class NRB200Engine:
         for k in ("los", "blocked"):
             if k in out:
                 res[k] = out[k]
+        if self.dl is not None:       # dl_newest, dl_queue_len; with DL traffic models the dl_* frame outputs
+            self.dl.prb_avail += float(cfg.nprb) * E * n_dl
+            if self.dl.traffic is not None:
+                self.dl.last_arrivals = ent["dl_arr"]
+            res.update({n: out[n] for n, dt, shape, f in self.dl.out_spec()})
         return res
 
     # ------------------------------------------------------------------ observability

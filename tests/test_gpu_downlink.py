@@ -139,3 +139,39 @@ def test_downlink_policy_frames_and_snr_input():
         for k, v in st_o.items():
             assert _eq_t(st_k[k], v), f"step {s} state {k}"
     assert eng.counters()["dl"]["tb_new"] > 0
+
+
+@pytest.mark.parametrize("case", DL_CASES)
+def test_downlink_graph_steps_equal_eager_steps(case):
+    """DL configs step through CUDA graphs (the DL traffic models, the DL MAC and finish launches captured with the
+    uplink's, the DL outputs in the step's output block): graph steps equal eager steps bitwise, in every output and
+    state tensor of both links, with add_dl_frames between steps and a partial reset."""
+    g = Golden(case)
+    cfg, wl = g.config(), g.workload()
+    dev = torch.device("cuda:0")
+    eager = ib.make_engine("L2", g.E, g.R, dev, cfg, seed=wl.seed)
+    eager.graphs = False
+    graph = ib.make_engine("L2", g.E, g.R, dev, cfg, seed=wl.seed)
+    gen = torch.Generator().manual_seed(11)
+    for s in range(g.steps):
+        ids = g.reset_ids(s)
+        if ids:
+            eager.reset(ids)
+            graph.reset(ids)
+        if s % 3 == 1:
+            nb = torch.where(torch.rand(g.E, g.R, generator=gen) < 0.3,
+                             torch.randint(200, 6000, (g.E, g.R), generator=gen),
+                             torch.zeros(g.E, g.R, dtype=torch.long)).float().to(dev)
+            assert torch.equal(eager.add_dl_frames(None, nb), graph.add_dl_frames(None, nb)), s
+        pos = torch.as_tensor(g.pos(s)).to(dev)
+        o_e, o_g = eager.step(None, pos), graph.step(None, pos)
+        assert set(o_e) == set(o_g), s
+        for k in o_e:
+            if torch.is_tensor(o_e[k]):
+                assert _eq_t(o_e[k], o_g[k]), f"step {s} output {k}"
+    assert graph._graphs, "no graph was captured"
+    st_e, st_g = eager.reference_state(), graph.reference_state()
+    for k, v in st_e.items():
+        if torch.is_tensor(v):
+            assert _eq_t(st_g[k], v), f"state {k}"
+    assert eager.counters() == graph.counters()
