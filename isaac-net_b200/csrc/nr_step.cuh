@@ -863,7 +863,9 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
     bool new_el = act && any_free && need > 0 && !has_rx;
     float pcv = -INFINITY;   // power-control backoff (dB), -inf without power control
     if constexpr (MC) {
-      // the env's N+I in dB of this slot, the serving link's reference, power control and the PHR cap
+      // the env's N+I in dB of this slot, the serving link's reference, power control and the PHR cap.  The previous
+      // slot's decode reads s_nidb with no barrier after it, so every warp of the env must be past it first.
+      if constexpr (GW > 32) __syncthreads(); else __syncwarp();
       for (int i = r; i < C * S; i += GW) s_nidb[gi][i / S][i % S] = fm(10.0f, log10f(s_ni[gi][i / S][i % S]));
       float pg_s = pg_c[0];
 #pragma unroll
@@ -914,26 +916,47 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
             for (int s = 0; s < S; ++s) v_m[s * NP] = x_fdv(v_x[s * NP], avg_den);
         }
       } else {
+        // the CSI of robot a on this lane's RBG (every lane calls it: it shuffles); the next robot's is loaded while
+        // the warp works on this one
+        auto csi_of = [&](int a) {
+          const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
+          const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
+          const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
+          float v = 0.0f;
+          if (lane < S) {
+            const int s = lane;
+            if constexpr (MC) {
+              v = CSI_A(csrc_a, ra / S, serv_a, s);
+            } else if constexpr (DL) {
+              v = st.csi[CK(ra + s, NERS, 5)];
+            } else {
+              v = A.gain[CK(g_csi + ra + s, GCAP, 13)];
+            }
+          }
+          return v;
+        };
+        float csi_next = wm0 ? csi_of(__ffs(wm0) - 1) : 0.0f;
         for (uint32_t wm = wm0; wm; wm &= wm - 1u) {
           const int a = __ffs(wm) - 1;
+          const float csi_a = csi_next;
+          const uint32_t later = wm & (wm - 1u);
+          if (later) csi_next = csi_of(__ffs(later) - 1);
           const int ta = wbase + a;
-          const long long ra = __shfl_sync(0xFFFFFFFFu, er, a) * S;
           const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
           const float olla_a = __shfl_sync(0xFFFFFFFFu, olla, a);
           const float avgd_a = __shfl_sync(0xFFFFFFFFu, avg_den, a);
           const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
-          const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
           const float pc_a = MC ? __shfl_sync(0xFFFFFFFFu, pcv, a) : 0.0f;
           if (lane < S) {
             const int s = lane;
             const float refs = REF_A(s, ta, ref_a, serv_a);
             float est;
             if constexpr (MC) {   // one RBG at the power-control PSD (mac_ul.py:160-161)
-              est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), CSI_A(csrc_a, ra / S, serv_a, s));
+              est = fa(fs(refs, fmaxf(s_lw10[s], pc_a)), csi_a);
             } else if constexpr (DL) {
-              est = fa(refs, st.csi[CK(ra + s, NERS, 5)]);
+              est = fa(refs, csi_a);
             } else {
-              est = fa(fs(refs, s_lw10[s]), A.gain[CK(g_csi + ra + s, GCAP, 13)]);
+              est = fa(fs(refs, s_lw10[s]), csi_a);
             }
             const float eo = p.olla_on ? fa(est, olla_a) : fa(est, 0.0f);
             const int m = mcs_at(s_thr, p.mcs_max, thr_mono, eo);
@@ -1227,12 +1250,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
     const int k_tx = __popc(la_serial);
     const int won_max = (int)__reduce_max_sync(0xFFFFFFFFu, tx ? (unsigned)__popc(won) : 0u);
     // (measured: one cell, any two or more transmitters whose largest grant is under 5 k_tx - 4 RBGs; several cells,
-    // where the loaded cells grant many RBGs per robot, six or more for link adaptation and, for the decode and the
-    // interference, only while no grant is larger than the number of transmitters: a round-robin run of most of the
-    // band makes its lane the longest chain).  The same on every lane of the warp.
+    // where the loaded cells grant many RBGs per robot, six or more for link adaptation and, with the per-RBG rounds of
+    // PF, for the decode and the interference (config 3: 4.88 -> 3.75 ms per step); with several cells and round robin,
+    // whose runs give a few robots most of the band, the decode and the interference stay one robot at a time (config
+    // 5: 5.38 vs 5.52 ms)).  The same on every lane of the warp.
     const bool lane_one = k_tx >= 2 && won_max + 4 <= 5 * k_tx;
-    const bool lane_own = MC ? k_tx >= 6 : lane_one;                    // link adaptation
-    const bool lane_dec = MC ? (k_tx >= 6 && won_max <= k_tx) : lane_one;   // decode SINR, interference
+    const bool lane_own = MC ? k_tx >= 6 : lane_one;                                   // link adaptation
+    const bool lane_dec = MC ? (!RRK && k_tx >= 6 && won_max <= k_tx) : lane_one;   // decode SINR, interference
     {
       // link adaptation: grant, lnw and the top MCS per lane; only robots whose top MCS fails take the lane-per-MCS
       // search below, with their -SINR_lin already in their column
