@@ -34,11 +34,11 @@
 extern "C" {
 #endif
 
-#define INB_ABI_VERSION 16
+#define INB_ABI_VERSION 17
 #define INB_MAX_C 3       /* cells (more need an ordered interference sum) */
 #define INB_MAX_S 32      /* RBGs per carrier */
 #define INB_MAX_P 32      /* HARQ processes */
-#define INB_MAX_F 64      /* frame slots per robot */
+#define INB_MAX_F 128     /* frame slots per robot (inb_net_obs: 64) */
 #define INB_MAX_M 64      /* traffic arrivals per robot per step */
 #define INB_MAX_MCS 32
 #define INB_MAX_ROWS 128  /* scheduled slots per control step */
@@ -187,6 +187,12 @@ typedef struct {
    * and, with special_dl_data, an S slot's), dl_nsym_tab[nsym] = the set of a slot with nsym DL data symbols */
   int32_t la_sets;
   int32_t dl_nsym_tab[16];
+  /* ul_power = "whole_band" (UlMac._sched_estimate / _split, mac_ul.py:154-180; MacLink's AMC, mac.py:393-400): a
+   * fixed PSD over the carrier, so the power split of every grant is wb_db = float32(10 log10(nprb / snr_ref_prbs))
+   * (raised to the power-control backoff where that is larger); the scheduler estimate uses the same split (InbTables.
+   * lw10 holds wb_db on every RBG, and there is no PHR cap); with amc_prev the MCS is chosen over the whole band. */
+  int32_t whole_band;
+  float wb_db;
 } InbParams;
 
 /* Radio launch (channel "radio_map" and / or blockage model A): ahead of the fading, one thread per robot computes

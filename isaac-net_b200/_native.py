@@ -12,7 +12,7 @@ import os
 LIB_DIR = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_lib")
 LIB_PATH = os.path.join(LIB_DIR, "libisaac_net_b200_check.so" if os.environ.get("INB_CHECK") == "1"
                         else "libisaac_net_b200.so")
-ABI_VERSION = 16
+ABI_VERSION = 17
 MAX_ROWS = 128
 NCTR = 64
 BLK_REGIONS = 4        # INB_BLK_REGIONS
@@ -80,7 +80,7 @@ class InbParams(ctypes.Structure):
                 + [(n, i32) for n in ("bsr_on", "sr_boot_slots", "sr_boot_bytes", "bsr_delay", "rlc_tail_slots",
                                       "bsr_hdr", "bsr_est_hdr", "rlc_tail_bytes")]
                 + [(n, i32) for n in ("dl_on", "n_ul_rows", "n_dl_rows")] + [("rows_dl", (i32 * 4) * MAX_ROWS)]
-                + [("la_sets", i32), ("dl_nsym_tab", i32 * 16)])
+                + [("la_sets", i32), ("dl_nsym_tab", i32 * 16), ("whole_band", i32), ("wb_db", f32)])
 
 
 class InbRadio(ctypes.Structure):

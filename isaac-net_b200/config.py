@@ -371,7 +371,6 @@ class NRConfig:
                ("bler_source", "only the shipped Sionna PDSCH tables are built"),
                ("tbs_mode", "only the exact 38.214 TBS is built"),
                ("pf_metric", "only the subband PF metric is built"),
-               ("ul_power", "only the allocated-power split is built"),
                ("fading_freq_corr", "frequency-correlated fading is not built"),
                ("fading_doppler", "per-robot Doppler is not built"),
                ("proactive_grant", "proactive grants are not built"),
@@ -421,8 +420,13 @@ class NRConfig:
             out.append((f"los_source={self.los_source!r}", "geometric LOS sources are not built"))
         if self.shadow_modes > 32:
             out.append((f"shadow_modes={self.shadow_modes}", "at most 32 plane waves per shadowing field"))
-        if self.frame_buffer > 64:
-            out.append((f"frame_buffer={self.frame_buffer}", "at most 64 frames per robot"))
+        if self.ul_power not in ("allocated", "whole_band"):
+            out.append((f"ul_power={self.ul_power!r}", "UL power built: allocated, whole_band"))
+        if self.ul_power == "whole_band" and self.ul_amc_alloc == "previous" and self.pf_update != "rbg":
+            out.append(("ul_power='whole_band' with ul_amc_alloc='previous'", "the MCS choice over the whole band is "
+                        "built with pf_update='rbg' (the 5G-LENA switch set)"))
+        if self.frame_buffer > 128:
+            out.append((f"frame_buffer={self.frame_buffer}", "at most 128 frames per robot"))
         if self.n_harq > 32:
             out.append((f"n_harq={self.n_harq}", "at most 32 HARQ processes"))
         if self.n_subbands > 32:

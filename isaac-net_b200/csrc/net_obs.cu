@@ -184,7 +184,8 @@ __global__ void __launch_bounds__(OBS_THREADS) net_obs_kernel(const InbObsArgs A
 extern "C" int inb_net_obs(const InbObsArgs* args, void* cuda_stream) {
   if (args == nullptr) return -1;
   const InbObsArgs& a = *args;
-  if (a.E < 0 || a.R < 1 || a.F < 1 || a.F > INB_MAX_F || a.G < 1 || a.K < 0 || a.dim < 0) return -2;
+  // at most 64 frame slots: two per lane of a robot's 32 lanes
+  if (a.E < 0 || a.R < 1 || a.F < 1 || a.F > 64 || a.G < 1 || a.K < 0 || a.dim < 0) return -2;
   if (a.E == 0) return 0;
   if (a.newest == nullptr || a.t == nullptr || a.delivered == nullptr || a.cap == nullptr || a.delay == nullptr ||
       a.last_cap == nullptr || (a.dim > 0 && a.x == nullptr) || (a.off_serv >= 0 && a.serving == nullptr) ||

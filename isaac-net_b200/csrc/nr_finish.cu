@@ -2,8 +2,8 @@
 // FrameQueue.remove / floor, queues.py:105-143; the step-dict outputs of NREngine.step, engine.py:575-594, 918-960),
 // after the slot loop of the MAC kernel.
 //
-// One block per env; each robot is served by FW lanes with one frame per lane (two when F > FW), so every load and
-// store of the [E,R,F] frame arrays is coalesced.  Per frame: delivered / timed-out / dropped masks and the frame
+// One block per env; each robot is served by FW lanes with one frame per lane (FPL = 2 or 4 when F > FW, up to 128
+// frames), so every load and store of the [E,R,F] frame arrays is coalesced.  Per frame: delivered / timed-out / dropped masks and the frame
 // outputs.  Per robot (segmented shuffles): the in-order pointer, the newest delivered capture, the FIFO compaction
 // (kept frames first in order, then the freed slots in index order, each lane fetching its source frame from the
 // owning lane's registers), the stream floor, the send pointer, HARQ processes that only hold purged bytes, BSR and the
@@ -65,6 +65,16 @@ __device__ __forceinline__ int nth_set64(unsigned long long m, int n) {
   return pos;
 }
 
+// bit `i` of a 128-bit frame mask held as two words (the high word stays 0 with 64 frames or fewer)
+__device__ __forceinline__ bool bit128(unsigned long long lo, unsigned long long hi, int i) {
+  return ((i < 64 ? lo >> i : hi >> (i - 64)) & 1ull) != 0ull;
+}
+// index of the n-th set bit (0-based) of a 128-bit mask
+__device__ __forceinline__ int nth_set128(unsigned long long lo, unsigned long long hi, int n) {
+  const int c = __popcll(lo);
+  return n < c ? nth_set64(lo, n) : 64 + nth_set64(hi, n - c);
+}
+
 template <int FW, int FPL>                     // lanes per robot, frames per lane (F <= FW * FPL)
 __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A, const int e_begin) {
   const InbParams& p = A.p;
@@ -118,7 +128,8 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A, 
     long long cap[FPL], start[FPL], end_[FPL], cls[FPL], hid[FPL], tag[FPL], prio[FPL];
     double fin[FPL], off[FPL], dline[FPL];
     uint8_t lost[FPL], det[FPL];
-    unsigned long long gone = 0ull;
+    constexpr bool W2 = FW * FPL > 64;   // frame masks need a second word
+    unsigned long long gone = 0ull, gone_hi = 0ull;
     long long newest = -1;
 #pragma unroll
     for (int j = 0; j < FPL; ++j) {
@@ -162,41 +173,58 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A, 
         if (o.deadline_miss) o.deadline_miss[at] = late || ((timed || dropped) && isfinite(dline[j]));
       }
       const bool g_ = !fv || delivered || timed || dropped || !valid;
-      gone |= (unsigned long long)Seg<FW>::mask_bits(g_) << (j * FW);
+      const unsigned long long gb = (unsigned long long)Seg<FW>::mask_bits(g_);
+      if (!W2 || j * FW < 64) gone |= gb << (j * FW);
+      else gone_hi |= gb << (j * FW - 64);
     }
     newest = Seg<FW>::max_ll(newest);
     // ---- compaction: surviving frames first (stable), then the freed slots in index order (queues.py:105-110)
     const unsigned long long all = F >= 64 ? ~0ull : ((1ull << F) - 1ull);
+    const unsigned long long all_hi = !W2 || F <= 64 ? 0ull : (F >= 128 ? ~0ull : ((1ull << (F - 64)) - 1ull));
     gone &= all;
-    const unsigned long long keep = ~gone & all;
-    const int n_keep = __popcll(keep);
+    gone_hi &= all_hi;
+    const unsigned long long keep = ~gone & all, keep_hi = ~gone_hi & all_hi;
+    const int n_keep = __popcll(keep) + (W2 ? __popcll(keep_hi) : 0);
     long long floor_new = enq;
 #pragma unroll
     for (int j = 0; j < FPL; ++j) {
       const int f = l + j * FW;
-      const int src = f < F ? (f < n_keep ? nth_set64(keep, f) : nth_set64(gone, f - n_keep)) : 0;
+      int src = 0;
+      if (f < F) {
+        if constexpr (W2) src = f < n_keep ? nth_set128(keep, keep_hi, f) : nth_set128(gone, gone_hi, f - n_keep);
+        else src = f < n_keep ? nth_set64(keep, f) : nth_set64(gone, f - n_keep);
+      }
       const int sl = src % FW, sj = src / FW;
       // every lane takes part in each shuffle; the value comes from register sj of lane sl
       auto pick64 = [&](const long long* v) {
-        const long long a = Seg<FW>::from(v[0], sl);
-        if constexpr (FPL == 1) return a;
-        const long long b = Seg<FW>::from(v[FPL - 1], sl);
-        return sj == 0 ? a : b;
+        long long a = Seg<FW>::from(v[0], sl);
+#pragma unroll
+        for (int jj = 1; jj < FPL; ++jj) {
+          const long long b = Seg<FW>::from(v[jj], sl);
+          a = sj == jj ? b : a;
+        }
+        return a;
       };
       auto pickd = [&](const double* v) {
-        const double a = Seg<FW>::from(v[0], sl);
-        if constexpr (FPL == 1) return a;
-        const double b = Seg<FW>::from(v[FPL - 1], sl);
-        return sj == 0 ? a : b;
+        double a = Seg<FW>::from(v[0], sl);
+#pragma unroll
+        for (int jj = 1; jj < FPL; ++jj) {
+          const double b = Seg<FW>::from(v[jj], sl);
+          a = sj == jj ? b : a;
+        }
+        return a;
       };
       auto pick8 = [&](const uint8_t* v) {
-        const int a = Seg<FW>::from((int)v[0], sl);
-        if constexpr (FPL == 1) return (uint8_t)a;
-        const int b = Seg<FW>::from((int)v[FPL - 1], sl);
-        return (uint8_t)(sj == 0 ? a : b);
+        int a = Seg<FW>::from((int)v[0], sl);
+#pragma unroll
+        for (int jj = 1; jj < FPL; ++jj) {
+          const int b = Seg<FW>::from((int)v[jj], sl);
+          a = sj == jj ? b : a;
+        }
+        return (uint8_t)a;
       };
       const long long c_src = pick64(cap);   // every lane shuffles; the freed slots get cap -1
-      const long long n_cap = ((gone >> src) & 1ull) ? -1 : c_src;
+      const long long n_cap = (W2 ? bit128(gone, gone_hi, src) : ((gone >> src) & 1ull) != 0ull) ? -1 : c_src;
       const long long n_start = pick64(start), n_end = pick64(end_), n_cls = pick64(cls), n_hid = pick64(hid);
       const long long n_tag = pick64(tag), n_prio = pick64(prio);
       const uint8_t n_lost = pick8(lost), n_det = pick8(det);
@@ -241,7 +269,7 @@ __global__ void __launch_bounds__(512, 2) nr_finish_kernel(const InbStepArgs A, 
 cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream, const Range& rg) {
   const InbParams& p = a.p;
   const int FW = (p.P > 16 || p.F > 32) ? 32 : 16;   // lanes per robot: P <= FW, F <= 2 FW
-  const int FPL = p.F > FW ? 2 : 1;
+  const int FPL = p.F > 2 * FW ? 4 : (p.F > FW ? 2 : 1);
   int rp = 1;
   while (rp < p.R) rp <<= 1;
   int threads = rp * FW;
@@ -254,8 +282,10 @@ cudaError_t launch_finish(const InbStepArgs& a, cudaStream_t stream, const Range
     nr_finish_kernel<16, 2><<<n, threads, 0, stream>>>(a, rg.e0);
   else if (FPL == 1)
     nr_finish_kernel<32, 1><<<n, threads, 0, stream>>>(a, rg.e0);
-  else
+  else if (FPL == 2)
     nr_finish_kernel<32, 2><<<n, threads, 0, stream>>>(a, rg.e0);
+  else
+    nr_finish_kernel<32, 4><<<n, threads, 0, stream>>>(a, rg.e0);
   return cudaGetLastError();
 }
 

@@ -1231,7 +1231,8 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
     const bool tx = tx_rx || tx_new;
     // power split over the grant (UlMac._split, mac_ul.py:173-180)
     // (the DL has none: est_tx = est and the decode SINR ref + gain, mac_dl.py:44-45; ref - 0 is ref exactly)
-    float split = DL ? 0.0f : fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f)));
+    // (ul_power = "whole_band": a fixed PSD, the same split for every grant, mac_ul.py:173-176)
+    float split = DL ? 0.0f : (p.whole_band ? p.wb_db : fm(10.0f, log10f(clamp_min_t(fm(n_prb, p.inv_ref_prbs), 1e-3f))));
     if constexpr (MC) split = fmaxf(split, pcv);   // at least the power-control backoff (mac_ul.py:176-180)
     // The transmitting robots of a slot are few: the warp serves them one at a time, with one lane per RBG for the
     // EESM normalization (and the decode SINR below) and one lane per MCS for link adaptation.
@@ -1257,6 +1258,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
     const bool lane_one = k_tx >= 2 && won_max + 4 <= 5 * k_tx;
     const bool lane_own = MC ? k_tx >= 6 : lane_one;                                   // link adaptation
     const bool lane_dec = MC ? (!RRK && k_tx >= 6 && won_max <= k_tx) : lane_one;   // decode SINR, interference
+    // The RBGs whose EESM chooses a new TB's MCS: the grant, or with ul_amc_alloc = "previous" and the whole-band
+    // PSD every RBG of the band (mac.py:393-400); lnw_la is the logsumexp of log(w) over them (lnw: over the grant,
+    // for the decode).  Compiled into the per-RBG PF instance only, the scheduler of the 5G-LENA switch set (the host
+    // refuses the combination with the others): elsewhere its code cost 1-3 % of the step.
+    const bool la_band = PFR && !DL && p.whole_band && p.amc_prev;
+    const uint32_t band = S >= 32 ? 0xFFFFFFFFu : ((1u << S) - 1u);
+    float lnw_la = 0.0f;
     {
       // link adaptation: grant, lnw and the top MCS per lane; only robots whose top MCS fails take the lane-per-MCS
       // search below, with their -SINR_lin already in their column
@@ -1274,8 +1282,22 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
           }
           lnw = fa(logf(sw), lm0);
           if (tx_new) {
+            const uint32_t lam = la_band ? band : won;
+            lnw_la = lnw;
+            if (lam != won) {
+              uint32_t kml = 0u;
+              for (uint32_t bb = lam; bb; bb &= bb - 1u) kml = max(kml, fkey(s_lw[__ffs(bb) - 1]));
+              const float lml = fkey_inv(kml);
+              const float lm0l = isinf(lml) ? 0.0f : lml;
+              float swl = 0.0f;
+              for (uint32_t bb = lam; bb; bb &= bb - 1u) {
+                const float ev = expf(fs(s_lw[__ffs(bb) - 1], lm0l));
+                swl = bb == lam ? ev : fa(swl, ev);
+              }
+              lnw_la = fa(logf(swl), lm0l);
+            }
             const float off_ = p.olla_on ? olla : 0.0f;
-            for (uint32_t bb = won; bb; bb &= bb - 1u) {
+            for (uint32_t bb = lam; bb; bb &= bb - 1u) {
               const int s_ = __ffs(bb) - 1;
               const float est_tx = fa(fs(REF(s_), split), CSI_OWN(s_));
               v_x[s_ * NP] = -powf(10.0f, fm(clampf_t(est_tx, -30.0f, 60.0f), 0.1f));
@@ -1297,7 +1319,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
             if (mtop >= 0) {
               const float beta = s_beta[mtop];
               uint32_t kx = 0u;
-              for (uint32_t bb = won; bb; bb &= bb - 1u) {
+              for (uint32_t bb = lam; bb; bb &= bb - 1u) {
                 const int s_ = __ffs(bb) - 1;
                 const float x = fa(x_fdv(v_x[s_ * NP], beta), s_lw[s_]);
                 kx = max(kx, fkey(isnan(x) ? -INFINITY : x));
@@ -1305,13 +1327,13 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
               const float mx = fkey_inv(kx);
               const float m0 = isinf(mx) ? 0.0f : mx;
               float se = 0.0f;
-              for (uint32_t bb = won; bb; bb &= bb - 1u) {
+              for (uint32_t bb = lam; bb; bb &= bb - 1u) {
                 const int s_ = __ffs(bb) - 1;
                 const float ev = expf(fs(fa(x_fdv(v_x[s_ * NP], beta), s_lw[s_]), m0));
-                se = bb == won ? ev : fa(se, ev);
+                se = bb == lam ? ev : fa(se, ev);
               }
               const float lse = fa(logf(se), m0);
-              const float eff = fa(db_of(fm(-beta, fs(lse, lnw))), off_);
+              const float eff = fa(db_of(fm(-beta, fs(lse, lnw_la))), off_);
               const float b = bler_lookup(bgrid, mtop, eff, A.t.la_i0[CK(trow + mtop, NLA, 9)],
                                           A.t.la_wi[CK(trow + mtop, NLA, 9)]);
               const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + mtop, NLA, 9)]));
@@ -1349,7 +1371,19 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
       if (__shfl_sync(0xFFFFFFFFu, tx_new ? 1 : 0, a)) {
         // ---- link adaptation of a new TB (PHY.select_mcs, phy.py:339-350): the highest MCS <= mcs_max with a TBS
         // whose TB BLER at the EESM SINR (+ OLLA) meets the target, else 0; MCS scanned downward (the first that
-        // passes is the highest), the EESM of each with one lane per RBG
+        // passes is the highest), the EESM of each with one lane per RBG of lam_a (the grant, or the whole band)
+        const uint32_t lam_a = la_band ? band : won_a;
+        const bool in_l = lane < S && ((lam_a >> lane) & 1u);
+        float lnw_l = lnw_a;
+        if (lam_a != won_a) {
+          if (rest_only) {
+            lnw_l = __shfl_sync(0xFFFFFFFFu, lnw_la, a);
+          } else {
+            const float lml = warp_max(in_l ? lw_l : -INFINITY);
+            const float lm0l = isinf(lml) ? 0.0f : lml;
+            lnw_l = fa(logf(ordered_sum(in_l ? expf(fs(lw_l, lm0l)) : 0.0f, lam_a)), lm0l);
+          }
+        }
         const float split_a = __shfl_sync(0xFFFFFFFFu, split, a);
         const float ref_a = __shfl_sync(0xFFFFFFFFu, ref_pg, a);
         const float off_a = __shfl_sync(0xFFFFFFFFu, p.olla_on ? olla : 0.0f, a);
@@ -1358,7 +1392,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
         const int serv_a = MC ? __shfl_sync(0xFFFFFFFFu, serv, a) : 0;
         const int csrc_a = MC ? __shfl_sync(0xFFFFFFFFu, csi_src, a) : 0;
         float ng = 0.0f;   // -10^(clamp(est, -30, 60) / 10) of this lane's RBG
-        if (in && !rest_only) {
+        if (in_l && !rest_only) {
           const int s = lane;
           const float refs = REF_A(s, ta, ref_a, serv_a);
           const float csi_s = MC ? CSI_A(csrc_a, ra / S, serv_a, s)
@@ -1378,11 +1412,11 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
         if (cand && !rest_only) {
           const int m = 31 - __clz(cand);
           const float beta = s_beta[m];
-          const float x = in ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
+          const float x = in_l ? fa(x_fdv(ng, beta), lw_l) : -INFINITY;
           const float mx = warp_max(x);
           const float m0 = isinf(mx) ? 0.0f : mx;
-          const float lse = fa(logf(ordered_sum(in ? expf(fs(x, m0)) : 0.0f, won_a)), m0);
-          const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
+          const float lse = fa(logf(ordered_sum(in_l ? expf(fs(x, m0)) : 0.0f, lam_a)), m0);
+          const float eff = fa(db_of(fm(-beta, fs(lse, lnw_l))), off_a);
           const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
           const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
           if (tbler <= p.target) chosen = m;   // the same value on every lane
@@ -1390,7 +1424,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
         const uint32_t rest = chosen < 0 && cand ? cand & ~(1u << (31 - __clz(cand))) : 0u;
         if (rest) {
           // the grant's -SINR_lin into robot a's column (its rates are done; already there in rest_only mode)
-          if (in && !rest_only) d_x[lane * NP + ta] = ng;
+          if (in_l && !rest_only) d_x[lane * NP + ta] = ng;
           __syncwarp();
           bool pass = false;
           if ((rest >> lane) & 1u) {
@@ -1399,7 +1433,7 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
             // x_s of this lane's MCS kept in the warp's columns of the PF-metric rows (free once RBGs are allocated)
             float* const xcol = d_m + wbase + lane;
             float mx = -INFINITY;
-            for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
+            for (uint32_t bb = lam_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
               const float x = fa(x_fdv(d_x[s * NP + ta], beta), s_lw[s]);
               xcol[s * NP] = x;
@@ -1408,14 +1442,14 @@ __global__ void __launch_bounds__(GW > 32 ? GW : 128, GW > 32 ? 896 / GW : 7)
             const float m0 = isinf(mx) ? 0.0f : mx;
             float sum = 0.0f;
             bool first = true;
-            for (uint32_t bb = won_a; bb; bb &= bb - 1u) {
+            for (uint32_t bb = lam_a; bb; bb &= bb - 1u) {
               const int s = __ffs(bb) - 1;
               const float e = expf(fs(xcol[s * NP], m0));
               sum = first ? e : fa(sum, e);
               first = false;
             }
             const float lse = fa(logf(sum), m0);
-            const float eff = fa(db_of(fm(-beta, fs(lse, lnw_a))), off_a);
+            const float eff = fa(db_of(fm(-beta, fs(lse, lnw_l))), off_a);
             const float b = bler_lookup(bgrid, m, eff, A.t.la_i0[CK(trow + m, NLA, 9)], A.t.la_wi[CK(trow + m, NLA, 9)]);
             const float tbler = fs(1.0f, powf(fs(1.0f, b), A.t.la_ncb[CK(trow + m, NLA, 9)]));
             pass = tbler <= p.target;

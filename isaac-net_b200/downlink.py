@@ -153,7 +153,7 @@ class Downlink:
         d = nat.InbStepArgs.from_buffer_copy(a)
         p = d.p
         p.mcs_max, p.thr_mono = self.mcs_max, self.thr_mono
-        p.phr_cap = p.tdma = p.amc_prev = p.bsr_on = 0
+        p.phr_cap = p.tdma = p.amc_prev = p.bsr_on = p.whole_band = 0   # uplink-only switches
         p.ul_ref0, p.noise_prb = self.ref0, self.noise
         p.la_sets = self.la_sets
         for n in range(16):

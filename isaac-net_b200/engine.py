@@ -246,6 +246,13 @@ class NRB200Engine:
         thr = tab.thr_ref[: tab.mcs_max + 1].cpu()
         p.thr_mono = int(bool((thr[1:] >= thr[:-1]).all()))
         p.olla_on, p.phr_cap, p.retx_priority = int(cfg.olla), int(cfg.phr_cap), int(cfg.retx_priority)
+        # ul_power="whole_band": a fixed PSD over the carrier, the same split for every grant and no PHR cap
+        # (mac_ul.py:154-180); the scheduler estimate reads the split from the per-RBG table
+        p.whole_band = int(cfg.ul_power == "whole_band")
+        p.wb_db = _f32(10 * math.log10(cfg.nprb / cfg.snr_ref_prbs))
+        if p.whole_band:
+            p.phr_cap = 0
+            tab.lw10.fill_(p.wb_db)
         p.comb_cc, p.harq_drop = int(cfg.harq_combining == "cc"), int(cfg.harq_fail == "drop")
         p.purge, p.fading, p.rician = int(cfg.discard == "purge"), int(cfg.fading), int(self.rician)
         p.sr_delay, p.ul_rtt, p.rlc_retx = cfg.sr_delay, cfg.ul_rtt, cfg.rlc_retx_slots

@@ -246,6 +246,9 @@ class NetModule:
         if isc.gnb_pos is not None:
             raise B200Unsupported("IsaacNetCfg.gnb_pos: with radio='engine' the cells are NRConfig's")
         cfg = config if config is not None else NRConfig()
+        if cfg.frame_buffer > 64:
+            raise B200Unsupported(f"frame_buffer={cfg.frame_buffer}: the observation packing handles at most 64 frame "
+                                  "slots per robot")
         if isc.dr_ranges and isc.dr_mode != "off":      # none is honored at level L2 on the engine's radio
             msg = (f"level L2 does not honor these dr_ranges keys with radio='engine': {sorted(isc.dr_ranges)}")
             if isc.dr_strict:

@@ -72,6 +72,17 @@ CASES = {
     "2g": (2, 3, 32, 24, {9: [1]}, 2, dict(ul_grant_model="bsr", ue_tx_dbm=-6.0)),
     "3g": (3, 2, 64, 16, {9: [1]}, 1, dict(ul_grant_model="bsr", a3_ttt_ms=2.0, a3_hyst_db=0.5,
                                            ho_interruption_ms=1.5), 2000.0),
+    # the UE's power over the whole band (ul_power="whole_band": a fixed PSD, no PHR cap): one cell, and three cells
+    # where the power-control backoff competes with the whole-band split
+    "2w": (2, 3, 32, 24, {9: [1]}, 2, dict(ul_power="whole_band", ue_tx_dbm=-4.0)),
+    "3w": (3, 2, 64, 16, {9: [1]}, 2, dict(ul_power="whole_band")),
+    # the reference's ul_v2l case (lena_validation_v2: the 5G-LENA MAC switches with the SR / BSR grant pipeline,
+    # fading off, the whole-band PSD with its MCS chosen over the whole band for the previous PUSCH's PRBs, a 7 dB
+    # noise figure and 128-frame buffers) on config 2's cell
+    "2x": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
+                                           ul_amc_alloc="previous", ul_grant_model="bsr", tb_overhead_bytes=8,
+                                           fading=False, ul_power="whole_band", gnb_nf_db=6.99697,
+                                           frame_buffer=128, ue_tx_dbm=-6.0)),
 }
 
 

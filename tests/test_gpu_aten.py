@@ -8,7 +8,9 @@ Measured on a B200 over every golden case (free-running with the kernel's arriva
 and teacher-forced by loading the oracle's state into the engine before every step): no integer output and no
 integer state ever differs.  What does differ, and the bound each test writes down:
   * h_comb (the chase-combining sum, float state): an ulp of the EESM logsumexp moves 10^(eff/10) by an ulp in a few
-    HARQ processes per case (relative 1e-5 bound);
+    HARQ processes per case (relative 1e-5 bound).  With the whole-band PSD (ul_power="whole_band") the per-RBG SINRs
+    of a grant are low, so the EESM's lse - lnw is a small difference of two ~log(S) terms and one ulp of either is a
+    larger share of it: relative 1e-4 bound there (the CPU's logsumexp order against the left-to-right sum: 9.6e-6);
   * sinr_db with several cells: the serving SINR subtracts 10 log10(mean over RBGs of the N+I) from terms of ~100 dB,
     and torch's CUDA mean adds the RBGs in its own order, so the result moves by a few ulps of a 100 dB term (bound:
     1e-5 relative + 3.1e-5 dB, 4 ulps of a 128 dB value), which for SINRs near 0 dB is more than 1e-5 relative.
@@ -67,6 +69,7 @@ def _check_outputs(out, ref, s, sinr_atol):
 
 def _check_state(eng, orc, s, radio):
     st_k, st_o = eng.reference_state(), orc.reference_state()
+    comb_rtol = 1e-4 if eng.config.ul_power == "whole_band" else 1e-5
     for k, v in st_o.items():
         a = st_k[k]
         if not v.dtype.is_floating_point:
@@ -76,7 +79,8 @@ def _check_state(eng, orc, s, radio):
         elif radio:     # 5e-3 dB of path gain is 0.12 % in linear terms (N+I, combining sums)
             assert torch.allclose(a, v, rtol=2e-3, atol=0.0, equal_nan=True), f"step {s} float state {k}"
         else:
-            assert torch.allclose(a, v, rtol=1e-5, atol=0.0, equal_nan=True), f"step {s} float state {k}"
+            rtol = comb_rtol if k.endswith("h_comb") else 1e-5
+            assert torch.allclose(a, v, rtol=rtol, atol=0.0, equal_nan=True), f"step {s} float state {k}"
 
 
 def _run(case, teacher_forced, radio=False):

@@ -4,7 +4,10 @@ grid's blocks (every 16th block of config 2 and a different env slot inside each
 configs 5 and 4), is stepped by the oracle ("seq", same device) keyed by the same global env ids and fed the kernel's
 own arrivals and path gains.  Every output and every state tensor of the sampled envs must be bitwise equal: this
 covers the large-E index arithmetic, many-block grids and the multi-block paths the small golden cases never reach.
-The whole-batch MAC counters are checked for conservation (every transmitted TB decodes or fails)."""
+The whole-batch MAC counters are checked for conservation (every transmitted TB decodes or fails).  "2x" is config 2's
+cell at 1024 envs with the switches of the reference's ul_v2l case that this engine builds (the 5G-LENA MAC switches,
+the SR / BSR grant pipeline, fading off, the whole-band PSD, 128-frame buffers): the frame compaction over 128 slots
+and the whole-band link adaptation at scale."""
 import importlib
 
 import pytest
@@ -42,18 +45,23 @@ def _rows(x, ids, E):
     return x.index_select(0, ids) if torch.is_tensor(x) and x.dim() > 0 and x.shape[0] == E else x
 
 
-SHAPES = {   # workload: (envs, env ids of the sample, steps)
+SHAPES = {   # name: (envs, env ids of the sample, steps[, workload id, config overrides])
     "2": (4096, torch.arange(64) * 64 + torch.arange(64) % 4, 5),
     "5": (8192, torch.arange(64) * 128 + 127, 4),
     "4": (512, torch.arange(64) * 8 + 3, 4),
+    "2x": (1024, torch.arange(64) * 16 + torch.arange(64) % 4, 6, 2,
+           dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma", ul_amc_alloc="previous",
+                ul_grant_model="bsr", tb_overhead_bytes=8, fading=False, ul_power="whole_band", gnb_nf_db=6.99697,
+                frame_buffer=128, ue_tx_dbm=-6.0)),
 }
 
 
 @pytest.mark.parametrize("wl_i", sorted(SHAPES))
 def test_full_batch_sample_equals_oracle(wl_i):
-    E, ids, steps = SHAPES[wl_i]
-    wl = presets.workload(int(wl_i))
-    cfg = wl.config()
+    E, ids, steps = SHAPES[wl_i][:3]
+    wid, over = (SHAPES[wl_i][3], SHAPES[wl_i][4]) if len(SHAPES[wl_i]) > 3 else (int(wl_i), {})
+    wl = presets.workload(wid)
+    cfg = wl.config(**over)
     R = wl.R
     dev = torch.device("cuda:0")
     ids = ids.to(dev)
@@ -62,7 +70,7 @@ def test_full_batch_sample_equals_oracle(wl_i):
     st_k, st_o = eng.reference_state(), orc.reference_state()
     for k, v in st_o.items():
         assert _eq_t(_rows(st_k[k], ids, E), v), f"initial state {k}"
-    mo = presets.Motion(int(wl_i), E, R, seed=11, step_ms=cfg.control_step_ms)
+    mo = presets.Motion(wid, E, R, seed=11, step_ms=cfg.control_step_ms)
     pos = mo.current()
     reset_env = int(ids[5])
     for s in range(steps):
