@@ -555,6 +555,8 @@ def main():
         try:
             tj = json.load(open(tp))
             traffic = tj.get("bytes_per_launch_scaled", {}).get(wl.name)
+            if traffic is not None:      # captured at the workload's whole batch on one GPU: this rank's share
+                traffic = traffic * E / wl.E
         except Exception:
             traffic = None
     line = {"metric": "env-steps/sec", "value": value, "unit": "env-steps/s", "n_gpus": world, "steps": a.steps,
