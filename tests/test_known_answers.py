@@ -85,3 +85,18 @@ def test_bsr_level_table_matches_the_oracle():
                             "nr_bsr.cuh")).read()
     body = re.search(r"kBsrLevels\[64\] = \{([^}]*)\}", src).group(1)
     assert [int(x) for x in body.replace("\n", " ").split(",")] == list(O.BSR_LEVELS)
+
+
+def test_whole_band_power_settings():
+    """ul_power="whole_band" runs, with or without a PHR cap (the whole-band PSD has none, mac_ul.py:154-168); with
+    ul_amc_alloc="previous" it needs the per-RBG PF instance; 128-frame buffers run, 129 are refused; the split the
+    kernel receives, float32(10 log10(nprb / snr_ref_prbs)), rounds the reference's float64 value."""
+    import math
+    ok = NRConfig(ul_power="whole_band", phr_cap=True)
+    assert ok.refusals() == []
+    lena = NRConfig(ul_power="whole_band", ul_amc_alloc="previous", pf_update="rbg", frame_buffer=128)
+    assert lena.refusals() == []
+    assert any("whole_band" in r[0] for r in NRConfig(ul_power="whole_band", ul_amc_alloc="previous").refusals())
+    assert any("frame_buffer" in r[0] for r in NRConfig(frame_buffer=129).refusals())
+    wb = 10 * math.log10(ok.nprb / ok.snr_ref_prbs)
+    assert abs(float(torch.tensor(wb, dtype=torch.float32)) - wb) <= 1e-6 * abs(wb)
