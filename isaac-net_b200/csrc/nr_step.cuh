@@ -13,10 +13,10 @@
 //
 // The AR(1) fading of the step runs before this kernel (nr_fading.cu): the CSI and the fading gain of the u-th UL
 // row are rows u and u + 1 of the gain buffer [n_ul + 1][E R][S].  Per-RBG work (rates, link adaptation, the decode
-// SINR) is only needed for the few robots that want or use RBGs in a slot, so a warp serves those robots one at a
-// time with a lane per RBG (or per MCS); their per-RBG vectors (rate, PF metric, link-adaptation SINR, the optional
-// per-RBG SNR input) live in shared memory, laid out [vector][RBG][thread] with an odd row stride, so a warp reading
-// a row or a column is conflict-free.  Counters accumulate in shared memory, one block of words per env.
+// SINR) is only needed for the robots that want or use RBGs in a slot: a warp serves a few such robots one at a time
+// with a lane per RBG (or per MCS), and several at once with a lane per robot; their per-RBG vectors (rate, PF metric,
+// link-adaptation SINR, the optional per-RBG SNR input) live in shared memory, laid out [vector][RBG][thread] with an
+// odd row stride, so a warp reading a row or a column is conflict-free.  Counters accumulate in shared memory, one block of words per env.
 //
 // Semantics follow isaac-net v0.2.0 (file:line in the comments); reductions over the RBG axis are left-to-right sums
 // (the oracle's "seq" mode), ties in every argmax resolve to the lowest robot / process index (torch.max / argmin),
