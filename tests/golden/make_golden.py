@@ -79,6 +79,13 @@ CASES = {
     # the reference's ul_v2l case (lena_validation_v2: the 5G-LENA MAC switches with the SR / BSR grant pipeline,
     # fading off, the whole-band PSD with its MCS chosen over the whole band for the previous PUSCH's PRBs, a 7 dB
     # noise figure and 128-frame buffers) on config 2's cell
+    # the largest per-robot sizes (32 HARQ processes, 128 frame slots) on ragged robot counts: 5 robots in a 16-lane
+    # group (11 idle lanes), and one env of 100 robots in a 128-lane block
+    "1m": (1, 2, 5, 20, {8: [1]}, 1, dict(n_harq=32, frame_buffer=128, max_harq_tx=6, ue_tx_dbm=-8.0)),
+    "2m": (2, 1, 100, 12, {6: [0]}, 2, dict(n_harq=32, frame_buffer=128)),
+    # three cells on a weak uplink with long timeouts: the queues fill all 128 frame slots (refused messages, the
+    # compaction over the second word of the frame masks)
+    "3m": (3, 1, 20, 32, {20: [0]}, 2, dict(n_harq=32, frame_buffer=128, timeout_steps=400, ue_tx_dbm=-24.0)),
     "2x": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
                                            ul_amc_alloc="previous", ul_grant_model="bsr", tb_overhead_bytes=8,
                                            fading=False, ul_power="whole_band", gnb_nf_db=6.99697,
