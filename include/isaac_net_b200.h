@@ -269,7 +269,9 @@ typedef struct InbStepArgs_ {
 } InbStepArgs;
 
 /* One control step of the NR uplink engine: the radio (rm.on), fading, MAC and finish launches, on `cuda_stream`.
- * With rm.on and pathgain_in NULL the radio launch evaluates the poses and the MAC reads rm.pg; a pathgain_in
+ * Replaces the slot loop and finish of NRNet.step / step_cells (isaac_net/core/nr_engine.py:634-668, 718-835,
+ * 843-888) with MacLink.slot (mac.py:228-508), the traffic enqueue and gate of NREngine.step (engine.py:505-573) and
+ * the seam of the Triton backend's launch_step (nr_triton.py:1104-1167).  With rm.on and pathgain_in NULL the radio launch evaluates the poses and the MAC reads rm.pg; a pathgain_in
  * skips it.  -11: a radio pointer or size is missing or out of range, or o.blocked is set without the launch.
  * -12: p.bsr_on without the InbState.bsr_* buffers (or a negative pipeline delay).
  * -13: p.dl_on with several cells, without InbStepArgs.dl, or with DL args / DL rows that do not fit the step. */
@@ -296,7 +298,9 @@ int inb_nr_step_after(const InbStepArgs *args, void *cuda_stream, void *mac_wait
 #define INB_NOALLOC_GAIN_MAX (1 << 25)
 int inb_nr_step_noalloc(const InbStepArgs *args, void *cuda_stream);
 
-/* Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial
+/* Replaces the device work of NRNet.reset(env_ids) (nr_engine.py:250-320), MacLink.reset and FrameQueue.reset
+ * (mac.py:176-189, queues.py:70-80).
+ * Reset the envs of mask [E] (uint8; NULL = all): episode += 1, STEP counter = 0, per-robot state to its initial
  * values, fading state h = N(0,1)/sqrt(2) draws (site H0, element ((r C + c) S + s) 2 + re/im), Rician phasor (site
  * KPHI, element r C + c) and K; with C > 1 cells also the association (pending for the next step) and N+I. */
 typedef struct {
@@ -314,7 +318,8 @@ typedef struct {
 int inb_nr_reset(const InbResetArgs *args, void *cuda_stream);
 
 /* Counter-RNG draws out[E, n] (float32) for every env row: uniforms (normal = 0) or normals (normal = 1), channel
- * RESET or STEP with the given counters. */
+ * RESET or STEP with the given counters.  Replaces CounterRNG._draw (isaac_net/core/proto/rng.py:137-161) and the
+ * Triton backend's rng_triton.launch_draw. */
 int inb_rng_draw(int32_t E, int32_t n, uint32_t s0, uint32_t channel, uint32_t stream, const int64_t *env_id,
                  const int64_t *episode, const int64_t *ctr, int32_t normal, float *out, void *cuda_stream);
 
@@ -368,7 +373,8 @@ typedef struct {
 int inb_traffic_step(const InbTrafficArgs *args, void *cuda_stream);
 
 /* Store two int64 values at dst[0], dst[1] in stream order (e.g. the control step and the output block address that
- * a captured step reads through T_dev / o_base). */
+ * a captured step reads through T_dev / o_base).  No counterpart in the reference (its graph backend captures
+ * torch ops around static tensors, cuda_graph.py:19-30). */
 int inb_store2(int64_t *dst, int64_t v0, int64_t v1, void *cuda_stream);
 
 /* Network observation packing of one control step: what isaac-net's Isaac-side module does with the engine's step
@@ -397,7 +403,7 @@ typedef struct {
 } InbObsArgs;
 int inb_net_obs(const InbObsArgs *args, void *cuda_stream);
 
-/* ABI version of the loaded library (INB_ABI_VERSION). */
+/* ABI version of the loaded library (INB_ABI_VERSION).  No counterpart in the reference. */
 int inb_abi_version(void);
 
 #ifdef __cplusplus
