@@ -190,10 +190,8 @@ def wl_id(wl):
 def shard_seed(seed, rank, cfg, traffic_rng="generator"):
     """Seed of shard `rank` (isaac_net/core/sharded.py:95-103): the common seed when every draw is keyed by global env
     id (no traffic models, or the counter-keyed traffic stream), else (seed + rank * 0x9E3779B97F4A7C15) mod 2^62 (the
-    traffic models draw from one generator per engine)."""
-    if cfg.traffic and traffic_rng == "generator":
-        return (int(seed) + rank * 0x9E3779B97F4A7C15) % 2 ** 62
-    return int(seed)
+    traffic models draw from one generator per engine); the rule ShardedEngine applies to its shards."""
+    return importlib.import_module("isaac-net_b200.sharded").shard_seed(seed, rank, cfg, traffic_rng)
 
 
 def max_over_ranks(vals, dist, dev):

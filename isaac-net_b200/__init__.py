@@ -7,6 +7,7 @@ Public API (a drop-in for ``isaac_net.make_engine("L2", ...)`` on the uplink pat
     make_engine(level, E, R, device, config, backend="b200", *, seed=None) -> NRB200Engine
     NRConfig, TrafficModel, Requests
     NetModule, IsaacNetCfg, TrafficRequest  (the Isaac-side module on the engine's radio, net_module.py)
+    ShardedEngine, shard_invariant  (one batch split over several GPUs in one process, sharded.py)
 """
 import importlib as _importlib
 import importlib.abc as _abc
@@ -52,7 +53,10 @@ def __getattr__(name):
     """The Isaac-side module (net_module.py) on first use: NetModule, IsaacNetCfg, TrafficRequest."""
     if name in ("NetModule", "IsaacNetCfg", "TrafficRequest"):
         return getattr(_importlib.import_module(__name__ + ".net_module"), name)
+    if name in ("ShardedEngine", "shard_invariant"):
+        return getattr(_importlib.import_module(__name__ + ".sharded"), name)
     raise AttributeError(name)
 
 
-__all__ = ["make_engine", "NRConfig", "TrafficModel", "Requests", "NetModule", "IsaacNetCfg", "TrafficRequest"]
+__all__ = ["make_engine", "NRConfig", "TrafficModel", "Requests", "NetModule", "IsaacNetCfg", "TrafficRequest",
+           "ShardedEngine", "shard_invariant"]
