@@ -406,6 +406,12 @@ class NRConfig:
             out.append((f"n_cells={self.n_cells}", "at most 3 cells (more need an ordered interference sum)"))
         if self.dl and self.n_cells > 1:
             out.append(("dl with n_cells > 1", "the downlink with several cells (DL interference) is not built"))
+        # the reference adds same-slot UL interference only with thermal noise and ul_interference on
+        # (nr_engine.py:220, 229); the kernels' multi-cell instances always add it
+        if self.n_cells > 1 and not (self.noise_model == "thermal" and self.ul_interference):
+            out.append((f"n_cells={self.n_cells} with noise_model={self.noise_model!r}, "
+                        f"ul_interference={self.ul_interference!r}",
+                        "several cells without same-slot UL interference are not built (use noise_model='thermal')"))
         if self.dl and self.cqi_table != "mcs":
             out.append((f"cqi_table={self.cqi_table!r}", "only the MCS-grid CQI report is built"))
         if self.channel not in ("log_distance", "tr38901", "radio_map"):

@@ -86,6 +86,9 @@ CASES = {
     # three cells on a weak uplink with long timeouts: the queues fill all 128 frame slots (refused messages, the
     # compaction over the second word of the frame masks)
     "3m": (3, 1, 20, 32, {20: [0]}, 2, dict(n_harq=32, frame_buffer=128, timeout_steps=400, ue_tx_dbm=-24.0)),
+    # three cells with the reference's default fixed noise: no same-slot interference (it needs thermal noise), the
+    # gNBs' N+I stays the fixed noise (oracle only: the kernels always add the UL interference and refuse this)
+    "3f": (3, 2, 64, 16, {9: [1]}, 2, dict(noise_model="fixed")),
     "2x": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
                                            ul_amc_alloc="previous", ul_grant_model="bsr", tb_overhead_bytes=8,
                                            fading=False, ul_power="whole_band", gnb_nf_db=6.99697,
@@ -168,6 +171,8 @@ def ref_state(eng):
             st["assoc." + n] = getattr(net.assoc, n)
         st["net.ni_ul"] = net.ni_ul
         st["net.pg"] = net._pg
+        if net.dl is not None:
+            st["net.ni_dl"] = net.ni_dl
     for k, v in ul.ctr.items():
         st["ctr." + k] = v
     st["ctr.ntx_hist"], st["ctr.rv_tx"], st["ctr.rv_fail"] = ul.ntx_hist, ul.rv_tx, ul.rv_fail
@@ -175,8 +180,10 @@ def ref_state(eng):
     return {k: v.detach().cpu().clone().numpy() for k, v in st.items()}
 
 
-# Downlink cases (dl=True, one cell): a TDD pattern with D, S and U slots, DL traffic models (direction="dl") beside
-# the uplink's, CQI reports, DL HARQ with the HARQ-ACK timing; the fixture adds the DL arrivals of each step.
+# Downlink cases (dl=True): a TDD pattern with D, S and U slots, DL traffic models (direction="dl") beside the
+# uplink's, CQI reports, DL HARQ with the HARQ-ACK timing; the fixture adds the DL arrivals of each step.  The "d3"
+# cases run config 3's three cells: the DL reference from each robot's own N+I estimate, the DL inter-cell
+# interference, DL handovers (oracle only: the kernels refuse the downlink with several cells).
 def dl_traffic(i, R):
     """The DL traffic models of the DL cases next to workload i's uplink models."""
     TM = importlib.import_module("isaac-net_b200.traffic").TrafficModel
@@ -193,6 +200,13 @@ DL_CASES = {
     # weak links both ways: DL HARQ failures and exhaustion, purged and refused DL frames; the PF switches
     "d2s": (2, 3, 32, 20, {9: [0]}, 1, dict(tdd_pattern="DDDSU", dl=True, ue_tx_dbm=-8.0, gnb_tx_dbm=12.0,
                                              timeout_steps=6, frame_buffer=8, max_harq_tx=2, pf_update="rbg")),
+    "d3": (3, 2, 64, 20, {9: [1]}, 2, dict(tdd_pattern="DDDSU", dl=True)),
+    # frequent handovers on weak links both ways, the N+I estimates as EWMAs (li_alpha < 1)
+    "d3s": (3, 2, 64, 20, {9: [0]}, 2, dict(tdd_pattern="DDSUU", dl=True, a3_ttt_ms=2.0, a3_hyst_db=0.5,
+                                             ho_interruption_ms=1.5, ue_tx_dbm=-6.0, gnb_tx_dbm=14.0, li_alpha=0.5,
+                                             n_harq=4, max_harq_tx=3, frame_buffer=10, timeout_steps=8), 2000.0),
+    # fixed noise: neither link adds interference, the DL reference still comes from the (constant) N+I estimate
+    "d3n": (3, 2, 64, 16, {9: [1]}, 2, dict(tdd_pattern="DDDSU", dl=True, noise_model="fixed")),
 }
 
 
@@ -398,9 +412,9 @@ def main():
         if c in CKPT_CASES:
             rec = run_ckpt_case(*CKPT_CASES[c])
         elif c in DL_CASES:
-            i, E, R, steps, resets, every, over = DL_CASES[c]
+            i, E, R, steps, resets, every, over, *speed = DL_CASES[c]
             over = dict(over, traffic=dl_traffic(i, R))
-            rec = run_case(i, E, R, steps, resets, every, over)
+            rec = run_case(i, E, R, steps, resets, every, over, *speed)
             rec["overrides"] = np.array(repr(DL_CASES[c][6]))
             rec["dl_traffic"] = np.int64(1)
         elif c in POLICY_CASES:

@@ -100,3 +100,15 @@ def test_whole_band_power_settings():
     assert any("frame_buffer" in r[0] for r in NRConfig(frame_buffer=129).refusals())
     wb = 10 * math.log10(ok.nprb / ok.snr_ref_prbs)
     assert abs(float(torch.tensor(wb, dtype=torch.float32)) - wb) <= 1e-6 * abs(wb)
+
+
+def test_several_cells_need_the_interference_the_kernels_add():
+    """The reference adds the other cells' UL interference only with thermal noise and ul_interference on
+    (nr_engine.py:220); the kernels always add it, so a multi-cell config without it is refused, and so is the
+    downlink with several cells.  The oracle runs both (fixtures cfg3f, cfgd3*)."""
+    import importlib
+    wl3 = importlib.import_module("isaac-net_b200.presets").workload(3)
+    assert wl3.config().noise_model == "thermal" and wl3.config().refusals() == []
+    for over in (dict(noise_model="fixed"), dict(ul_interference=False), dict(dl=True, tdd_pattern="DDDSU")):
+        assert wl3.config(**over).refusals(), over
+    assert NRConfig(noise_model="fixed").refusals() == []          # one cell: no interference either way

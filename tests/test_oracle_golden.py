@@ -12,7 +12,7 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import BSR_CASES, CASES, DL_CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES
+from golden_io import BSR_CASES, CASES, DL_CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES, ORACLE_ONLY_DL_CASES
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -45,7 +45,7 @@ def _state_diff(o, ref):
     return bad
 
 
-@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES + DL_CASES)
+@pytest.mark.parametrize("case", CASES + ORACLE_ONLY_CASES + DL_CASES + ORACLE_ONLY_DL_CASES)
 def test_oracle_aten_bitwise_free_running(case):
     g = Golden(case)
     wl = g.workload()
