@@ -89,6 +89,24 @@ CASES = {
     # three cells with the reference's default fixed noise: no same-slot interference (it needs thermal noise), the
     # gNBs' N+I stays the fixed noise (oracle only: the kernels always add the UL interference and refuse this)
     "3f": (3, 2, 64, 16, {9: [1]}, 2, dict(noise_model="fixed")),
+    # the rest of the reference's lena_like base (config.py:1685-1701; oracle only, the kernels refuse these): the PF
+    # rate from one wideband EESM MCS per robot (pf_metric="wideband"), PDCP discard of arriving frames behind a
+    # stale head of line (discard="pdcp_arrival", no purge) and a per-packet overhead on the air
+    # (pkt_overhead_bytes per started pkt_payload_bytes); one cell and three cells
+    "2L": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_metric="wideband", discard="pdcp_arrival", pkt_overhead_bytes=50,
+                                           timeout_steps=4, ue_tx_dbm=-8.0)),
+    "3L": (3, 2, 64, 16, {9: [1]}, 2, dict(pf_metric="wideband", discard="pdcp_arrival", pkt_overhead_bytes=50,
+                                           pkt_payload_bytes=600, timeout_steps=3)),
+    # the reference's ul_v2l benchmark config (lena_validation_v2) with the shipped tables in place of the 5G-LENA
+    # extraction (bler_source="pdsch", tbs_mode="38214", harq_combining="cc"), on config 2's traffic
+    "2V": (2, 3, 32, 24, {9: [1]}, 2, dict(tdd_pattern="DDDSU", bandwidth_mhz=20, n_prb=50, rbg_size=10,
+                                           ul_data_symbols=13, dmrs_re_per_prb=0, n_harq=16, max_harq_tx=4,
+                                           harq_fail="drop", discard="pdcp_arrival", olla=False,
+                                           pf_metric="wideband", pf_update="rbg", pf_avg_idle="freeze",
+                                           ul_retx_sched="tdma", ul_amc_alloc="previous", ul_grant_model="bsr",
+                                           ul_power="whole_band", phr_cap=False, fading=False,
+                                           noise_model="thermal", gnb_nf_db=6.99697, tb_overhead_bytes=8,
+                                           pkt_overhead_bytes=50, frame_buffer=128)),
     "2x": (2, 3, 32, 24, {9: [1]}, 2, dict(pf_update="rbg", pf_avg_idle="freeze", ul_retx_sched="tdma",
                                            ul_amc_alloc="previous", ul_grant_model="bsr", tb_overhead_bytes=8,
                                            fading=False, ul_power="whole_band", gnb_nf_db=6.99697,
@@ -205,6 +223,10 @@ DL_CASES = {
     "d3s": (3, 2, 64, 20, {9: [0]}, 2, dict(tdd_pattern="DDSUU", dl=True, a3_ttt_ms=2.0, a3_hyst_db=0.5,
                                              ho_interruption_ms=1.5, ue_tx_dbm=-6.0, gnb_tx_dbm=14.0, li_alpha=0.5,
                                              n_harq=4, max_harq_tx=3, frame_buffer=10, timeout_steps=8), 2000.0),
+    # the lena_like switches on the downlink (one cell; oracle only): DL PDCP discard, overhead, wideband PF
+    "d2L": (2, 3, 32, 20, {9: [2]}, 2, dict(tdd_pattern="DDDSU", dl=True, pf_metric="wideband", discard="pdcp_arrival",
+                                             pkt_overhead_bytes=50, timeout_steps=4, gnb_tx_dbm=14.0,
+                                             ue_tx_dbm=-8.0)),
     # fixed noise: neither link adds interference, the DL reference still comes from the (constant) N+I estimate
     "d3n": (3, 2, 64, 16, {9: [1]}, 2, dict(tdd_pattern="DDDSU", dl=True, noise_model="fixed")),
 }
@@ -274,6 +296,10 @@ def run_case(i, E, R, steps, resets, every, over, speed=1.0):
 # name: (workload id, E, R, steps, resets {step: env ids}, state every k steps, config overrides, legacy step)
 POLICY_CASES = {
     "1p": (1, 6, 16, 30, {11: [2]}, 1, dict(traffic=None, msg_sizes=(1500.0, 4000.0), timeout_steps=6), 21),
+    # submits under PDCP discard with a per-packet overhead (oracle only)
+    "1pL": (1, 6, 16, 30, {11: [2]}, 2, dict(traffic=None, msg_sizes=(1500.0, 4000.0), timeout_steps=3,
+                                             discard="pdcp_arrival", pkt_overhead_bytes=40, pkt_payload_bytes=1000,
+                                             ue_tx_dbm=-10.0), 21),
 }
 
 

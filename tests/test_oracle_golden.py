@@ -12,7 +12,8 @@ import numpy as np
 import pytest
 import torch
 
-from golden_io import BSR_CASES, CASES, DL_CASES, POLICY_CASES, Golden, ORACLE_ONLY_CASES, ORACLE_ONLY_DL_CASES
+from golden_io import (BSR_CASES, CASES, DL_CASES, ORACLE_ONLY_CASES, ORACLE_ONLY_DL_CASES, ORACLE_ONLY_POLICY_CASES,
+                       POLICY_CASES, Golden)
 from oracle.nr_oracle import OracleEngine
 
 INT_OUT = ("newest", "det_env", "delivered", "timed_out", "dropped", "cap", "cls", "queue_len", "arrival_slot", "tag",
@@ -162,7 +163,7 @@ def run_policy_step(eng, g, s, dev="cpu", oracle=True):
     return acc, eng.step(None, inp["snr"])
 
 
-@pytest.mark.parametrize("case", POLICY_CASES)
+@pytest.mark.parametrize("case", POLICY_CASES + ORACLE_ONLY_POLICY_CASES)
 def test_oracle_aten_bitwise_policy_case(case):
     """Policy submits with tag / priority / deadline extras, SNR inputs ([E,R] and per RBG) and the legacy step form:
     the oracle equals the reference bitwise, outputs and state, free-running."""
