@@ -406,6 +406,12 @@ class NRConfig:
             out.append((f"n_cells={self.n_cells}", "at most 3 cells (more need an ordered interference sum)"))
         if self.dl and self.n_cells > 1:
             out.append(("dl with n_cells > 1", "the downlink with several cells (DL interference) is not built"))
+        # ho_rlc="flush" under traffic models: the reference keeps the step's later arrivals through a flush (its
+        # handover wrapper, engine.py:486-497); the kernels' handover drops them too
+        if self.ho_rlc == "flush" and self.n_cells > 1 and any(m.generates and m.direction == "ul"
+                                                               for m in (self.traffic or ())):
+            out.append(("ho_rlc='flush' with traffic models", "the flush that keeps the step's later arrivals is not "
+                                                              "built"))
         # the reference adds same-slot UL interference only with thermal noise and ul_interference on
         # (nr_engine.py:220, 229); the kernels' multi-cell instances always add it
         if self.n_cells > 1 and not (self.noise_model == "thermal" and self.ul_interference):

@@ -89,6 +89,10 @@ CASES = {
     # three cells with the reference's default fixed noise: no same-slot interference (it needs thermal noise), the
     # gNBs' N+I stays the fixed noise (oracle only: the kernels always add the UL interference and refuse this)
     "3f": (3, 2, 64, 16, {9: [1]}, 2, dict(noise_model="fixed")),
+    # ho_rlc="flush" with frequent handovers: the queue is flushed at a handover, but messages of the step's traffic
+    # that arrive in a later slot are not queued yet and survive it (NREngine's handover wrapper, engine.py:486-497)
+    "3h": (3, 2, 64, 16, {9: [1]}, 1, dict(ho_rlc="flush", a3_ttt_ms=2.0, a3_hyst_db=0.5, ho_interruption_ms=1.5),
+           2000.0),
     # the rest of the reference's lena_like base (config.py:1685-1701; oracle only, the kernels refuse these): the PF
     # rate from one wideband EESM MCS per robot (pf_metric="wideband"), PDCP discard of arriving frames behind a
     # stale head of line (discard="pdcp_arrival", no purge) and a per-packet overhead on the air

@@ -11,8 +11,9 @@ CASES = ("1", "2", "4", "1s", "2s", "3", "3s", "3t", "5", "5s", "1b", "2r", "3r"
 BSR_CASES = ("2g", "3g", "2x")   # the SR / BSR grant pipeline (ul_grant_model = "bsr") on one and three cells
 # fixtures the oracle is pinned to but the kernels refuse: several cells with the reference's default fixed noise (no
 # same-slot interference), the downlink with several cells, and the lena_like switches (wideband PF rate, PDCP
-# arrival discard, per-packet overhead; "2V" the ul_v2l config with the shipped tables)
-ORACLE_ONLY_CASES = ("3f", "2L", "3L", "2V")
+# arrival discard, per-packet overhead; "2V" the ul_v2l config with the shipped tables), ho_rlc="flush" with traffic
+# models ("3h": the step's later arrivals survive a flush)
+ORACLE_ONLY_CASES = ("3f", "2L", "3L", "2V", "3h")
 ORACLE_ONLY_DL_CASES = ("d3", "d3s", "d3n", "d2L")
 ORACLE_ONLY_POLICY_CASES = ("1pL",)
 DL_CASES = ("d1", "d2", "d2s")   # the downlink MAC with CQI and DL traffic models (TDD patterns with D, S, U slots)

@@ -112,3 +112,6 @@ def test_several_cells_need_the_interference_the_kernels_add():
     for over in (dict(noise_model="fixed"), dict(ul_interference=False), dict(dl=True, tdd_pattern="DDDSU")):
         assert wl3.config(**over).refusals(), over
     assert NRConfig(noise_model="fixed").refusals() == []          # one cell: no interference either way
+    # a flush at handover under traffic models keeps the step's later arrivals in the reference (fixture cfg3h)
+    assert wl3.config(ho_rlc="flush").refusals()
+    assert wl3.config(ho_rlc="flush", traffic=None).refusals() == []
