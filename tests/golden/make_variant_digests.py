@@ -31,7 +31,8 @@ VARIANTS = [
     (2, dict(retx_priority=False, ue_tx_dbm=-6.0)), (2, dict(scheduler="maxci")), (1, dict(timeout_steps=2)),
     (1, dict(frame_buffer=4)), (1, dict(discard="none", timeout_steps=2)), (1, dict(proc_offset_ms=0.7)),
     (1, dict(ul_mcs_max=10)), (2, dict(mcs_table=2)), (1, dict(dmrs_re_per_prb=24)), (1, dict(overhead_re_per_prb=18)),
-    (1, dict(ul_data_symbols=13)), (1, dict(tdd_pattern="DDDSU")), (1, dict(tdd_pattern="DSUUU", special_split=(6, 4, 4))),
+    (1, dict(ul_data_symbols=13)), (1, dict(tdd_pattern="DDDSU")),
+    (1, dict(tdd_pattern="DSUUU", special_split=(6, 4, 4))),
     (1, dict(fading=False)), (1, dict(fading_rho_per_ms=0.5)), (2, dict(rician_k_db=10.0)), (1, dict(gnb_nf_db=9.0)),
     (1, dict(snr_ref_prbs=20)), (1, dict(rbg_size=4)), (1, dict(rbg_config=2)), (2, dict(n_prb=100)),
     (1, dict(tb_overhead_bytes=12)), (1, dict(carrier_ghz=28.0)), (1, dict(ue_height_m=3.0)),
@@ -47,6 +48,20 @@ VARIANTS = [
     (1, dict(channel="tr38901", tr38901_scenario="UMa", tr38901_los="los")),
     (2, dict(tdd_pattern="DDSUU", k1=3)), (2, dict(pf_update="rbg", retx_priority=False)),
     (2, dict(ul_grant_model="bsr", sr_boot_slots=3, bsr_delay_slots=4, rlc_tail_bytes=40)),
+]
+# the downlink (one cell, DDDSU, make_golden.dl_traffic's DL models beside the uplink's): (workload, overrides)
+DL_BASE = dict(tdd_pattern="DDDSU", dl=True)
+DL_VARIANTS = [
+    (1, dict()), (1, dict(ul=False)), (1, dict(dl_mcs_max=12)), (1, dict(k1=4)), (1, dict(cqi_period_slots=2)),
+    (1, dict(cqi_period_slots=40)), (1, dict(gnb_tx_dbm=20.0)), (1, dict(special_dl_data=False)),
+    (1, dict(dl_ctrl_symbols=3)), (1, dict(gnb_proc_slots=3)),
+    (1, dict(harq_fail="drop", gnb_tx_dbm=10.0, max_harq_tx=2)),
+    (1, dict(harq_combining="none", gnb_tx_dbm=12.0)), (1, dict(tdd_pattern="DDSUU")),
+    (1, dict(tdd_pattern="DSUUU", special_split=(6, 4, 4))), (1, dict(ue_nf_db=4.0)), (1, dict(scheduler="rr")),
+    (1, dict(scheduler="maxci")), (1, dict(olla=False)), (1, dict(timeout_steps=2, gnb_tx_dbm=8.0)),
+    (1, dict(frame_buffer=4)), (2, dict(mcs_table=2)), (2, dict(pf_update="rbg", pf_avg_idle="freeze")),
+    (1, dict(mu=0, control_step_ms=10.0)), (1, dict(fading=False)), (2, dict(rician_k_db=8.0)),
+    (1, dict(proc_offset_ms=0.4)),
 ]
 
 
@@ -89,18 +104,22 @@ def main():
     sys.path.insert(0, HERE)
     import json
     import torch
-    from make_golden import run_case
+    from make_golden import dl_traffic, run_case
     torch.set_num_threads(8)
     res = []
-    for i, over in VARIANTS:
-        rec = run_case(i, E, robots(i), STEPS, RESETS, STEPS, over)
+    runs = [(i, over, over) for i, over in VARIANTS]
+    runs += [(i, dict(DL_BASE, **over), dict(DL_BASE, **over, traffic=dl_traffic(i, robots(i))))
+             for i, over in DL_VARIANTS]
+    for i, over, run_over in runs:
+        rec = run_case(i, E, robots(i), STEPS, RESETS, STEPS, run_over)
         ds, sd = [], {}
         for s in range(STEPS):
             pre = f"s{s}/out."
             ds.append(digest({k[len(pre):]: v for k, v in rec.items() if k.startswith(pre)}))
             if f"s{s}/st.ul.sent" in rec:
                 sd[str(s)] = digest({k: rec[f"s{s}/st.{k}"] for k in STATE_KEYS})
-        res.append({"workload": i, "over": repr(over), "digests": ds, "state_digests": sd})
+        res.append({"workload": i, "over": repr(over), "dl_traffic": "traffic" in run_over, "digests": ds,
+                    "state_digests": sd})
         print(i, over, ds[-1], flush=True)
     path = os.path.join(HERE, "variant_digests.json")
     with open(path, "w") as fh:

@@ -40,5 +40,4 @@ def test_schedule_rows_equal_the_reference(i):
     for g0, ref in e["rows"].items():
         want = _rows(ref, cfg.dl)
         assert _rows(cfg.schedule(int(g0)), cfg.dl) == want, (f, g0)
-        if cfg.ul:      # the oracle restates the uplink engine (the UL link always on)
-            assert _rows(d.schedule(int(g0)), cfg.dl) == want, (f, g0)
+        assert _rows(d.schedule(int(g0)), cfg.dl) == want, (f, g0)
