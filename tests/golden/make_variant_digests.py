@@ -48,6 +48,12 @@ VARIANTS = [
     (1, dict(channel="tr38901", tr38901_scenario="UMa", tr38901_los="los")),
     (2, dict(tdd_pattern="DDSUU", k1=3)), (2, dict(pf_update="rbg", retx_priority=False)),
     (2, dict(ul_grant_model="bsr", sr_boot_slots=3, bsr_delay_slots=4, rlc_tail_bytes=40)),
+    # settings the kernels refuse but the oracle restates: lena_like's switches, no same-slot interference, a flush
+    # at handover under traffic models
+    (1, dict(pf_metric="wideband")), (2, dict(pf_metric="wideband", scheduler="maxci")),
+    (2, dict(discard="pdcp_arrival", timeout_steps=2, ue_tx_dbm=-8.0)), (1, dict(pkt_overhead_bytes=60)),
+    (3, dict(pf_metric="wideband", discard="pdcp_arrival", timeout_steps=3)), (3, dict(ul_interference=False)),
+    (3, dict(ho_rlc="flush", a3_ttt_ms=2.0, a3_hyst_db=0.5)),
 ]
 # the downlink (one cell, DDDSU, make_golden.dl_traffic's DL models beside the uplink's): (workload, overrides)
 DL_BASE = dict(tdd_pattern="DDDSU", dl=True)
@@ -62,6 +68,12 @@ DL_VARIANTS = [
     (1, dict(frame_buffer=4)), (2, dict(mcs_table=2)), (2, dict(pf_update="rbg", pf_avg_idle="freeze")),
     (1, dict(mu=0, control_step_ms=10.0)), (1, dict(fading=False)), (2, dict(rician_k_db=8.0)),
     (1, dict(proc_offset_ms=0.4)),
+    # several cells (oracle only: the kernels refuse the downlink with several cells)
+    (3, dict()), (3, dict(dl_interference=False)), (3, dict(li_alpha=0.5, gnb_tx_dbm=30.0)),
+    (3, dict(a3_ttt_ms=2.0, a3_hyst_db=0.5, ho_interruption_ms=1.5)), (3, dict(harq_fail="drop", a3_ttt_ms=2.0)),
+    # lena_like's switches on both links (oracle only)
+    (1, dict(pf_metric="wideband")), (1, dict(discard="pdcp_arrival", timeout_steps=2, gnb_tx_dbm=8.0)),
+    (1, dict(pkt_overhead_bytes=60, pkt_payload_bytes=500)),
 ]
 
 
