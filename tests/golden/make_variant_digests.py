@@ -54,6 +54,13 @@ VARIANTS = [
     (2, dict(discard="pdcp_arrival", timeout_steps=2, ue_tx_dbm=-8.0)), (1, dict(pkt_overhead_bytes=60)),
     (3, dict(pf_metric="wideband", discard="pdcp_arrival", timeout_steps=3)), (3, dict(ul_interference=False)),
     (3, dict(ho_rlc="flush", a3_ttt_ms=2.0, a3_hyst_db=0.5)),
+    # radio: blockage model A on the other channels and cell layouts, forced-LOS / NLOS TR 38.901, no blockage on the map
+    (5, dict(blockage=False)), (5, dict(a3_hyst_db=1.0, a3_ttt_ms=10.0)),
+    (1, dict(blockage=True, blockage_model="stochastic")), (3, dict(blockage=True, blockage_model="stochastic")),
+    (1, dict(channel="tr38901", tr38901_scenario="UMi", tr38901_los="los", blockage=True,
+             blockage_model="stochastic", gnb_height_m=10.0)),
+    (3, dict(channel="tr38901", tr38901_scenario="UMa", tr38901_los="los")),
+    (1, dict(channel="tr38901", tr38901_scenario="UMi", tr38901_los="nlos")),
 ]
 # the downlink (one cell, DDDSU, make_golden.dl_traffic's DL models beside the uplink's): (workload, overrides)
 DL_BASE = dict(tdd_pattern="DDDSU", dl=True)
